@@ -1,0 +1,445 @@
+"""Benchmark: VisionHOPE-T forward images/s at 224x224 (bf16 autocast, channels-last, CUDA graph).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+
+One step = one forward of B synthetic images per GPU (N(0,1), seed 3 + rank) through the
+prepared model, plus the NCCL all-gather of the logits when N > 1 (batch sharding: weak
+scaling).  Inputs and the model's activation footprint are far larger than L2, and a
+256 MiB buffer is additionally rewritten between timed steps (outside the timed events).
+Rank 0 prints one JSON line; the time is the max over ranks of the summed per-step CUDA
+event times.  Extra keys:
+  e2e          -- the same metric through the public model call with the batch copied from
+                  pinned host memory and the logits copied back inside every timed step;
+  roofline     -- the dominant kernel (the fused SRNL operator at the stage-1 shape of this
+                  batch) timed alone with CUDA events, against the measured FP32 FMA peak;
+  cpu_baseline -- the CPU stand-in for the reference (oracle port of SRNL + PyTorch CPU
+                  LayerNorm/GRN/convolutions) on a small sample, rank 0 at N = 1 only;
+  clocks       -- nvidia-smi samples taken during the timed region.
+--impl reference runs only that CPU workload (rank 0), timed per step, and prints its line.
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "VisionHOPE-T fwd images/sec @224"
+UNIT = "images/s"
+IMG = 224
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--model", default="visionhope_tiny")
+    ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU baseline step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def config(args, world):
+    return {"workload": f"{args.model} classification forward, {IMG}x{IMG}, batch {args.batch}/GPU",
+            "model": args.model, "global_batch": args.batch * world, "batch_per_gpu": args.batch,
+            "image_size": IMG, "precision": "bf16 autocast, fp32 params", "channels_last": True,
+            "execution": "cuda_graph", "parallelism": f"dp{world} (batch-sharded, all_gather logits)",
+            "l2": "256 MiB buffer rewritten between timed steps; activations >> L2",
+            "seed": 3}
+
+
+# ----------------------------------------------------------------------------------------
+# CPU stand-in for the reference: the reference has no CPU SRNL path (models/srnl.py:113-114),
+# so SRNL runs on the oracle port (oracle/vhope_oracle.c, float arithmetic, OpenMP); LayerNorm
+# and GRN use the reference's own CPU formulas (models/layers.py:25-35, utils/grn.py:26-38).
+@contextlib.contextmanager
+def cpu_reference_patches():
+    import numpy as np
+    import torch.nn.functional as F
+
+    from oracle import oracle as orc
+    from visionhope_b200 import backbone, operator
+    from visionhope_b200.utils import grn as grn_mod
+
+    saved = (backbone.LayerNorm2d.forward, grn_mod.GlobalResponseNorm.forward,
+             operator.VisionHOPEOperator._forward_fast, operator.VisionHOPEOperator._inference_path)
+
+    def ln_forward(self, x):
+        return F.layer_norm(x.permute(0, 2, 3, 1), (self.weight.numel(),), self.weight, self.bias,
+                            self.eps).permute(0, 3, 1, 2)
+
+    def grn_forward(self, x):
+        return grn_mod.grn_reference(x, self.gamma, self.beta, self.eps)
+
+    def fast(self, x, path):
+        H, W = x.shape[-2:]
+        seq_hw = x.flatten(2).transpose(1, 2)
+        xs = self.serialize(x, seq_hw)
+        q = self.project_queries(seq_hw, H, W)
+        out = orc.srnl_spatial([m.detach() for m in self.srnl.initial_memories], xs, q,
+                               self.d_skip.detach(), self._fusion_weights(), H, W, self.head_dim,
+                               use_f32=True)
+        return torch.from_numpy(out.astype(np.float32))
+
+    backbone.LayerNorm2d.forward = ln_forward
+    grn_mod.GlobalResponseNorm.forward = grn_forward
+    operator.VisionHOPEOperator._forward_fast = fast
+    operator.VisionHOPEOperator._inference_path = lambda self, x: ("spatial", None)
+    try:
+        yield
+    finally:
+        (backbone.LayerNorm2d.forward, grn_mod.GlobalResponseNorm.forward,
+         operator.VisionHOPEOperator._forward_fast, operator.VisionHOPEOperator._inference_path) = saved
+
+
+def build_model(name, device):
+    from visionhope_b200.backbone import create_model, prepare_for_inference
+
+    torch.manual_seed(3)
+    model = create_model(name).to(device)
+    model = model.to(memory_format=torch.channels_last)
+    prepare_for_inference(model)
+    return model
+
+
+def cpu_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def run_cpu(args, steps, warmup):
+    """Time the CPU stand-in: returns (images/s, per-step seconds list, cores, sample text)."""
+    cores = cpu_threads()
+    torch.set_num_threads(cores)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    model = build_model(args.model, torch.device("cpu"))
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(args.cpu_sample, 3, IMG, IMG, generator=gen).contiguous(memory_format=torch.channels_last)
+    times = []
+    with cpu_reference_patches(), torch.inference_mode():
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            model(x)
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+    ips = args.cpu_sample * len(times) / sum(times)
+    sample = (f"{args.cpu_sample} images/step of the same {args.model} forward at {IMG}x{IMG}, fp32 on CPU "
+              f"(SRNL: oracle port, float, OpenMP; LN/GRN/convs: PyTorch CPU), {steps} timed steps")
+    return ips, times, cores, sample
+
+
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region (every 200 ms)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, devices):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        mhz, mx, reasons, power = [], [], set(), []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) not in devices:
+                    continue
+                mhz.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None, "samples": len(mhz),
+                "reasons": sorted(reasons)}
+
+
+def measure_ffma_peak(device):
+    """Measured FP32 (non-tensor) FMA throughput of this GPU, TFLOP/s (own probe kernel)."""
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks, iters = sms * 16, 4096
+    out = torch.empty(blocks * 256, device=device)
+    st = _lib.stream_handle(device)
+    for _ in range(2):
+        _lib.check(lib.vh_probe_ffma(out.data_ptr(), blocks, iters, st), "vh_probe_ffma")
+    best = 0.0
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        _lib.check(lib.vh_probe_ffma(out.data_ptr(), blocks, iters, st), "vh_probe_ffma")
+        b.record()
+        b.synchronize()
+        flops = 2.0 * 32 * iters * blocks * 256
+        best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)
+    return best
+
+
+def srnl_flops(B, H, W, heads, D=16):
+    """2 x the reference's analytic recurrence MACs (analysis/operation_count.py:226-258)."""
+    token = 6 * D * D + 20 * D
+    boundary = 3 * D ** 3 + 2 * D ** 2
+    macs = 0
+    for chunk, nchunks in ((W, H), (W, H), (H, W), (H, W)):
+        macs += B * heads * (nchunks * chunk * token + nchunks * boundary)
+    return 2.0 * macs
+
+
+def roofline_scan(args, device, steps):
+    """Time the fused SRNL operator alone at the stage-1 shape of this batch."""
+    from visionhope_b200.srnl_core.fused import spatial_forward
+
+    B, H, W, D = args.batch, IMG // 4, IMG // 4, 16
+    heads = 32 // D  # VisionHOPE-T stage 1: mixer_dim 32
+    C = heads * D
+    g = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(B, H, W, C, device=device, generator=g).to(torch.bfloat16)
+    q = torch.randn(B, H, W, C, device=device, generator=g).to(torch.bfloat16)
+    mems = [torch.randn(4, heads, D, D, device=device, generator=g) * 0.01 for _ in range(3)]
+    mems += [torch.zeros(4, heads, D, device=device) for _ in range(2)]
+    skip = torch.zeros(C, device=device)
+    wts = torch.ones(4, C, device=device)
+    out = torch.empty(B, H, W, C, device=device)
+    for _ in range(3):
+        spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", out=out)
+    torch.cuda.synchronize()
+    n = max(steps, 5)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", out=out)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / n
+    flops = srnl_flops(B, H, W, heads, D)
+    peak = measure_ffma_peak(device)
+    achieved = flops / (ms * 1e-3) / 1e12
+    alg_bytes = B * H * W * C * (2 + 2 + 4)
+    peaks = {}
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        peaks = json.loads(peaks_path.read_text())
+    return {
+        "kernel": "srnl_scan_kernel (fused 4-direction SRNL operator: rows + columns pass)",
+        "shape": f"B={B} H={H} W={W} C={C} heads={heads} D={D} bf16 in, fp32 out",
+        "bound": "fp32", "unit": "TFLOP/s", "achieved": achieved, "peak": peak,
+        "frac": achieved / peak if peak else None,
+        "peak_source": "measured FP32 FFMA probe on this GPU (vh_probe_ffma), no tensor cores",
+        "traffic": None, "launch_ms": ms, "flops_per_launch": flops,
+        "alg_bytes_per_launch": alg_bytes,
+        "hbm_frac_of_measured": (alg_bytes / (ms * 1e-3) / 1e9) / peaks["hbm_gbs"] if "hbm_gbs" in peaks else None,
+        "tensor_frac_of_measured": (achieved / peaks["bf16_tflops"]) if "bf16_tflops" in peaks else None,
+    }
+
+
+def run_ours(args, world, rank, local):
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from visionhope_b200 import _lib
+
+    model = build_model(args.model, device)
+    if world > 1:
+        for p in model.parameters():
+            dist.broadcast(p.data, 0)
+        for bname, buf in model.named_buffers():
+            dist.broadcast(buf, 0)
+    gen = torch.Generator(device=device).manual_seed(3 + rank)
+    static_in = torch.randn(args.batch, 3, IMG, IMG, device=device, generator=gen).contiguous(
+        memory_format=torch.channels_last)
+
+    def fwd():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(static_in)
+
+    with torch.inference_mode():
+        for _ in range(2):
+            out = fwd()
+        torch.cuda.synchronize()
+        c0 = _lib.launch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = fwd()
+        launches_per_step = _lib.launch_count - c0
+        gathered = [torch.empty_like(static_out) for _ in range(world)] if world > 1 else None
+        flush = torch.empty(64 * 1024 * 1024, device=device)  # 256 MiB
+
+        def step():
+            graph.replay()
+            if world > 1:
+                dist.all_gather(gathered, static_out)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        with ClockSampler() as clk:
+            for a, b in evs:
+                flush.fill_(1.0)
+                a.record()
+                step()
+                b.record()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        t = torch.tensor([ms], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+        clocks = clk.summary(set(range(torch.cuda.device_count())) if world > 1 else {device.index})
+
+        # ---- end to end: pinned host batch in, logits out, inside every timed step ----
+        host_in = torch.randn(args.batch, 3, IMG, IMG, generator=torch.Generator().manual_seed(3 + rank)
+                              ).contiguous(memory_format=torch.channels_last).pin_memory()
+        host_out = torch.empty(static_out.shape, dtype=static_out.dtype).pin_memory()
+
+        def e2e_step():
+            static_in.copy_(host_in, non_blocking=True)
+            graph.replay()
+            if world > 1:
+                dist.all_gather(gathered, static_out)
+            host_out.copy_(static_out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for a, b in evs:
+            flush.fill_(1.0)
+            a.record()
+            e2e_step()
+            b.record()
+        torch.cuda.synchronize()
+        e2e_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        t = torch.tensor([e2e_ms], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        if not torch.isfinite(host_out).all():
+            raise RuntimeError("non-finite logits")
+
+        roof = roofline_scan(args, device, args.steps) if rank == 0 else None
+        del graph
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": world * args.batch * 1000.0 / ms_max, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1) images, random-init weights (seed 3)",
+            "config": config(args, world),
+            "e2e": {"value": world * args.batch * 1000.0 / e2e_ms, "unit": UNIT,
+                    "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                    "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_per_step": launches_per_step,
+            "roofline": roof, "clocks": clocks,
+        }
+    return result
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if world > 1:
+        from datetime import timedelta
+
+        backend = "nccl" if args.impl == "ours" else "gloo"
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=timedelta(seconds=300))
+    try:
+        if args.impl == "reference":
+            if rank != 0:
+                return
+            ips, times, cores, sample = run_cpu(args, args.steps, args.warmup)
+            line = {"metric": METRIC, "value": ips, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(times),
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                    "data": "synthetic N(0,1) images, random-init weights (seed 3)", "impl": "reference",
+                    "config": dict(config(args, world), workload=f"{args.model} forward on host CPU "
+                                   f"(reference stand-in), {args.cpu_sample} images/step"),
+                    "cpu_baseline": {"value": ips, "unit": UNIT, "cores": cores, "kind": "port",
+                                     "sample": sample},
+                    "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+            return
+        result = run_ours(args, world, rank, local)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                ips, times, cores, sample = run_cpu(args, steps=2, warmup=1)
+                result["cpu_baseline"] = {"value": ips, "unit": UNIT, "cores": cores, "kind": "port",
+                                          "sample": sample}
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/* vhope.h -- C ABI of libvhope.so, the sm_100a implementation of VisionHOPE's inference
+ * hot path: the SRNL five-memory recurrence run as four directional chunked scans, spatial
+ * restoration and channel-wise direction fusion, query normalization, GRN and LayerNorm.
+ *
+ * Conventions (every entry point):
+ *   - Plain device pointers, element counts and element strides; no framework types.
+ *   - The caller allocates every output (the reference allocated inside each op, e.g.
+ *     models/srnl_core/csrc/fused.cu:334-335; here ownership moves to the caller so that
+ *     calls can be captured in CUDA graphs and hosts without an allocator can use them).
+ *   - Work is enqueued on `stream`; nothing synchronizes the host.
+ *   - Return 0 on success, a negative VH_E* code when validation rejects the call (nothing
+ *     was launched), or a positive cudaError_t when a launch failed.  vh_last_error()
+ *     returns a thread-local description of the most recent failure on this thread.
+ *   - Call vh_init(device) once per device before capturing any call in a CUDA graph; it
+ *     sets the kernels' shared-memory attributes (the reference did this on every call,
+ *     fused.cu:23-29).
+ *   - Stateless apart from that one-time set-up; thread-safe across streams.
+ */
+#ifndef VHOPE_H_
+#define VHOPE_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* vh_stream_t; /* a cudaStream_t */
+
+enum vh_dtype { VH_F32 = 0, VH_BF16 = 1, VH_F16 = 2 };
+
+enum vh_status {
+    VH_OK = 0,
+    VH_E_ARG = -1,      /* null pointer, bad enum, non-positive size */
+    VH_E_SHAPE = -2,    /* inconsistent shapes */
+    VH_E_DTYPE = -3,    /* unsupported dtype combination */
+    VH_E_HEADDIM = -4,  /* head_dim not in {4, 8, 16, 32, 64} */
+    VH_E_ALIGN = -5,    /* pointer or stride misaligned for vector access */
+    VH_E_RANGE = -6,    /* sizes beyond the supported index range */
+    VH_E_DEVICE = -7    /* device query / attribute set-up failed */
+};
+
+/* Recurrence constants (models/srnl_core/chunk.py:44-49, env-overridable there; runtime
+ * arguments here).  spectral_factor = 2 * spectral_margin (fused.py:61). */
+typedef struct {
+    float step_scale;       /* VISIONHOPE_STEP_SCALE, 0.025 */
+    float min_retention;    /* VISIONHOPE_MIN_RETENTION, 0.0 */
+    float retention_bias;   /* VISIONHOPE_RETENTION_BIAS, 2.197224577 */
+    float injection_margin; /* VISIONHOPE_INJECTION_MARGIN, 0.999 */
+    float spectral_factor;  /* 2 * VISIONHOPE_SPECTRAL_MARGIN, 1.999998 */
+    int32_t spectral_clamp; /* SPECTRAL_CLAMP, 1 */
+} vh_srnl_consts;
+
+/* The five initial memories of one SRNL module, fp32, contiguous.
+ * Matrices [dirs, heads, D, D] (content m, value v, key k), vectors [dirs, heads, D]
+ * (learning rate eta, retention alpha): models/srnl.py:55-68 (core order m, v, k, eta, alpha).
+ * per_chain != 0 selects one state per (batch, dir, head) chain, [B, dirs, heads, ...]
+ * (models/srnl_core/chunk.py:193-200, StateCount == N). */
+typedef struct {
+    const float* m;
+    const float* v;
+    const float* k;
+    const float* eta;
+    const float* alpha;
+    int32_t per_chain;
+} vh_srnl_memories;
+
+/* ---------------------------------------------------------------------------------------
+ * Fused four-direction spatial operator.
+ * Replaces models/srnl_core/csrc/fused.cu:307-351 `srnl_line_forward_seq_noatomic`
+ * (kernels parallel_line.cuh:26-59 + merge fused.cu:47-59), bound at
+ * models/operator.py:190 through models/srnl_core/fused.py:69-93.
+ *
+ *   out[b, h, w, c] = sum_d weight[d, c] * (y_d + skip_d[c] * x_d)   at the restored pixel,
+ *
+ * where y_d is the SRNL output of scan d: 0 row-major, 1 reversed row-major, 2 column-major,
+ * 3 reversed column-major (models/operator.py:79-86), chunk = W for rows, H for columns.
+ *
+ * Input addressing: element (b, d, t, head, i) -- batch b, scan d, token t, head, channel i
+ * of the head (unit stride) -- is read at
+ *   base + b*batch_stride + d*dir_stride + t*token_stride + head*head_stride + i.
+ *   remap == 0: x, q hold the four scans, e.g. [B, 4, L, C] (the reference's
+ *               srnl_line_forward_seq* layout: token_stride C, head_stride D) or packed
+ *               [B, 4, heads, L, D] (srnl_line_forward*: token_stride D, head_stride L*D).
+ *   remap == 1: x, q hold one image in row-major pixel order, e.g. channels-last
+ *               [B, H*W, C]; each scan reads it through its own index map (t -> pixel) and
+ *               dir_stride is ignored.
+ * x and q share dtype (VH_F32 / VH_BF16 / VH_F16).  out: fp32 [B, H, W, C], caller-allocated
+ * with out_batch_stride elements per image and C per pixel.
+ * skip: C values (shared across directions) or 4*C (skip_per_dir = 1); weight: fp32 [4, C].
+ * -------------------------------------------------------------------------------------*/
+typedef struct {
+    vh_srnl_memories mem;
+    const void* x;
+    const void* q;
+    int64_t x_batch_stride, x_dir_stride, x_token_stride, x_head_stride;
+    int64_t q_batch_stride, q_dir_stride, q_token_stride, q_head_stride;
+    int32_t io_dtype;
+    int32_t remap;
+    const float* skip;
+    int32_t skip_per_dir;
+    const float* weight;
+    float* out;
+    int64_t out_batch_stride;
+    int32_t batch, height, width, heads, head_dim;
+    vh_srnl_consts consts;
+} vh_srnl_spatial_args;
+
+int vh_srnl_spatial_fwd(const vh_srnl_spatial_args* args, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Packed-sequence recurrence (no fusion), y in the dtype of x:
+ *   x: [B, R, heads, L, D] packed (models/srnl.py:183-185), R in {1, 2, 4};
+ *   q_mode 0: raw queries [B, R, L, C] normalized inside (query_normalization folded in);
+ *   q_mode 1: unit-norm fp32 queries [B, R, heads, L, D];
+ *   chunk[r]: chunk length of direction r; tokens past L are zero (tail padding).
+ * Replaces, forward only:
+ *   models/srnl_core/csrc/fused.cu:131-179 `srnl_sequence_forward` (fused.py:96-106),
+ *   models/srnl_core/csrc/chunk.cu:1083-1131 `srnl_forward` / `srnl_forward_qraw`
+ *     (chunk.py:172-284, 366-505: srnl_normalized_query / srnl_raw_query),
+ *   models/srnl_core/csrc/lines.cu:3-237 large/varline forward (lines.py:183-671:
+ *     srnl_long_chunk / srnl_variable_lines).
+ * -------------------------------------------------------------------------------------*/
+typedef struct {
+    vh_srnl_memories mem;
+    const void* x;
+    const void* q;
+    void* y;
+    int32_t x_dtype;  /* dtype of x and y */
+    int32_t q_dtype;  /* == x_dtype for q_mode 0; VH_F32 for q_mode 1 */
+    int32_t q_mode;
+    int32_t batch, dirs, heads, length, head_dim;
+    int32_t chunk[4];
+    vh_srnl_consts consts;
+} vh_srnl_sequence_args;
+
+int vh_srnl_sequence_fwd(const vh_srnl_sequence_args* args, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Query normalization + relayout, replaces utils/csrc/query_normalization.cu:136-178,
+ * 223-265 `visionhope_qnorm_forward` (utils/query_normalization.py:53-90):
+ *   q_raw [B, R, L, C] (f32/bf16/f16) -> out fp32 [B, R, heads, L, D] = q / max(||q||, 1e-12),
+ *   inv_norm fp32 [B*R*L*heads] (may be NULL).
+ * -------------------------------------------------------------------------------------*/
+int vh_qnorm_fwd(const void* q_raw, int32_t q_dtype, float* out, float* inv_norm, int32_t batch,
+                 int32_t dirs, int32_t length, int32_t heads, int32_t head_dim, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Direction restoration + skip + scale fusion, replaces utils/csrc/direction_fusion.cu:
+ * 11-65, 505-575 `visionhope_postprocess_scale_forward` (utils/direction_fusion.py:84-145):
+ *   y, x: [B, 4, heads, L, D] (same dtype), skip fp32 C or 4*C values, scale fp32 [4, C];
+ *   out fp32 logical [B, C, H, W]: channels_last == 0 -> contiguous NCHW,
+ *   channels_last != 0 -> physical [B, H, W, C].
+ * -------------------------------------------------------------------------------------*/
+int vh_dirfuse_fwd(const void* y, const void* x, int32_t io_dtype, const float* skip,
+                   int32_t skip_per_dir, const float* scale, float* out, int32_t channels_last,
+                   int32_t batch, int32_t heads, int32_t height, int32_t width, int32_t head_dim,
+                   vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Global response norm on channels-last input, fp32 output; replaces utils/csrc/
+ * grn_cuda.cu:46-124, 267-300 `grn_forward_cuda` (utils/grn_cuda.py:103-117, utils/grn.py:41-70):
+ *   x physical [B, H, W, C] (f32/bf16/f16), gamma/beta fp32 [C], y fp32 [B, H, W, C];
+ *   y = x * (1 + gamma * Gx / (mean_c Gx + eps)) + beta, Gx[b,c] = ||x[b,:,:,c]||_2.
+ *   gx (fp32 [B, C]) and inv_den (fp32 [B]) receive the statistics (the reference saves them
+ *   for backward); both may be NULL.
+ *   workspace: caller-provided device scratch of vh_grn_workspace_bytes(...) bytes.
+ * -------------------------------------------------------------------------------------*/
+int64_t vh_grn_workspace_bytes(int32_t batch, int32_t height, int32_t width, int32_t channels);
+int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* beta, float eps,
+               float* y, float* gx, float* inv_den, void* workspace, int64_t workspace_bytes,
+               int32_t batch, int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * LayerNorm over the channel axis of channels-last rows, fp32 output; replaces the Triton
+ * kernel utils/layer_norm_cuda.py:31-57, 122-147 `visionhope_layernorm2d` and the
+ * F.layer_norm path of models/layers.py:17-35:
+ *   x [rows, C] (f32/bf16/f16), weight/bias fp32 [C], y fp32 [rows, C];
+ *   mean/rstd fp32 [rows] (may be NULL).
+ * -------------------------------------------------------------------------------------*/
+int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight, const float* bias,
+                     float eps, float* y, float* mean, float* rstd, int64_t rows, int32_t channels,
+                     vh_stream_t stream);
+
+/* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
+ * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it
+ * to measure the device's FP32 (non-tensor) FMA peak. */
+int vh_probe_ffma(float* out, int32_t blocks, int32_t iters, vh_stream_t stream);
+
+/* One-time per-device set-up (kernel shared-memory attributes).  Idempotent. */
+int vh_init(int32_t device);
+
+/* Thread-local description of the last failure on this thread ("" if none). */
+const char* vh_last_error(void);
+
+/* Library version string. */
+const char* vh_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VHOPE_H_ */

@@ -1,0 +1,144 @@
+"""Compile the reference's own CUDA kernels into ``oracle/_ref/`` (test infrastructure only).
+
+PSRben/VisionHOPE has no CPU implementation of SRNL, direction fusion or query
+normalization (``models/srnl.py:113-114`` rejects CPU tensors), and ships no golden
+vectors.  The strongest parity pin available is therefore the reference's own CUDA
+extensions, run on a B200.  This recipe:
+
+1. imports the reference package read-only from ``/root/reference`` (with a
+   four-alias ``timm`` shim, because timm is not installed) so that the reference
+   renders its own templated sources exactly as it does at run time
+   (``models/srnl_core/fused.py:51-64``, ``chunk.py:89-105``, ``lines.py:59-70``,
+   ``utils/query_normalization.py:28-33``, ``utils/direction_fusion.py:39-41``);
+2. compiles those rendered strings with ``torch.utils.cpp_extension.load_inline``
+   for sm_100a into ``oracle/_ref/<name>/`` (git-ignored; the built ``.so`` files
+   travel to the GPU box, the sources never enter the repository).
+
+The reference's own JIT loaders are not called; only the build flags it uses
+(``-O3 --use_fast_math``) are mirrored, plus an explicit ``-gencode`` for sm_100a.
+Nothing in the product imports this module or its outputs.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import tempfile
+import types
+from pathlib import Path
+
+REF_ROOT = Path(os.environ.get("VHOPE_REFERENCE", "/root/reference"))
+OUT_DIR = Path(__file__).resolve().parent / "_ref"
+GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _install_reference():
+    import torch
+
+    base = tempfile.mkdtemp(prefix="vhref_")
+    os.symlink(REF_ROOT, os.path.join(base, "visionhope"))
+    sys.path.insert(0, base)
+    if "timm" not in sys.modules:
+        timm = types.ModuleType("timm")
+        models = types.ModuleType("timm.models")
+        layers = types.ModuleType("timm.models.layers")
+        registry = types.ModuleType("timm.models.registry")
+        data = types.ModuleType("timm.data")
+        layers.trunc_normal_ = lambda t, mean=0.0, std=1.0, a=-2.0, b=2.0: torch.nn.init.trunc_normal_(
+            t, mean, std, a, b)
+
+        class DropPath(torch.nn.Module):
+            def __init__(self, p=0.0):
+                super().__init__()
+                self.drop_prob = p
+
+            def forward(self, x):
+                return x
+
+        layers.DropPath = DropPath
+        registry.register_model = lambda f: f
+        data.IMAGENET_DEFAULT_MEAN = (0.485, 0.456, 0.406)
+        data.IMAGENET_DEFAULT_STD = (0.229, 0.224, 0.225)
+        timm.models, models.layers, models.registry, timm.data = models, layers, registry, data
+        for name, mod in (("timm", timm), ("timm.models", models), ("timm.models.layers", layers),
+                          ("timm.models.registry", registry), ("timm.data", data)):
+            sys.modules[name] = mod
+
+
+def _targets():
+    """(extension name, cpp source, cuda source, exported functions) for every kernel we pin."""
+    import torch
+    import visionhope.models.srnl_core.chunk as chunk
+    import visionhope.models.srnl_core.fused as fused
+    import visionhope.models.srnl_core.lines as lines
+    import visionhope.utils.direction_fusion as dirfuse
+    import visionhope.utils.query_normalization as qnorm
+
+    fused_fns = ["srnl_line_forward_seq_noatomic", "srnl_sequence_forward"]
+    chunk_fns = ["srnl_forward", "srnl_forward_qraw"]
+    line_fns = ["srnl_forward_qraw_large", "srnl_forward_qraw_varline"]
+    base_chunk = chunk.cuda_helper_source
+    return [
+        ("vhref_fused_bf16", fused.cpp_source, fused.cuda_source, fused_fns),
+        ("vhref_fused_fp32", fused.cpp_source, fused.cuda_source_fp32, fused_fns),
+        ("vhref_chunk_bf16", chunk.cpp_source, chunk.cuda_source, chunk_fns),
+        ("vhref_chunk_fp32", chunk.cpp_source, chunk.cuda_source_fp32, chunk_fns),
+        ("vhref_lines_bf16", lines.cpp_source,
+         base_chunk + lines.large_cuda_source + lines.varline_cuda_source, line_fns),
+        ("vhref_qnorm_bf16", qnorm.cpp_source, qnorm.cuda_source, ["visionhope_qnorm_forward"]),
+        ("vhref_qnorm_fp32", qnorm.cpp_source, qnorm.cuda_source_fp32, ["visionhope_qnorm_forward"]),
+        ("vhref_dirfuse_bf16", dirfuse.cpp_source, dirfuse.cuda_source,
+         ["visionhope_postprocess_scale_forward"]),
+        ("vhref_dirfuse_fp32", dirfuse.cpp_source, dirfuse.cuda_source_fp32,
+         ["visionhope_postprocess_scale_forward"]),
+    ]
+
+
+def _grn_target():
+    src = REF_ROOT / "utils" / "csrc"
+    return "vhref_grn", [str(src / "grn.cpp"), str(src / "grn_cuda.cu")]
+
+
+def build(only=None):
+    if not REF_ROOT.is_dir():
+        raise FileNotFoundError(f"reference tree not found at {REF_ROOT}")
+    _install_reference()
+    from torch.utils.cpp_extension import load, load_inline
+
+    OUT_DIR.mkdir(parents=True, exist_ok=True)
+    flags = ["-O3", "--use_fast_math", *GENCODE]
+    built = []
+    for name, cpp, cuda, fns in _targets():
+        if only and name not in only:
+            continue
+        build_dir = OUT_DIR / name
+        build_dir.mkdir(parents=True, exist_ok=True)
+        load_inline(name=name, cpp_sources=cpp, cuda_sources=cuda, functions=fns,
+                    extra_cuda_cflags=flags, build_directory=str(build_dir), verbose=False)
+        built.append(name)
+    name, sources = _grn_target()
+    if not only or name in only:
+        build_dir = OUT_DIR / name
+        build_dir.mkdir(parents=True, exist_ok=True)
+        load(name=name, sources=sources, extra_cuda_cflags=["-O3", *GENCODE], extra_cflags=["-O3"],
+             build_directory=str(build_dir), verbose=False)
+        built.append(name)
+    return built
+
+
+def load_built(name):
+    """Import a previously built reference extension from ``oracle/_ref/<name>/``."""
+    import importlib.util
+
+    import torch  # noqa: F401  (the extension links against libtorch)
+
+    path = OUT_DIR / name / f"{name}.so"
+    if not path.is_file():
+        raise FileNotFoundError(f"reference extension {name} not built at {path}")
+    spec = importlib.util.spec_from_file_location(name, path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+if __name__ == "__main__":
+    print("built:", build(sys.argv[1:] or None))

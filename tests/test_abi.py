@@ -1,0 +1,123 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol declared in
+include/vhope.h, and rejects invalid arguments before any CUDA call (status + message)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "vhope.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(vh_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_symbols()
+    for want in ("vh_srnl_spatial_fwd", "vh_srnl_sequence_fwd", "vh_qnorm_fwd", "vh_dirfuse_fwd",
+                 "vh_grn_fwd", "vh_grn_workspace_bytes", "vh_layernorm_fwd", "vh_init",
+                 "vh_last_error", "vh_version"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert "sm_100a" in _lib.version()
+
+
+def test_struct_layouts_match_header_sizes():
+    from visionhope_b200 import _lib
+
+    # 6 x 4-byte fields; 5 pointers + int (padded); see include/vhope.h
+    assert ctypes.sizeof(_lib.VhConsts) == 24
+    assert ctypes.sizeof(_lib.VhMemories) == 48
+    assert ctypes.sizeof(_lib.VhSequenceArgs) == 48 + 3 * 8 + 8 * 4 + 4 * 4 + 24 + 0
+
+
+def _err(lib):
+    return lib.vh_last_error().decode()
+
+
+def test_null_arguments_are_rejected_without_a_gpu():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.vh_srnl_spatial_fwd(None, None) == -1
+    assert "null" in _err(lib)
+    args = _lib.VhSpatialArgs()
+    assert lib.vh_srnl_spatial_fwd(ctypes.byref(args), None) == -1
+    seq = _lib.VhSequenceArgs()
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq), None) == -1
+    assert lib.vh_qnorm_fwd(None, 1, None, None, 1, 4, 1, 1, 16, None) == -1
+    assert lib.vh_dirfuse_fwd(None, None, 1, None, 0, None, None, 0, 1, 1, 1, 1, 16, None) == -1
+    assert lib.vh_layernorm_fwd(None, 0, None, None, 1e-6, None, None, None, 1, 4, None) == -1
+
+
+def _fake(n=1 << 12):
+    """A host buffer used only as a non-null, aligned address (validation never dereferences)."""
+    buf = (ctypes.c_float * n)()
+    return ctypes.addressof(buf), buf
+
+
+@pytest.mark.parametrize("head_dim,code", [(12, -4), (0, -4), (128, -4)])
+def test_bad_head_dim(head_dim, code):
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    seq = _lib.VhSequenceArgs(_lib.VhMemories(p, p, p, p, p, 0), p, p, p, 0, 0, 0, 1, 1, 1, 8,
+                              head_dim, (_lib.c_int32 * 4)(4, 4, 4, 4), _lib.consts(0.025, 0, 2.2, 0.999, 0.999999))
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq), None) == code
+    assert "head_dim" in _err(lib)
+
+
+def test_sequence_validation_messages():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    k = _lib.consts(0.025, 0, 2.2, 0.999, 0.999999)
+
+    def seq(**kw):
+        base = dict(x_dtype=0, q_dtype=0, q_mode=0, batch=1, dirs=1, heads=1, length=8, head_dim=16,
+                    chunk=(4, 4, 4, 4))
+        base.update(kw)
+        return _lib.VhSequenceArgs(_lib.VhMemories(p, p, p, p, p, 0), p, p, p, base["x_dtype"],
+                                   base["q_dtype"], base["q_mode"], base["batch"], base["dirs"],
+                                   base["heads"], base["length"], base["head_dim"],
+                                   (_lib.c_int32 * 4)(*base["chunk"]), k)
+
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(dirs=3)), None) == -2
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(batch=0)), None) == -2
+    assert "nonempty" in _err(lib)
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(chunk=(0, 4, 4, 4))), None) == -2
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(x_dtype=1, q_dtype=0)), None) == -3
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(q_mode=1, q_dtype=1, x_dtype=1)), None) == -3
+    assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq(x_dtype=7, q_dtype=7)), None) == -3
+
+
+def test_spatial_misalignment_is_rejected():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    k = _lib.consts(0.025, 0, 2.2, 0.999, 0.999999)
+    C = 32
+    args = _lib.VhSpatialArgs(_lib.VhMemories(p, p, p, p, p, 0), p + 2, p, 4 * 16 * C, 16 * C, C, 16,
+                              4 * 16 * C, 16 * C, C, 16, 1, 0, p, 0, p, p, 16 * C, 1, 4, 4, 2, 16, k)
+    assert lib.vh_srnl_spatial_fwd(ctypes.byref(args), None) == -5
+    assert "aligned" in _err(lib)
+
+
+def test_grn_workspace_query():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.vh_grn_workspace_bytes(128, 56, 56, 96) > 0
+    assert lib.vh_grn_workspace_bytes(0, 56, 56, 96) == 0

@@ -1,0 +1,105 @@
+"""GPU parity of query normalization, direction fusion, GRN and LayerNorm against the oracle
+(fp32 outputs: 1e-4 normwise relative error; these are pure-fp32 arithmetic kernels)."""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def _dev(a, dev, dt=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev, dt)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("D", [4, 16, 64])
+def test_qnorm(dt, D, oracle, cuda):
+    from visionhope_b200.utils.query_normalization import visionhope_qnorm
+
+    gen = np.random.default_rng(D)
+    B, L, heads = 2, 37, 3
+    q = _dev(gen.normal(size=(B, 4, L, heads * D)), cuda, DT[dt])
+    q[0, 1, 3] = 0  # an all-zero query row hits the 1e-12 floor
+    out = visionhope_qnorm(q, heads, D)
+    exp, _ = oracle.qnorm(q, heads, D)
+    assert out.dtype == torch.float32 and tuple(out.shape) == (B, 4, heads, L, D)
+    assert rel_err(out.cpu().numpy(), exp) < 1e-6
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("channels_last", [False, True])
+@pytest.mark.parametrize("per_dir", [False, True])
+def test_direction_fusion(dt, channels_last, per_dir, oracle, cuda):
+    from visionhope_b200.utils.direction_fusion import visionhope_postprocess_scale
+
+    gen = np.random.default_rng(3)
+    B, heads, H, W, D = 2, 3, 9, 13, 16
+    C = heads * D
+    y = _dev(gen.normal(size=(B, 4, heads, H * W, D)), cuda, DT[dt])
+    x = _dev(gen.normal(size=(B, 4, heads, H * W, D)), cuda, DT[dt])
+    skip = _dev(gen.normal(size=(4, heads, D) if per_dir else (heads, D)), cuda)
+    scale = _dev(gen.normal(1, 0.3, size=(4, C)), cuda)
+    out = visionhope_postprocess_scale(y, x, skip, scale, H, W, channels_last)
+    exp = oracle.dirfuse(y, x, skip, scale, H, W, False)
+    assert out.shape == (B, C, H, W)
+    assert out.is_contiguous(memory_format=torch.channels_last if channels_last else torch.contiguous_format)
+    assert rel_err(out.cpu().numpy(), exp) < 1e-6
+
+
+GRN_CASES = [(4, 14, 14, 96, "f32"), (3, 7, 7, 768, "bf16"), (2, 5, 3, 2048, "f16"),
+             (1, 56, 56, 32, "bf16"), (6, 1, 1, 12, "f32"), (2, 9, 9, 4100, "f32")]
+
+
+@pytest.mark.parametrize("case", GRN_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_grn(case, oracle, cuda):
+    from visionhope_b200.utils.grn import global_response_norm
+
+    B, H, W, C, dt = case
+    gen = np.random.default_rng(zlib.crc32(repr(case).encode()))
+    x_nhwc = gen.normal(size=(B, H, W, C))
+    x = _dev(x_nhwc, cuda, DT[dt]).permute(0, 3, 1, 2)  # channels-last logical NCHW
+    gamma = _dev(gen.normal(0, 0.02, size=(1, C, 1, 1)), cuda)
+    beta = _dev(gen.normal(0, 0.02, size=(1, C, 1, 1)), cuda)
+    y = global_response_norm(x, gamma, beta)
+    exp = oracle.grn_nhwc(x.permute(0, 2, 3, 1), gamma, beta)
+    assert y.dtype == torch.float32 and y.is_contiguous(memory_format=torch.channels_last)
+    assert rel_err(y.permute(0, 2, 3, 1).cpu().numpy(), exp) < 1e-5
+
+
+def test_grn_stats_outputs(oracle, cuda):
+    from visionhope_b200.utils.grn_cuda import grn_forward
+
+    gen = np.random.default_rng(9)
+    x = _dev(gen.normal(size=(3, 10, 10, 64)), cuda).permute(0, 3, 1, 2)
+    g, b = _dev(gen.normal(size=64), cuda), _dev(gen.normal(size=64), cuda)
+    _, gx, inv = grn_forward(x, g, b, 1e-6, want_stats=True)
+    xn = x.permute(0, 2, 3, 1).double().cpu()
+    gx_exp = xn.pow(2).sum(dim=(1, 2)).sqrt()
+    assert torch.allclose(gx.double().cpu(), gx_exp, rtol=1e-5)
+    assert torch.allclose(inv.double().cpu(), 1.0 / (gx_exp.mean(1) + 1e-6), rtol=1e-5)
+
+
+LN_CASES = [(4, 14, 14, 96, "f32"), (3, 7, 7, 768, "bf16"), (2, 56, 56, 64, "bf16"),
+            (2, 5, 5, 32, "f16"), (2, 3, 3, 2048, "f32"), (2, 4, 4, 100, "f32"),
+            (1, 3, 3, 4099, "bf16"), (1, 2, 2, 30, "f32")]
+
+
+@pytest.mark.parametrize("case", LN_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_layernorm(case, oracle, cuda):
+    from visionhope_b200.utils.layer_norm_cuda import visionhope_layernorm2d
+
+    B, H, W, C, dt = case
+    gen = np.random.default_rng(zlib.crc32(repr(case).encode()))
+    x = _dev(gen.normal(size=(B, H, W, C)) * 3 + 1, cuda, DT[dt]).permute(0, 3, 1, 2)
+    w = _dev(gen.normal(1, 0.02, size=C), cuda)
+    b = _dev(gen.normal(0, 0.02, size=C), cuda)
+    y = visionhope_layernorm2d(x, w, b, 1e-6)
+    exp = oracle.layernorm_rows(x.permute(0, 2, 3, 1).reshape(-1, C), w, b)
+    assert y.dtype == torch.float32 and y.shape == (B, C, H, W)
+    assert rel_err(y.permute(0, 2, 3, 1).reshape(-1, C).cpu().numpy(), exp) < 1e-5

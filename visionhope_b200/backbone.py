@@ -1,0 +1,319 @@
+"""VisionHOPE backbone assembly used to drive the hot path end to end (configs 4 and 5).
+
+This is caller code, not part of the hot path: it wires cuDNN convolutions, cuBLAS
+projections and BatchNorm around the library's operator, LayerNorm and GRN so that
+whole-model throughput can be measured.  Parameter names and shapes match the
+reference's modules (models/block.py, models/layers.py, models/hierarchical.py,
+models/factory.py) so a reference state_dict loads unchanged; the forward order of
+every block follows models/block.py:63-106 and the prepared fast branch block.py:73-80.
+Every LayerNorm, GRN and SRNL operator call runs on libvhope.so.
+"""
+from __future__ import annotations
+
+from copy import deepcopy
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from .operator import VisionHOPEOperator
+from .srnl import SRNL, trunc_normal_
+from .utils.grn import GlobalResponseNorm
+from .utils.layer_norm_cuda import layernorm_rows
+
+MODEL_CONFIGS = {
+    "visionhope_tiny": dict(embed_dims=(64, 128, 256, 512), mixer_dims=(32, 64, 128, 256),
+                            depths=(3, 4, 18, 4)),
+    "visionhope_small": dict(embed_dims=(64, 160, 320, 512), mixer_dims=(32, 80, 160, 256),
+                             depths=(4, 8, 25, 8)),
+    "visionhope_base": dict(embed_dims=(96, 192, 448, 640), mixer_dims=(48, 96, 224, 320),
+                            depths=(4, 8, 25, 8)),
+}
+
+
+class LayerNorm2d(nn.Module):
+    """LayerNorm over the channels of an NCHW tensor; fp32 output in channels-last storage.
+
+    Replaces models/layers.py:9-35: both the Triton path and the ``inference_layout``
+    F.layer_norm path map to ``vh_layernorm_fwd``.
+    """
+
+    def __init__(self, dim, eps=1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.bias = nn.Parameter(torch.zeros(dim))
+        self.eps = eps
+        self.inference_layout = False
+
+    def forward(self, x):
+        b, c, h, w = x.shape
+        rows = x.permute(0, 2, 3, 1)
+        if not rows.is_contiguous():
+            rows = rows.contiguous()
+        y = layernorm_rows(rows.reshape(b * h * w, c), self.weight, self.bias, self.eps)
+        return y.view(b, h, w, c).permute(0, 3, 1, 2)
+
+
+def build_norm(dim, norm_layer="group"):
+    if norm_layer == "group":
+        return nn.GroupNorm(1, dim)
+    if norm_layer == "layernorm2d":
+        return LayerNorm2d(dim)
+    raise ValueError(f"Unsupported norm_layer={norm_layer!r}.")
+
+
+class FeedForwardNetwork(nn.Module):
+    """1x1 expand, GELU, residual depthwise 3x3 + GELU, GRN (fp32), 1x1 project."""
+
+    def __init__(self, in_features, hidden_features=None, out_features=None, act_layer=nn.GELU,
+                 drop=0.0, use_grn=False, use_dwconv=False):
+        super().__init__()
+        hidden_features = hidden_features or in_features
+        out_features = out_features or in_features
+        self.fc1 = nn.Conv2d(in_features, hidden_features, kernel_size=1)
+        self.act = act_layer()
+        self.use_dwconv = use_dwconv
+        self.dwconv = (nn.Conv2d(hidden_features, hidden_features, kernel_size=3, padding=1,
+                                 groups=hidden_features) if use_dwconv else nn.Identity())
+        self.dwconv_act = act_layer() if use_dwconv else nn.Identity()
+        self.grn = GlobalResponseNorm(hidden_features) if use_grn else nn.Identity()
+        self.fc2 = nn.Conv2d(hidden_features, out_features, kernel_size=1)
+        self.drop = nn.Dropout(drop)
+
+    def forward(self, x):
+        x = self.act(self.fc1(x))
+        if self.use_dwconv:
+            x = self.dwconv_act(x + self.dwconv(x))
+        x = self.drop(self.grn(x))
+        return self.drop(self.fc2(x))
+
+
+class PatchEmbedding(nn.Module):
+    """Stride-4 convolutional stem: conv/BN/GELU x3 then conv/BN (layers.py:85-107)."""
+
+    def __init__(self, in_chans, embed_dim, patch_size=4):
+        super().__init__()
+        if patch_size != 4:
+            raise ValueError("The VisionHOPE stem requires patch_size=4")
+        widths = [embed_dim // 2, embed_dim // 2, embed_dim, embed_dim]
+        strides = [2, 1, 2, 1]
+        if min(widths) <= 0:
+            raise ValueError("embed_dim is too small for the convolutional stem")
+        layers = []
+        for i, (width, stride) in enumerate(zip(widths, strides)):
+            layers += [nn.Conv2d(in_chans, width, 3, stride=stride, padding=1), nn.BatchNorm2d(width)]
+            if i < 3:
+                layers.append(nn.GELU())
+            in_chans = width
+        self.proj = nn.Sequential(*layers)
+        self.norm = nn.Identity()
+
+    def forward(self, x):
+        return self.norm(self.proj(x))
+
+
+class Downsample(nn.Module):
+    def __init__(self, in_dim, out_dim):
+        super().__init__()
+        self.proj = nn.Conv2d(in_dim, out_dim, 3, stride=2, padding=1, bias=False)
+        self.norm = nn.BatchNorm2d(out_dim)
+
+    def forward(self, x):
+        return self.norm(self.proj(x))
+
+
+class VisionHOPEBlock(nn.Module):
+    """cpe -> norm1 -> local features -> operator (+ output position conv) -> proj_out -> residual,
+    then norm2 -> FFN(GRN) -> residual, with optional LayerScale (models/block.py:13-106)."""
+
+    def __init__(self, dim, head_dim=16, chunk_size=None, mlp_ratio=4.0, drop_path=0.0,
+                 mixer_dim=None, local_mode="gated_dwconv7", norm_layer="layernorm2d",
+                 layer_scale_init_value=1e-6, use_grn=True, use_mlp_dwconv=True,
+                 use_direction_scale=True, direction_merge="sum", use_block_cpe=True,
+                 use_output_lepe=True, share_direction_skip=True):
+        super().__init__()
+        mixer_dim = int(mixer_dim) if mixer_dim is not None else dim
+        if local_mode not in {"gated_dwconv7", "residual_dwconv", "silu_dwconv"}:
+            raise ValueError("Unsupported local_mode")
+        self.dim, self.mixer_dim, self.local_mode = dim, mixer_dim, local_mode
+        self._inference_prepared = False
+        self.cpe = nn.Conv2d(dim, dim, 3, padding=1, groups=dim) if use_block_cpe else None
+        self.norm1 = build_norm(dim, norm_layer)
+        self.proj_in = nn.Conv2d(dim, mixer_dim, 1)
+        if use_direction_scale and direction_merge == "sum":
+            direction_merge = "scale"
+        self.operator = VisionHOPEOperator(mixer_dim, head_dim, chunk_size, direction_merge,
+                                           share_direction_skip, _initialize=False)
+        k = 7 if local_mode == "gated_dwconv7" else 3
+        self.local_conv = nn.Conv2d(mixer_dim, mixer_dim, k, padding=k // 2, groups=mixer_dim)
+        self.local_gate = nn.Conv2d(mixer_dim, mixer_dim, 1) if local_mode == "gated_dwconv7" else None
+        self.local_act = nn.SiLU() if local_mode == "silu_dwconv" else nn.Identity()
+        self.local_position = (nn.Conv2d(mixer_dim, mixer_dim, 5, padding=2, groups=mixer_dim)
+                               if use_output_lepe else None)
+        self.proj_out = nn.Linear(mixer_dim, dim)
+        self.operator.reset_parameters()
+        trunc_normal_(self.proj_out.weight, std=0.02)
+        nn.init.zeros_(self.proj_out.bias)
+        self.drop_path = nn.Identity()  # inference only: stochastic depth is the identity
+        self.drop_path_rate = float(drop_path)
+        self.norm2 = build_norm(dim, norm_layer)
+        self.ffn = FeedForwardNetwork(dim, int(dim * mlp_ratio), use_grn=use_grn, use_dwconv=use_mlp_dwconv)
+        if layer_scale_init_value is not None and layer_scale_init_value > 0.0:
+            self.gamma1 = nn.Parameter(layer_scale_init_value * torch.ones(dim, 1, 1))
+            self.gamma2 = nn.Parameter(layer_scale_init_value * torch.ones(dim, 1, 1))
+        else:
+            self.gamma1 = None
+            self.gamma2 = None
+
+    def _local_features(self, x):
+        inner = self.proj_in(x)
+        if self.local_mode == "gated_dwconv7":
+            return inner + torch.sigmoid(self.local_gate(inner)) * self.local_conv(inner)
+        conv = self.local_act(self.local_conv(inner))
+        return conv if self.local_mode == "silu_dwconv" else inner + conv
+
+    def spatial_branch(self, x):
+        channels_last = x.is_contiguous(memory_format=torch.channels_last)
+        x_local = self._local_features(x)
+        if self._inference_prepared:
+            path, _ = self.operator._inference_path(x_local)
+            if path != "ordinary":
+                out = self.operator._forward_fast(x_local, path)  # fp32 NHWC
+                if self.local_position is not None:
+                    out = out + self.local_position(x_local).permute(0, 2, 3, 1)
+                out = self.proj_out(out)
+                return out.permute(0, 3, 1, 2).contiguous()
+        out = self.operator(x_local, channels_last=channels_last)
+        if self.local_position is not None:
+            out = out + self.local_position(x_local)
+        out = F.conv2d(out, self.proj_out.weight[:, :, None, None], self.proj_out.bias)
+        return out.contiguous(memory_format=torch.channels_last if channels_last else torch.contiguous_format)
+
+    @staticmethod
+    def _residual(x, branch, gamma):
+        return x + branch if gamma is None else x + gamma * branch
+
+    def forward(self, x):
+        if self.training and self._inference_prepared:
+            raise RuntimeError("A block with folded LayerScale weights cannot be trained")
+        if self.cpe is not None:
+            x = x + self.cpe(x)
+        x = self._residual(x, self.spatial_branch(self.norm1(x)), self.gamma1)
+        return self._residual(x, self.ffn(self.norm2(x)), self.gamma2)
+
+
+def initialize_weights(module):
+    if isinstance(module, (nn.Linear, nn.Conv2d)):
+        trunc_normal_(module.weight, std=0.02)
+        if module.bias is not None:
+            nn.init.constant_(module.bias, 0)
+
+
+class HierarchicalVisionHOPE(nn.Module):
+    """Four-stage VisionHOPE with the projection classifier head (models/hierarchical.py:11-85)."""
+
+    def __init__(self, in_chans=3, num_classes=1000, embed_dims=(64, 128, 256, 512),
+                 mixer_dims=(32, 64, 128, 256), depths=(3, 4, 18, 4), chunk_sizes=None,
+                 mlp_ratios=(4.0, 4.0, 4.0, 4.0), head_dim=16, img_size=None, drop_path_rate=0.1,
+                 local_mode="gated_dwconv7", norm_layer="layernorm2d", layer_scale_init_value=1e-6,
+                 use_grn=True, use_mlp_dwconv=True, use_direction_scale=True, direction_merge="sum",
+                 use_block_cpe=True, use_output_lepe=True, projection_dim=1024,
+                 share_direction_skip=True):
+        super().__init__()
+        self.num_classes = num_classes
+        self.embed_dims = list(embed_dims)
+        self.mixer_dims = list(mixer_dims) if mixer_dims is not None else list(embed_dims)
+        self.depths = list(depths)
+        self.chunk_sizes = [None] * 4 if chunk_sizes is None else list(chunk_sizes)
+        self.head_dim = int(head_dim)
+        self.img_size = img_size
+        if isinstance(mlp_ratios, (int, float)):
+            mlp_ratios = [float(mlp_ratios)] * 4
+        if any(len(v) != 4 for v in (self.embed_dims, self.mixer_dims, self.depths, self.chunk_sizes,
+                                     mlp_ratios)):
+            raise ValueError("Hierarchical VisionHOPE requires four stage configurations")
+        self.downsample_layers = nn.ModuleList([PatchEmbedding(in_chans, embed_dims[0])])
+        for i in range(3):
+            self.downsample_layers.append(Downsample(embed_dims[i], embed_dims[i + 1]))
+        rates = [v.item() for v in torch.linspace(0, drop_path_rate, sum(depths))]
+        self.stages = nn.ModuleList()
+        offset = 0
+        for i in range(4):
+            self.stages.append(nn.Sequential(*[
+                VisionHOPEBlock(dim=embed_dims[i], head_dim=head_dim, chunk_size=self.chunk_sizes[i],
+                                mlp_ratio=mlp_ratios[i], drop_path=rates[offset + j],
+                                mixer_dim=self.mixer_dims[i], local_mode=local_mode,
+                                norm_layer=norm_layer, layer_scale_init_value=layer_scale_init_value,
+                                use_grn=use_grn, use_mlp_dwconv=use_mlp_dwconv,
+                                use_direction_scale=use_direction_scale, direction_merge=direction_merge,
+                                use_block_cpe=use_block_cpe, use_output_lepe=use_output_lepe,
+                                share_direction_skip=share_direction_skip)
+                for j in range(depths[i])]))
+            offset += depths[i]
+        self.norm = build_norm(embed_dims[-1], norm_layer)
+        self.head_pre_logits = nn.Conv2d(embed_dims[-1], projection_dim, 1)
+        self.head_norm = nn.BatchNorm2d(projection_dim)
+        self.head_act = nn.SiLU()
+        self.num_features = int(projection_dim)
+        self.head = nn.Linear(self.num_features, num_classes)
+        self.apply(initialize_weights)
+
+    def forward_intermediates(self, x):
+        outs = []
+        for down, stage in zip(self.downsample_layers, self.stages):
+            x = stage(down(x))
+            outs.append(x)
+        return tuple(outs)
+
+    def forward_features(self, x):
+        for down, stage in zip(self.downsample_layers, self.stages):
+            x = stage(down(x))
+        x = self.head_act(self.head_norm(self.head_pre_logits(self.norm(x))))
+        return x.mean(dim=[2, 3])
+
+    def forward(self, x):
+        return self.head(self.forward_features(x))
+
+
+def create_model(name, **kwargs):
+    if name not in MODEL_CONFIGS:
+        raise ValueError(f"Unknown model {name!r}; choose from {tuple(MODEL_CONFIGS)}")
+    config = deepcopy(MODEL_CONFIGS[name])
+    config.update(kwargs)
+    return HierarchicalVisionHOPE(**config)
+
+
+def prepare_for_inference(model):
+    """Eval mode, fast SRNL inference, LayerScale folded into proj_out / fc2
+    (inference/prepare.py:12-54).  Returns preparation counts."""
+    blocks = [m for m in model.modules() if isinstance(m, VisionHOPEBlock)]
+    model.eval()
+    counts = dict(line_mixer=0, srnl=0, operator=0, layernorm2d=0, grn=0, layerscale=0)
+    for m in model.modules():
+        if isinstance(m, SRNL):
+            m.fast_inference = True
+            counts["srnl"] += 1
+        elif isinstance(m, VisionHOPEOperator):
+            counts["operator"] += 1
+        elif isinstance(m, LayerNorm2d):
+            m.inference_layout = True
+            counts["layernorm2d"] += 1
+        elif isinstance(m, GlobalResponseNorm):
+            counts["grn"] += 1
+    with torch.no_grad():
+        for block in blocks:
+            counts["line_mixer"] += 1
+            for gname, proj in (("gamma1", block.proj_out), ("gamma2", block.ffn.fc2)):
+                gamma = getattr(block, gname)
+                if gamma is None:
+                    continue
+                scale = gamma.detach().view(-1).to(dtype=proj.weight.dtype, device=proj.weight.device)
+                proj.weight.mul_(scale.view((-1,) + (1,) * (proj.weight.ndim - 1)))
+                if proj.bias is not None:
+                    proj.bias.mul_(scale)
+                setattr(block, gname, None)
+                counts["layerscale"] += 1
+            block._inference_prepared = True
+    if blocks:
+        model._inference_prepared = True
+    return counts

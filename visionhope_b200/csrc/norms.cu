@@ -1,0 +1,322 @@
+// GRN and channel LayerNorm kernels on channels-last rows, fp32 output, with C entry points.
+// Both are HBM-bound: every load/store is a 4-channel vector and grids cover all SMs.
+#include <algorithm>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace vh {
+
+// =============================== GRN (utils/csrc/grn_cuda.cu:46-124) ==========================
+// Pass 1: per (b, pixel slice) partial sums of x^2 per channel -> workspace [B, splits, C].
+// Pass 2: every CTA of (b, slice) folds the partials into Gx[c] = sqrt(sum), the per-image
+//         1 / (mean_c Gx + eps), a per-channel factor f[c] = 1 + gamma[c] Gx[c] inv_den, and
+//         writes y = x f[c] + beta[c] for its slice.
+constexpr int kGrnThreads = 256;
+constexpr int kGrnTargetCtas = 600;  // ~4 CTAs per SM on a 148-SM B200
+
+inline int grn_splits(int B, int64_t S) {
+    int64_t s = (kGrnTargetCtas + B - 1) / B;
+    s = std::min<int64_t>(s, std::max<int64_t>(1, S / 8));
+    return (int)std::max<int64_t>(1, std::min<int64_t>(s, 1024));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGrnThreads) grn_stats_kernel(const T* __restrict__ x,
+                                                                float* __restrict__ part, int C,
+                                                                int64_t S, int splits) {
+    extern __shared__ float red[];  // [rphases][Geff * 4]
+    const int b = blockIdx.y, split = blockIdx.x;
+    const int G = C / 4;
+    const int Geff = min(G, kGrnThreads);
+    const int rph = kGrnThreads / Geff;
+    const int gi = threadIdx.x % Geff, ri = threadIdx.x / Geff;
+    const int64_t s0 = S * split / splits, s1 = S * (split + 1) / splits;
+    const T* xb = x + (int64_t)b * S * C;
+    for (int gb = 0; gb < G; gb += Geff) {
+        const int g = gb + gi;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ri < rph && g < G) {
+            for (int64_t s = s0 + ri; s < s1; s += rph) {
+                const float4 v = load4(xb + s * C + 4 * g);
+                acc.x = fmaf(v.x, v.x, acc.x);
+                acc.y = fmaf(v.y, v.y, acc.y);
+                acc.z = fmaf(v.z, v.z, acc.z);
+                acc.w = fmaf(v.w, v.w, acc.w);
+            }
+        }
+        if (ri < rph) {
+            float* r = red + ((size_t)ri * Geff + gi) * 4;
+            r[0] = acc.x; r[1] = acc.y; r[2] = acc.z; r[3] = acc.w;
+        }
+        __syncthreads();
+        for (int it = threadIdx.x; it < Geff * 4; it += blockDim.x) {
+            const int cg = gb * 4 + it;
+            float sum = 0.f;
+            for (int k = 0; k < rph; ++k) sum += red[(size_t)k * Geff * 4 + it];
+            if (cg < C) part[((int64_t)b * splits + split) * C + cg] = sum;
+        }
+        __syncthreads();
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
+    const T* __restrict__ x, const float* __restrict__ part, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, float* __restrict__ y, float* __restrict__ gx_out,
+    float* __restrict__ inv_out, int C, int64_t S, int splits) {
+    extern __shared__ float fac[];  // [C] factors, then [32] reduction scratch
+    float* scratch = fac + C;
+    const int b = blockIdx.y, split = blockIdx.x;
+    const float* pb = part + (int64_t)b * splits * C;
+    float local = 0.f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < splits; ++k) s += pb[(int64_t)k * C + c];
+        const float g = sqrtf(s);
+        fac[c] = g;
+        local += g;
+    }
+    local = warp_sum(local);
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? scratch[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) scratch[0] = 1.f / (v / (float)C + eps);
+    }
+    __syncthreads();
+    const float inv_den = scratch[0];
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float g = fac[c];
+        if (split == 0 && gx_out) gx_out[(int64_t)b * C + c] = g;
+        fac[c] = 1.f + gamma[c] * (g * inv_den);
+    }
+    if (split == 0 && inv_out && threadIdx.x == 0) inv_out[b] = inv_den;
+    __syncthreads();
+    const int G = C / 4;
+    const int64_t s0 = S * split / splits, s1 = S * (split + 1) / splits;
+    const int64_t n = (s1 - s0) * G;
+    const T* xb = x + ((int64_t)b * S + s0) * C;
+    float* yb = y + ((int64_t)b * S + s0) * C;
+    for (int64_t it = threadIdx.x; it < n; it += blockDim.x) {
+        const int64_t s = it / G;
+        const int c = (int)(it % G) * 4;
+        const float4 v = load4(xb + s * C + c);
+        float4 o;
+        o.x = fmaf(v.x, fac[c + 0], beta[c + 0]);
+        o.y = fmaf(v.y, fac[c + 1], beta[c + 1]);
+        o.z = fmaf(v.z, fac[c + 2], beta[c + 2]);
+        o.w = fmaf(v.w, fac[c + 3], beta[c + 3]);
+        store4(yb + s * C + c, o);
+    }
+}
+
+// ====================== LayerNorm over channels (layer_norm_cuda.py:31-57) ======================
+// SW lanes per row (SW in {8, 16, 32}), each lane holds NV 4-channel vectors in registers;
+// mean and biased variance by two in-register passes (the Triton kernel's order).
+constexpr int kLnThreads = 256;
+
+template <typename T, int SW, int NV>
+__global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
+                                                        const float* __restrict__ w,
+                                                        const float* __restrict__ bias, float eps,
+                                                        float* __restrict__ y, float* __restrict__ mean_out,
+                                                        float* __restrict__ rstd_out, int64_t rows, int C) {
+    const int lane = threadIdx.x % SW;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / SW;
+    const unsigned mask = SW == 32 ? 0xffffffffu : (((1u << SW) - 1u) << ((threadIdx.x & 31) & ~(SW - 1)));
+    const bool live = row < rows;
+    const int G = C / 4;
+    const T* xr = x + (live ? row : 0) * C;
+    float4 v[NV];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int g = lane + k * SW;
+        if (live && g < G) {
+            v[k] = load4(xr + 4 * g);
+            s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        } else {
+            v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+#pragma unroll
+    for (int o = SW / 2; o > 0; o >>= 1) s += __shfl_xor_sync(mask, s, o, SW);
+    const float mean = s / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int g = lane + k * SW;
+        if (g < G) {
+            const float a = v[k].x - mean, b2 = v[k].y - mean, c2 = v[k].z - mean, d = v[k].w - mean;
+            q += (a * a + b2 * b2) + (c2 * c2 + d * d);
+        }
+    }
+#pragma unroll
+    for (int o = SW / 2; o > 0; o >>= 1) q += __shfl_xor_sync(mask, q, o, SW);
+    const float rstd = 1.f / sqrtf(q / (float)C + eps);
+    if (!live) return;
+    float* yr = y + row * C;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int g = lane + k * SW;
+        if (g < G) {
+            const int c = 4 * g;
+            float4 o;
+            o.x = (v[k].x - mean) * rstd * w[c + 0] + bias[c + 0];
+            o.y = (v[k].y - mean) * rstd * w[c + 1] + bias[c + 1];
+            o.z = (v[k].z - mean) * rstd * w[c + 2] + bias[c + 2];
+            o.w = (v[k].w - mean) * rstd * w[c + 3] + bias[c + 3];
+            store4(yr + c, o);
+        }
+    }
+    if (lane == 0) {
+        if (mean_out) mean_out[row] = mean;
+        if (rstd_out) rstd_out[row] = rstd;
+    }
+}
+
+// Any C: one warp per row, scalar accesses, two passes over global memory.
+template <typename T>
+__global__ void __launch_bounds__(kLnThreads) ln_generic_kernel(const T* __restrict__ x,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias, float eps,
+                                                                float* __restrict__ y,
+                                                                float* __restrict__ mean_out,
+                                                                float* __restrict__ rstd_out,
+                                                                int64_t rows, int C) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    const T* xr = x + row * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) s += to_f(xr[c]);
+    s = warp_sum(s);
+    const float mean = s / (float)C;
+    float q = 0.f;
+    for (int c = lane; c < C; c += 32) {
+        const float a = to_f(xr[c]) - mean;
+        q += a * a;
+    }
+    q = warp_sum(q);
+    const float rstd = 1.f / sqrtf(q / (float)C + eps);
+    float* yr = y + row * C;
+    for (int c = lane; c < C; c += 32) yr[c] = (to_f(xr[c]) - mean) * rstd * w[c] + bias[c];
+    if (lane == 0) {
+        if (mean_out) mean_out[row] = mean;
+        if (rstd_out) rstd_out[row] = rstd;
+    }
+}
+
+template <typename T>
+int grn_run(const void* xv, const float* gamma, const float* beta, float eps, float* y, float* gx,
+            float* inv, float* part, int B, int64_t S, int C, cudaStream_t st) {
+    const T* x = static_cast<const T*>(xv);
+    const int splits = grn_splits(B, S);
+    const int G = C / 4;
+    const int Geff = std::min(G, kGrnThreads);
+    const int rph = kGrnThreads / Geff;
+    const size_t red_bytes = sizeof(float) * (size_t)rph * Geff * 4;
+    dim3 grid(splits, B);
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&grn_stats_kernel<T>), red_bytes))
+        return fail(VH_E_DEVICE, "grn: shared memory");
+    grn_stats_kernel<T><<<grid, kGrnThreads, red_bytes, st>>>(x, part, C, S, splits);
+    int rc = launch_status("grn stats");
+    if (rc) return rc;
+    const size_t fac_bytes = sizeof(float) * ((size_t)C + 32);
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&grn_apply_kernel<T>), fac_bytes))
+        return fail(VH_E_DEVICE, "grn: shared memory");
+    grn_apply_kernel<T><<<grid, kGrnThreads, fac_bytes, st>>>(x, part, gamma, beta, eps, y, gx, inv, C,
+                                                               S, splits);
+    return launch_status("grn apply");
+}
+
+template <typename T, int SW, int NV>
+int ln_launch(const void* x, const float* w, const float* b, float eps, float* y, float* m, float* r,
+              int64_t rows, int C, cudaStream_t st) {
+    const int64_t rows_per_cta = kLnThreads / SW;
+    const int64_t blocks = (rows + rows_per_cta - 1) / rows_per_cta;
+    ln_kernel<T, SW, NV><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
+                                                                  m, r, rows, C);
+    return launch_status("layernorm");
+}
+
+template <typename T>
+int ln_run(const void* x, const float* w, const float* b, float eps, float* y, float* m, float* r,
+           int64_t rows, int C, bool vec_ok, cudaStream_t st) {
+    const int G = C / 4;
+    if (vec_ok && C % 4 == 0) {
+        if (G <= 8) return ln_launch<T, 8, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 16) return ln_launch<T, 16, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 32) return ln_launch<T, 32, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 64) return ln_launch<T, 32, 2>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 128) return ln_launch<T, 32, 4>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 256) return ln_launch<T, 32, 8>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 512) return ln_launch<T, 32, 16>(x, w, b, eps, y, m, r, rows, C, st);
+    }
+    const int64_t blocks = (rows * 32 + kLnThreads - 1) / kLnThreads;
+    ln_generic_kernel<T><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
+                                                                  m, r, rows, C);
+    return launch_status("layernorm");
+}
+
+}  // namespace vh
+
+using namespace vh;
+
+namespace vh {
+int init_norm_kernels() { return 0; }
+}  // namespace vh
+
+extern "C" int64_t vh_grn_workspace_bytes(int32_t batch, int32_t height, int32_t width,
+                                          int32_t channels) {
+    if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0) return 0;
+    const int64_t S = (int64_t)height * width;
+    return (int64_t)sizeof(float) * batch * grn_splits(batch, S) * channels;
+}
+
+extern "C" int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* beta,
+                          float eps, float* y, float* gx, float* inv_den, void* workspace,
+                          int64_t workspace_bytes, int32_t batch, int32_t height, int32_t width,
+                          int32_t channels, vh_stream_t stream) {
+    clear_error();
+    if (!x || !gamma || !beta || !y || !workspace) return fail(VH_E_ARG, "vh_grn_fwd: null pointer argument");
+    if (!dtype_ok(x_dtype)) return fail(VH_E_DTYPE, "GRN supports FP32, FP16 and BF16 input");
+    if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0)
+        return fail(VH_E_SHAPE, "GRN expects nonempty input");
+    if (channels % 4) return fail(VH_E_SHAPE, "vh_grn_fwd: channels must be a multiple of 4");
+    if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_fwd: batch must be <= 65535");
+    if (!aligned(x, x_dtype == VH_F32 ? 16 : 8) || !aligned(y, 16) || !aligned(workspace, 16))
+        return fail(VH_E_ALIGN, "vh_grn_fwd: misaligned pointers");
+    if (workspace_bytes < vh_grn_workspace_bytes(batch, height, width, channels))
+        return fail(VH_E_ARG, "vh_grn_fwd: workspace too small (%lld < %lld bytes)",
+                    (long long)workspace_bytes,
+                    (long long)vh_grn_workspace_bytes(batch, height, width, channels));
+    if ((size_t)channels * 4 + 128 > 200 * 1024) return fail(VH_E_RANGE, "vh_grn_fwd: too many channels");
+    const int64_t S = (int64_t)height * width;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* part = static_cast<float*>(workspace);
+    switch (x_dtype) {
+        case VH_F32: return grn_run<float>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+        case VH_BF16: return grn_run<__nv_bfloat16>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+        default: return grn_run<__half>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+    }
+}
+
+extern "C" int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight,
+                                const float* bias, float eps, float* y, float* mean, float* rstd,
+                                int64_t rows, int32_t channels, vh_stream_t stream) {
+    clear_error();
+    if (!x || !weight || !bias || !y) return fail(VH_E_ARG, "vh_layernorm_fwd: null pointer argument");
+    if (!dtype_ok(x_dtype)) return fail(VH_E_DTYPE, "vh_layernorm_fwd: bad dtype");
+    if (rows <= 0 || channels <= 0) return fail(VH_E_SHAPE, "vh_layernorm_fwd: empty input");
+    if (rows > ((int64_t)1 << 40)) return fail(VH_E_RANGE, "vh_layernorm_fwd: too many rows");
+    const bool vec_ok = aligned(x, x_dtype == VH_F32 ? 16 : 8) && aligned(y, 16);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (x_dtype) {
+        case VH_F32: return ln_run<float>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+        case VH_BF16: return ln_run<__nv_bfloat16>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+        default: return ln_run<__half>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+    }
+}

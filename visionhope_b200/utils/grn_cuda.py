@@ -1,0 +1,62 @@
+"""GRN on channels-last CUDA tensors with fp32 output (mirror of utils/grn_cuda.py).
+
+``visionhope_grn`` calls ``vh_grn_fwd`` (replaces utils/csrc/grn_cuda.cu:267-300).  The
+statistics workspace comes from PyTorch's caching allocator.  Forward only.
+"""
+import torch
+
+from .. import _lib
+from .cuda import on_tensor_device
+
+
+@on_tensor_device
+def grn_forward(x, gamma, beta, eps, *, want_stats=False):
+    """x logical [B, C, H, W] stored channels-last -> fp32 channels-last y (and Gx, 1/den)."""
+    _lib.ensure_device(x)
+    if x.dim() != 4 or not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError("GRN CUDA expects channels-last NCHW input")
+    B, C, H, W = x.shape
+    g = gamma.detach().reshape(-1).contiguous().float()
+    b = beta.detach().reshape(-1).contiguous().float()
+    if g.numel() != C or b.numel() != C:
+        raise RuntimeError("GRN CUDA requires contiguous FP32 channel parameters on the input device")
+    y = torch.empty_like(x, dtype=torch.float32, memory_format=torch.channels_last)
+    gx = torch.empty((B, C), device=x.device, dtype=torch.float32) if want_stats else None
+    inv = torch.empty((B,), device=x.device, dtype=torch.float32) if want_stats else None
+    nbytes = int(_lib.load().vh_grn_workspace_bytes(B, H, W, C))
+    ws = torch.empty((max(nbytes, 16) + 3) // 4, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().vh_grn_fwd(
+        x.data_ptr(), _lib.dtype_code(x.dtype), g.data_ptr(), b.data_ptr(), float(eps), y.data_ptr(),
+        _lib.ptr(gx), _lib.ptr(inv), ws.data_ptr(), ws.numel() * 4, B, H, W, C,
+        _lib.stream_handle(x.device)), "vh_grn_fwd")
+    return (y, gx, inv) if want_stats else y
+
+
+class _GRNForwardOnly(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, gamma, beta, eps):
+        return grn_forward(x, gamma, beta, eps)
+
+    @staticmethod
+    def backward(ctx, grad):
+        raise NotImplementedError("GRN backward is not implemented by visionhope_b200")
+
+
+def can_fuse_grn(x, gamma, beta):
+    if x.ndim != 4 or not x.is_cuda or not x.is_contiguous(memory_format=torch.channels_last):
+        return False
+    if x.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        return False
+    channels = x.shape[1]
+    spatial = x.shape[2] * x.shape[3]
+    if x.shape[0] < 1 or x.shape[0] > 65535 or channels < 1 or spatial < 1 or channels % 4:
+        return False
+    return (gamma.device == x.device and beta.device == x.device
+            and gamma.dtype == torch.float32 and beta.dtype == torch.float32
+            and gamma.numel() == channels and beta.numel() == channels)
+
+
+def visionhope_grn(x, gamma, beta, eps):
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (x, gamma, beta)):
+        return _GRNForwardOnly.apply(x, gamma, beta, eps)
+    return grn_forward(x, gamma, beta, eps)

@@ -1,0 +1,68 @@
+"""Channels-last LayerNorm over C with fp32 output (mirror of utils/layer_norm_cuda.py).
+
+The reference's Triton kernel (layer_norm_cuda.py:31-57) is replaced by ``vh_layernorm_fwd``.
+Forward only.
+"""
+import torch
+
+from .. import _lib
+from .cuda import on_tensor_device
+
+
+@on_tensor_device
+def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False):
+    """x_rows [rows, C] (any float dtype, contiguous) -> fp32 [rows, C] (and mean, rstd)."""
+    _lib.ensure_device(x_rows)
+    x = x_rows.contiguous()
+    rows, C = x.shape
+    w = weight.detach().reshape(-1).contiguous().float()
+    b = bias.detach().reshape(-1).contiguous().float()
+    y = torch.empty((rows, C), device=x.device, dtype=torch.float32)
+    mean = torch.empty((rows,), device=x.device, dtype=torch.float32) if want_stats else None
+    rstd = torch.empty((rows,), device=x.device, dtype=torch.float32) if want_stats else None
+    _lib.check(_lib.load().vh_layernorm_fwd(
+        x.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), b.data_ptr(), float(eps), y.data_ptr(),
+        _lib.ptr(mean), _lib.ptr(rstd), rows, C, _lib.stream_handle(x.device)), "vh_layernorm_fwd")
+    return (y, mean, rstd) if want_stats else y
+
+
+@on_tensor_device
+def _layernorm2d_forward(x, weight, bias, eps):
+    batch, channels, height, width = x.shape
+    rows = x.permute(0, 2, 3, 1).reshape(batch * height * width, channels)
+    y = layernorm_rows(rows, weight, bias, eps)
+    return y.view(batch, height, width, channels).permute(0, 3, 1, 2)
+
+
+class _LayerNorm2dForwardOnly(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        return _layernorm2d_forward(x, weight, bias, eps)
+
+    @staticmethod
+    def backward(ctx, grad):
+        raise NotImplementedError("LayerNorm2d backward is not implemented by visionhope_b200")
+
+
+def can_fuse_layernorm2d(x, weight, bias):
+    if x.ndim != 4 or not x.is_cuda:
+        return False
+    if not x.is_contiguous(memory_format=torch.channels_last):
+        return False
+    if x.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        return False
+    channels = x.shape[1]
+    if channels < 1 or weight is None or bias is None:
+        return False
+    return (weight.device == x.device and bias.device == x.device
+            and weight.is_floating_point() and bias.is_floating_point()
+            and weight.numel() == channels and bias.numel() == channels)
+
+
+def visionhope_layernorm2d(x, weight, bias, eps):
+    """fp32 LayerNorm over C of a channels-last [B, C, H, W] tensor; returns channels-last."""
+    if not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError("visionhope_layernorm2d expects channels-last input")
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (x, weight, bias)):
+        return _LayerNorm2dForwardOnly.apply(x, weight, bias, float(eps))
+    return _layernorm2d_forward(x, weight, bias, float(eps))
