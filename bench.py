@@ -27,7 +27,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 
@@ -52,6 +51,8 @@ def parse():
     ap.add_argument("--model", default="visionhope_tiny")
     ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU baseline step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-scan", action="store_true",
+                    help="time only the fused SRNL operator at the stage-1 shape (profiling aid)")
     return ap.parse_args()
 
 
@@ -123,6 +124,29 @@ def build_model(name, device):
     model = model.to(memory_format=torch.channels_last)
     prepare_for_inference(model)
     return model
+
+
+def sync_model(model, world):
+    """Make every rank's weights identical to rank 0's (one broadcast per tensor at init)."""
+    if world > 1:
+        for p in model.parameters():
+            dist.broadcast(p.data, 0)
+        for buf in model.buffers():
+            dist.broadcast(buf, 0)
+
+
+def rank_inputs(batch, rank, device, generator_device=None):
+    """This rank's shard of the synthetic batch: N(0,1) images from seed 3 + rank."""
+    gen = torch.Generator(device=generator_device or device).manual_seed(3 + rank)
+    x = torch.randn(batch, 3, IMG, IMG, device=generator_device or device, generator=gen)
+    return x.to(device).contiguous(memory_format=torch.channels_last)
+
+
+def max_over_ranks(value, device, world):
+    t = torch.tensor([float(value)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def cpu_threads():
@@ -294,14 +318,8 @@ def run_ours(args, world, rank, local):
     from visionhope_b200 import _lib
 
     model = build_model(args.model, device)
-    if world > 1:
-        for p in model.parameters():
-            dist.broadcast(p.data, 0)
-        for bname, buf in model.named_buffers():
-            dist.broadcast(buf, 0)
-    gen = torch.Generator(device=device).manual_seed(3 + rank)
-    static_in = torch.randn(args.batch, 3, IMG, IMG, device=device, generator=gen).contiguous(
-        memory_format=torch.channels_last)
+    sync_model(model, world)
+    static_in = rank_inputs(args.batch, rank, device)
 
     def fwd():
         with torch.autocast("cuda", dtype=torch.bfloat16):
@@ -343,10 +361,7 @@ def run_ours(args, world, rank, local):
             dist.barrier()
         torch.cuda.synchronize()
         ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-        t = torch.tensor([ms], device=device)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+        ms_max = max_over_ranks(ms, device, world)
         clocks = clk.summary(set(range(torch.cuda.device_count())) if world > 1 else {device.index})
 
         # ---- end to end: pinned host batch in, logits out, inside every timed step ----
@@ -374,11 +389,7 @@ def run_ours(args, world, rank, local):
             e2e_step()
             b.record()
         torch.cuda.synchronize()
-        e2e_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-        t = torch.tensor([e2e_ms], device=device)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / args.steps, device, world)
         if not torch.isfinite(host_out).all():
             raise RuntimeError("non-finite logits")
 
@@ -428,6 +439,11 @@ def main():
                                      "sample": sample},
                     "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
+            return
+        if args.only_scan:
+            if rank == 0:
+                torch.cuda.set_device(local)
+                print(json.dumps(roofline_scan(args, torch.device("cuda", local), args.steps)), flush=True)
             return
         result = run_ours(args, world, rank, local)
         if rank == 0:

@@ -32,10 +32,21 @@ def cuda():
     return torch.device("cuda:0")
 
 
+def _np(a):
+    try:
+        import torch
+
+        if isinstance(a, torch.Tensor):
+            return a.detach().float().cpu().numpy()
+    except ImportError:  # pragma: no cover
+        pass
+    return a
+
+
 def rel_err(actual, expected) -> float:
     """Normwise relative error max|a - e| / max|e| (0 when both are zero)."""
-    a = np.asarray(actual, dtype=np.float64)
-    e = np.asarray(expected, dtype=np.float64)
+    a = np.asarray(_np(actual), dtype=np.float64)
+    e = np.asarray(_np(expected), dtype=np.float64)
     scale = float(np.max(np.abs(e))) if e.size else 0.0
     diff = float(np.max(np.abs(a - e))) if e.size else 0.0
     return diff / scale if scale > 0 else diff

@@ -28,7 +28,7 @@ inline ScanPlan plan_scan(int D, int max_chunk, bool spatial) {
 
 template <int D, typename XT, typename QT, int KIND>
 size_t scan_smem(const ScanPlan& pl) {
-    return ScanSmem<D, XT, QT>(pl.nch, pl.tile, KIND != kKindSeq).total;
+    return ScanSmem<D>(pl.nch, pl.tile).total;
 }
 
 // Halve the token tile (raising chains per CTA only within the thread budget) until the
@@ -51,6 +51,8 @@ template <int D, typename XT, typename QT, int KIND>
 int launch_scan(ScanParams p, const ScanPlan& pl, dim3 grid, cudaStream_t st) {
     p.nch = pl.nch;
     p.tile = pl.tile;
+    p.log2tile = 0;
+    while ((1 << p.log2tile) < pl.tile) ++p.log2tile;
     p.kind = KIND;
     const size_t smem = scan_smem<D, XT, QT, KIND>(pl);
     const void* fn = reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND>);
