@@ -171,6 +171,20 @@ int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* 
                float* y, float* gx, float* inv_den, void* workspace, int64_t workspace_bytes,
                int32_t batch, int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
 
+/* GRN that allocates nothing (no counterpart in the reference).  Same result as vh_grn_fwd,
+ * for callers that cannot allocate device memory when they run -- plugin or serving hosts
+ * whose op interface provides only input and output buffers, and deployments that fix their
+ * device memory at start-up.  The partial sums live in a 4 MiB array built into the library
+ * (held on every device that loads it until the process exits), so batch * channels must not
+ * exceed 1,048,576; larger calls are rejected with VH_E_RANGE.  The first call on each device
+ * looks up that array's device address once (make that first call before any stream capture).
+ * All calls share the one array: calls that may overlap on the GPU (different streams, or
+ * different host threads on one device) race and must be serialized by the caller; the array
+ * keeps the last call's contents, which no call relies on. */
+int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma, const float* beta,
+                       float eps, float* y, float* gx, float* inv_den, int32_t batch,
+                       int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * LayerNorm over the channel axis of channels-last rows, fp32 output; replaces the Triton
  * kernel utils/layer_norm_cuda.py:31-57, 122-147 `visionhope_layernorm2d` and the

@@ -1,6 +1,7 @@
 // GRN and channel LayerNorm kernels on channels-last rows, fp32 output, with C entry points.
 // Both are HBM-bound: every load/store is a 4-channel vector and grids cover all SMs.
 #include <algorithm>
+#include <mutex>
 
 #include "abi_util.h"
 #include "common.cuh"
@@ -318,5 +319,102 @@ extern "C" int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* wei
         case VH_F32: return ln_run<float>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
         case VH_BF16: return ln_run<__nv_bfloat16>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
         default: return ln_run<__half>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+    }
+}
+
+// =========================== GRN without any device allocation ===========================
+// Some callers cannot allocate device memory at the time they run GRN: inference servers and
+// plugin hosts whose custom-op interface hands an op only its input and output buffers (no
+// allocator, no workspace), and deployments that fix their device memory budget at start-up
+// and forbid allocation afterwards (an allocation can fail, fragment the pool or, for
+// cudaFree, synchronize the whole device).  vh_grn_fwd_noalloc serves them: it runs the same
+// two GRN passes as vh_grn_fwd, but keeps the per-slice partial sums in a fixed array that is
+// part of the library image on every device that loads it, so it allocates nothing.
+namespace vh {
+namespace {
+
+// Partial sums [batch, splits, channels] fp32; 4 MiB per device, held until process exit.
+constexpr int64_t kGrnNoAllocScratchFloats = int64_t(1) << 20;
+static __device__ __align__(256) float g_grn_noalloc_scratch[kGrnNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};  // device address of the array, per device ordinal
+
+// Device address of the scratch array on the current device (looked up once per device;
+// in host code the array's name is only a host-side stand-in, never a device address).
+int noalloc_scratch(float** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(VH_E_DEVICE, "vh_grn_fwd_noalloc: no usable current device");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_grn_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(VH_E_DEVICE, "vh_grn_fwd_noalloc: cudaGetSymbolAddress failed: %s",
+                        cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+
+}  // namespace
+}  // namespace vh
+
+extern "C" int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma,
+                                  const float* beta, float eps, float* y, float* gx, float* inv_den,
+                                  int32_t batch, int32_t height, int32_t width, int32_t channels,
+                                  vh_stream_t stream) {
+    clear_error();
+    if (!x || !gamma || !beta || !y) return fail(VH_E_ARG, "vh_grn_fwd_noalloc: null pointer argument");
+    if (!dtype_ok(x_dtype)) return fail(VH_E_DTYPE, "GRN supports FP32, FP16 and BF16 input");
+    if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0)
+        return fail(VH_E_SHAPE, "GRN expects nonempty input");
+    if (channels % 4) return fail(VH_E_SHAPE, "vh_grn_fwd_noalloc: channels must be a multiple of 4");
+    if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_fwd_noalloc: batch must be <= 65535");
+    if ((int64_t)batch * channels > kGrnNoAllocScratchFloats)
+        return fail(VH_E_RANGE,
+                    "vh_grn_fwd_noalloc: batch * channels = %lld exceeds the built-in scratch of %lld "
+                    "values; use vh_grn_fwd with a caller-provided workspace",
+                    (long long)batch * channels, (long long)kGrnNoAllocScratchFloats);
+    if ((size_t)channels * 4 + 128 > 200 * 1024) return fail(VH_E_RANGE, "vh_grn_fwd_noalloc: too many channels");
+    if (!aligned(x, x_dtype == VH_F32 ? 16 : 8) || !aligned(y, 16))
+        return fail(VH_E_ALIGN, "vh_grn_fwd_noalloc: misaligned pointers");
+    float* part = nullptr;
+    const int rc = noalloc_scratch(&part);
+    if (rc) return rc;
+    const int64_t S = (int64_t)height * width;
+    // Same two passes as vh_grn_fwd; the slice count shrinks when needed so that
+    // batch * splits * channels partial sums fit the fixed array.
+    int splits = grn_splits(batch, S);
+    const int64_t fit = kGrnNoAllocScratchFloats / ((int64_t)batch * channels);
+    if (splits > fit) splits = (int)fit;
+    const int G = channels / 4;
+    const int Geff = std::min(G, kGrnThreads);
+    const int rph = kGrnThreads / Geff;
+    const size_t red_bytes = sizeof(float) * (size_t)rph * Geff * 4;
+    const size_t fac_bytes = sizeof(float) * ((size_t)channels + 32);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    dim3 grid(splits, batch);
+    auto run = [&](auto tag) -> int {
+        using T = decltype(tag);
+        const T* xp = static_cast<const T*>(x);
+        if (!ensure_smem_attr(reinterpret_cast<const void*>(&grn_stats_kernel<T>), red_bytes) ||
+            !ensure_smem_attr(reinterpret_cast<const void*>(&grn_apply_kernel<T>), fac_bytes))
+            return fail(VH_E_DEVICE, "vh_grn_fwd_noalloc: shared memory");
+        // Every partial sum is written (not accumulated) by the stats pass, so the array needs
+        // no clearing between calls.
+        grn_stats_kernel<T><<<grid, kGrnThreads, red_bytes, st>>>(xp, part, channels, S, splits);
+        int r = launch_status("grn stats (no-alloc)");
+        if (r) return r;
+        grn_apply_kernel<T><<<grid, kGrnThreads, fac_bytes, st>>>(xp, part, gamma, beta, eps, y, gx,
+                                                                   inv_den, channels, S, splits);
+        return launch_status("grn apply (no-alloc)");
+    };
+    switch (x_dtype) {
+        case VH_F32: return run(float{});
+        case VH_BF16: return run(__nv_bfloat16{});
+        default: return run(__half{});
     }
 }
