@@ -162,13 +162,15 @@ int vh_dirfuse_fwd(const void* y, const void* x, int32_t io_dtype, const float* 
  * grn_cuda.cu:46-124, 267-300 `grn_forward_cuda` (utils/grn_cuda.py:103-117, utils/grn.py:41-70):
  *   x physical [B, H, W, C] (f32/bf16/f16), gamma/beta fp32 [C], y fp32 [B, H, W, C];
  *   y = x * (1 + gamma * Gx / (mean_c Gx + eps)) + beta, Gx[b,c] = ||x[b,:,:,c]||_2.
+ *   y_dtype: VH_F32 (the reference's output) or VH_BF16/VH_F16, the same fp32 result rounded
+ *   once -- what an autocast consumer would cast it to.
  *   gx (fp32 [B, C]) and inv_den (fp32 [B]) receive the statistics (the reference saves them
  *   for backward); both may be NULL.
  *   workspace: caller-provided device scratch of vh_grn_workspace_bytes(...) bytes.
  * -------------------------------------------------------------------------------------*/
 int64_t vh_grn_workspace_bytes(int32_t batch, int32_t height, int32_t width, int32_t channels);
 int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* beta, float eps,
-               float* y, float* gx, float* inv_den, void* workspace, int64_t workspace_bytes,
+               void* y, int32_t y_dtype, float* gx, float* inv_den, void* workspace, int64_t workspace_bytes,
                int32_t batch, int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
 
 /* GRN that allocates nothing (no counterpart in the reference).  Same result as vh_grn_fwd,
@@ -189,12 +191,13 @@ int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma, const
  * LayerNorm over the channel axis of channels-last rows, fp32 output; replaces the Triton
  * kernel utils/layer_norm_cuda.py:31-57, 122-147 `visionhope_layernorm2d` and the
  * F.layer_norm path of models/layers.py:17-35:
- *   x [rows, C] (f32/bf16/f16), weight/bias fp32 [C], y fp32 [rows, C];
- *   mean/rstd fp32 [rows] (may be NULL).
+ *   x [rows, C] (f32/bf16/f16), weight/bias fp32 [C], y [rows, C] of y_dtype (VH_F32 is the
+ *   reference's output; VH_BF16/VH_F16 round the fp32 result once); mean/rstd fp32 [rows]
+ *   (may be NULL).
  * -------------------------------------------------------------------------------------*/
 int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight, const float* bias,
-                     float eps, float* y, float* mean, float* rstd, int64_t rows, int32_t channels,
-                     vh_stream_t stream);
+                     float eps, void* y, int32_t y_dtype, float* mean, float* rstd, int64_t rows,
+                     int32_t channels, vh_stream_t stream);
 
 /* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
  * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it

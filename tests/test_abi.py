@@ -56,7 +56,7 @@ def test_null_arguments_are_rejected_without_a_gpu():
     assert lib.vh_srnl_sequence_fwd(ctypes.byref(seq), None) == -1
     assert lib.vh_qnorm_fwd(None, 1, None, None, 1, 4, 1, 1, 16, None) == -1
     assert lib.vh_dirfuse_fwd(None, None, 1, None, 0, None, None, 0, 1, 1, 1, 1, 16, None) == -1
-    assert lib.vh_layernorm_fwd(None, 0, None, None, 1e-6, None, None, None, 1, 4, None) == -1
+    assert lib.vh_layernorm_fwd(None, 0, None, None, 1e-6, None, 0, None, None, 1, 4, None) == -1
 
 
 def _fake(n=1 << 12):

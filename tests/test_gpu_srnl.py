@@ -41,6 +41,10 @@ SPATIAL_CASES = [
     (1, 6, 5, 2, 32, "bf16", "stress", False),
     (1, 4, 5, 1, 64, "f32", "stress", False),
     (5, 14, 14, 3, 16, "bf16", "stress", False),  # odd pair count per CTA
+    (1, 56, 56, 2, 16, "bf16", "stress", False),  # VisionHOPE-T stage 1 (tensor-core P1, 64-token tiles)
+    (2, 28, 28, 4, 16, "bf16", "clamp", True),    # stage 2 (32-token tiles)
+    (1, 33, 17, 2, 16, "bf16", "stress", False),  # odd sizes: coincident middle row and column
+    (1, 7, 7, 3, 16, "bf16", "stress", False),    # stage 4 (CUDA-core P1)
 ]
 
 
@@ -98,6 +102,8 @@ SEQ_CASES = [
     (1, 1, 2, 33, 32, [16], "f32", "norm", "stress"),
     (1, 4, 1, 12, 64, [4, 4, 3, 3], "bf16", "norm", "stress"),
     (2, 2, 2, 17, 4, [5, 3], "f32", "raw", "stress"),
+    (2, 4, 2, 196, 16, [14, 14, 14, 14], "bf16", "raw", "stress"),   # tensor-core P1, 16-token tiles
+    (1, 2, 1, 300, 16, [100, 33], "bf16", "raw", "clamp"),          # multi-tile chunks + padding
 ]
 
 

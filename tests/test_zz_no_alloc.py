@@ -38,7 +38,7 @@ def _with_workspace(L, lib, x, gamma, beta, stream):
     nbytes = lib.vh_grn_workspace_bytes(B, H, W, C)
     ws = torch.empty((nbytes + 3) // 4, device=x.device)
     rc = lib.vh_grn_fwd(x.data_ptr(), L.dtype_code(x.dtype), gamma.data_ptr(), beta.data_ptr(), 1e-6,
-                        y.data_ptr(), gx.data_ptr(), inv.data_ptr(), ws.data_ptr(), ws.numel() * 4,
+                        y.data_ptr(), 0, gx.data_ptr(), inv.data_ptr(), ws.data_ptr(), ws.numel() * 4,
                         B, H, W, C, stream)
     assert rc == 0, lib.vh_last_error()
     return y, gx, inv

@@ -84,10 +84,10 @@ def load() -> ctypes.CDLL:
                                            c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
                                            c_int32, c_void_p]
             lib.vh_grn_fwd.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_float, c_void_p,
-                                       c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
-                                       c_int32, c_int32, c_void_p]
+                                       c_int32, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                                       c_int32, c_int32, c_int32, c_void_p]
             lib.vh_layernorm_fwd.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_float,
-                                             c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                                             c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                                              c_void_p]
             lib.vh_init.argtypes = [c_int32]
             lib.vh_probe_ffma.restype = c_int32

@@ -19,7 +19,13 @@ from torch.nn import functional as F
 from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
+from .utils.grn_cuda import grn_forward
 from .utils.layer_norm_cuda import layernorm_rows
+
+
+def _autocast_dtype():
+    """The CUDA autocast dtype when autocast is on, else None."""
+    return torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else None
 
 MODEL_CONFIGS = {
     "visionhope_tiny": dict(embed_dims=(64, 128, 256, 512), mixer_dims=(32, 64, 128, 256),
@@ -44,13 +50,20 @@ class LayerNorm2d(nn.Module):
         self.bias = nn.Parameter(torch.zeros(dim))
         self.eps = eps
         self.inference_layout = False
+        # Set when the only consumer is a convolution that autocast runs in lower precision:
+        # the kernel then writes that dtype directly (the fp32 result rounded once, exactly
+        # the cast autocast would apply), saving a separate cast pass.
+        self.emit_autocast_dtype = False
 
     def forward(self, x):
         b, c, h, w = x.shape
         rows = x.permute(0, 2, 3, 1)
         if not rows.is_contiguous():
             rows = rows.contiguous()
-        y = layernorm_rows(rows.reshape(b * h * w, c), self.weight, self.bias, self.eps)
+        out_dtype = torch.float32
+        if self.emit_autocast_dtype and _autocast_dtype() in (torch.bfloat16, torch.float16):
+            out_dtype = _autocast_dtype()
+        y = layernorm_rows(rows.reshape(b * h * w, c), self.weight, self.bias, self.eps, out_dtype=out_dtype)
         return y.view(b, h, w, c).permute(0, 3, 1, 2)
 
 
@@ -84,8 +97,15 @@ class FeedForwardNetwork(nn.Module):
         x = self.act(self.fc1(x))
         if self.use_dwconv:
             x = self.dwconv_act(x + self.dwconv(x))
-        x = self.drop(self.grn(x))
-        return self.drop(self.fc2(x))
+        ac = _autocast_dtype()
+        if isinstance(self.grn, GlobalResponseNorm) and ac in (torch.bfloat16, torch.float16) and x.is_cuda:
+            # fc2 runs under autocast and casts GRN's fp32 output to `ac`; emit it directly.
+            if not x.is_contiguous(memory_format=torch.channels_last):
+                x = x.contiguous(memory_format=torch.channels_last)
+            x = grn_forward(x, self.grn.gamma, self.grn.beta, self.grn.eps, out_dtype=ac)
+        else:
+            x = self.grn(x)
+        return self.drop(self.fc2(self.drop(x)))
 
 
 class PatchEmbedding(nn.Module):
@@ -182,7 +202,10 @@ class VisionHOPEBlock(nn.Module):
                 if self.local_position is not None:
                     out = out + self.local_position(x_local).permute(0, 2, 3, 1)
                 out = self.proj_out(out)
-                return out.permute(0, 3, 1, 2).contiguous()
+                # NHWC storage viewed as NCHW (channels-last); the reference copies it to
+                # contiguous NCHW here, which only costs a layout pass before the residual add.
+                out = out.permute(0, 3, 1, 2)
+                return out if channels_last else out.contiguous()
         out = self.operator(x_local, channels_last=channels_last)
         if self.local_position is not None:
             out = out + self.local_position(x_local)
@@ -300,6 +323,12 @@ def prepare_for_inference(model):
             counts["layernorm2d"] += 1
         elif isinstance(m, GlobalResponseNorm):
             counts["grn"] += 1
+    for block in blocks:
+        for norm in (block.norm1, block.norm2):
+            if isinstance(norm, LayerNorm2d):
+                norm.emit_autocast_dtype = True  # consumed only by proj_in / fc1
+    if isinstance(getattr(model, "norm", None), LayerNorm2d):
+        model.norm.emit_autocast_dtype = True  # consumed only by head_pre_logits
     with torch.no_grad():
         for block in blocks:
             counts["line_mixer"] += 1

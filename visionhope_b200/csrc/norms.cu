@@ -61,10 +61,10 @@ __global__ void __launch_bounds__(kGrnThreads) grn_stats_kernel(const T* __restr
     }
 }
 
-template <typename T>
+template <typename T, typename YT = float>
 __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
     const T* __restrict__ x, const float* __restrict__ part, const float* __restrict__ gamma,
-    const float* __restrict__ beta, float eps, float* __restrict__ y, float* __restrict__ gx_out,
+    const float* __restrict__ beta, float eps, YT* __restrict__ y, float* __restrict__ gx_out,
     float* __restrict__ inv_out, int C, int64_t S, int splits) {
     extern __shared__ float fac[];  // [C] factors, then [32] reduction scratch
     float* scratch = fac + C;
@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
     const int64_t s0 = S * split / splits, s1 = S * (split + 1) / splits;
     const int64_t n = (s1 - s0) * G;
     const T* xb = x + ((int64_t)b * S + s0) * C;
-    float* yb = y + ((int64_t)b * S + s0) * C;
+    YT* yb = y + ((int64_t)b * S + s0) * C;
     for (int64_t it = threadIdx.x; it < n; it += blockDim.x) {
         const int64_t s = it / G;
         const int c = (int)(it % G) * 4;
@@ -118,11 +118,11 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
 // mean and biased variance by two in-register passes (the Triton kernel's order).
 constexpr int kLnThreads = 256;
 
-template <typename T, int SW, int NV>
+template <typename T, typename YT, int SW, int NV>
 __global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
                                                         const float* __restrict__ w,
                                                         const float* __restrict__ bias, float eps,
-                                                        float* __restrict__ y, float* __restrict__ mean_out,
+                                                        YT* __restrict__ y, float* __restrict__ mean_out,
                                                         float* __restrict__ rstd_out, int64_t rows, int C) {
     const int lane = threadIdx.x % SW;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / SW;
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
     for (int o = SW / 2; o > 0; o >>= 1) q += __shfl_xor_sync(mask, q, o, SW);
     const float rstd = 1.f / sqrtf(q / (float)C + eps);
     if (!live) return;
-    float* yr = y + row * C;
+    YT* yr = y + row * C;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
         const int g = lane + k * SW;
@@ -179,11 +179,11 @@ __global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
 }
 
 // Any C: one warp per row, scalar accesses, two passes over global memory.
-template <typename T>
+template <typename T, typename YT>
 __global__ void __launch_bounds__(kLnThreads) ln_generic_kernel(const T* __restrict__ x,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, float eps,
-                                                                float* __restrict__ y,
+                                                                YT* __restrict__ y,
                                                                 float* __restrict__ mean_out,
                                                                 float* __restrict__ rstd_out,
                                                                 int64_t rows, int C) {
@@ -202,16 +202,16 @@ __global__ void __launch_bounds__(kLnThreads) ln_generic_kernel(const T* __restr
     }
     q = warp_sum(q);
     const float rstd = 1.f / sqrtf(q / (float)C + eps);
-    float* yr = y + row * C;
-    for (int c = lane; c < C; c += 32) yr[c] = (to_f(xr[c]) - mean) * rstd * w[c] + bias[c];
+    YT* yr = y + row * C;
+    for (int c = lane; c < C; c += 32) yr[c] = from_f<YT>((to_f(xr[c]) - mean) * rstd * w[c] + bias[c]);
     if (lane == 0) {
         if (mean_out) mean_out[row] = mean;
         if (rstd_out) rstd_out[row] = rstd;
     }
 }
 
-template <typename T>
-int grn_run(const void* xv, const float* gamma, const float* beta, float eps, float* y, float* gx,
+template <typename T, typename YT>
+int grn_run(const void* xv, const float* gamma, const float* beta, float eps, YT* y, float* gx,
             float* inv, float* part, int B, int64_t S, int C, cudaStream_t st) {
     const T* x = static_cast<const T*>(xv);
     const int splits = grn_splits(B, S);
@@ -226,40 +226,60 @@ int grn_run(const void* xv, const float* gamma, const float* beta, float eps, fl
     int rc = launch_status("grn stats");
     if (rc) return rc;
     const size_t fac_bytes = sizeof(float) * ((size_t)C + 32);
-    if (!ensure_smem_attr(reinterpret_cast<const void*>(&grn_apply_kernel<T>), fac_bytes))
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(&grn_apply_kernel<T, YT>), fac_bytes))
         return fail(VH_E_DEVICE, "grn: shared memory");
-    grn_apply_kernel<T><<<grid, kGrnThreads, fac_bytes, st>>>(x, part, gamma, beta, eps, y, gx, inv, C,
-                                                               S, splits);
+    grn_apply_kernel<T, YT><<<grid, kGrnThreads, fac_bytes, st>>>(x, part, gamma, beta, eps, y, gx, inv, C,
+                                                                   S, splits);
     return launch_status("grn apply");
 }
 
-template <typename T, int SW, int NV>
-int ln_launch(const void* x, const float* w, const float* b, float eps, float* y, float* m, float* r,
+template <typename T>
+int grn_run_y(int y_dtype, const void* xv, const float* gamma, const float* beta, float eps, void* y,
+              float* gx, float* inv, float* part, int B, int64_t S, int C, cudaStream_t st) {
+    switch (y_dtype) {
+        case VH_F32: return grn_run<T, float>(xv, gamma, beta, eps, static_cast<float*>(y), gx, inv, part, B, S, C, st);
+        case VH_BF16: return grn_run<T, __nv_bfloat16>(xv, gamma, beta, eps, static_cast<__nv_bfloat16*>(y), gx, inv, part, B, S, C, st);
+        default: return grn_run<T, __half>(xv, gamma, beta, eps, static_cast<__half*>(y), gx, inv, part, B, S, C, st);
+    }
+}
+
+template <typename T, typename YT, int SW, int NV>
+int ln_launch(const void* x, const float* w, const float* b, float eps, YT* y, float* m, float* r,
               int64_t rows, int C, cudaStream_t st) {
     const int64_t rows_per_cta = kLnThreads / SW;
     const int64_t blocks = (rows + rows_per_cta - 1) / rows_per_cta;
-    ln_kernel<T, SW, NV><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
-                                                                  m, r, rows, C);
+    ln_kernel<T, YT, SW, NV><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
+                                                                      m, r, rows, C);
+    return launch_status("layernorm");
+}
+
+template <typename T, typename YT>
+int ln_run(const void* x, const float* w, const float* b, float eps, YT* y, float* m, float* r,
+           int64_t rows, int C, bool vec_ok, cudaStream_t st) {
+    const int G = C / 4;
+    if (vec_ok && C % 4 == 0) {
+        if (G <= 8) return ln_launch<T, YT, 8, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 16) return ln_launch<T, YT, 16, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 32) return ln_launch<T, YT, 32, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 64) return ln_launch<T, YT, 32, 2>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 128) return ln_launch<T, YT, 32, 4>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 256) return ln_launch<T, YT, 32, 8>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G <= 512) return ln_launch<T, YT, 32, 16>(x, w, b, eps, y, m, r, rows, C, st);
+    }
+    const int64_t blocks = (rows * 32 + kLnThreads - 1) / kLnThreads;
+    ln_generic_kernel<T, YT><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
+                                                                      m, r, rows, C);
     return launch_status("layernorm");
 }
 
 template <typename T>
-int ln_run(const void* x, const float* w, const float* b, float eps, float* y, float* m, float* r,
-           int64_t rows, int C, bool vec_ok, cudaStream_t st) {
-    const int G = C / 4;
-    if (vec_ok && C % 4 == 0) {
-        if (G <= 8) return ln_launch<T, 8, 1>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 16) return ln_launch<T, 16, 1>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 32) return ln_launch<T, 32, 1>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 64) return ln_launch<T, 32, 2>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 128) return ln_launch<T, 32, 4>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 256) return ln_launch<T, 32, 8>(x, w, b, eps, y, m, r, rows, C, st);
-        if (G <= 512) return ln_launch<T, 32, 16>(x, w, b, eps, y, m, r, rows, C, st);
+int ln_run_y(int y_dtype, const void* x, const float* w, const float* b, float eps, void* y, float* m,
+             float* r, int64_t rows, int C, bool vec_ok, cudaStream_t st) {
+    switch (y_dtype) {
+        case VH_F32: return ln_run<T, float>(x, w, b, eps, static_cast<float*>(y), m, r, rows, C, vec_ok, st);
+        case VH_BF16: return ln_run<T, __nv_bfloat16>(x, w, b, eps, static_cast<__nv_bfloat16*>(y), m, r, rows, C, vec_ok, st);
+        default: return ln_run<T, __half>(x, w, b, eps, static_cast<__half*>(y), m, r, rows, C, vec_ok, st);
     }
-    const int64_t blocks = (rows * 32 + kLnThreads - 1) / kLnThreads;
-    ln_generic_kernel<T><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps, y,
-                                                                  m, r, rows, C);
-    return launch_status("layernorm");
 }
 
 }  // namespace vh
@@ -278,17 +298,19 @@ extern "C" int64_t vh_grn_workspace_bytes(int32_t batch, int32_t height, int32_t
 }
 
 extern "C" int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* beta,
-                          float eps, float* y, float* gx, float* inv_den, void* workspace,
+                          float eps, void* y, int32_t y_dtype, float* gx, float* inv_den, void* workspace,
                           int64_t workspace_bytes, int32_t batch, int32_t height, int32_t width,
                           int32_t channels, vh_stream_t stream) {
     clear_error();
     if (!x || !gamma || !beta || !y || !workspace) return fail(VH_E_ARG, "vh_grn_fwd: null pointer argument");
     if (!dtype_ok(x_dtype)) return fail(VH_E_DTYPE, "GRN supports FP32, FP16 and BF16 input");
+    if (!dtype_ok(y_dtype)) return fail(VH_E_DTYPE, "vh_grn_fwd: bad output dtype");
     if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0)
         return fail(VH_E_SHAPE, "GRN expects nonempty input");
     if (channels % 4) return fail(VH_E_SHAPE, "vh_grn_fwd: channels must be a multiple of 4");
     if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_fwd: batch must be <= 65535");
-    if (!aligned(x, x_dtype == VH_F32 ? 16 : 8) || !aligned(y, 16) || !aligned(workspace, 16))
+    if (!aligned(x, x_dtype == VH_F32 ? 16 : 8) || !aligned(y, y_dtype == VH_F32 ? 16 : 8) ||
+        !aligned(workspace, 16))
         return fail(VH_E_ALIGN, "vh_grn_fwd: misaligned pointers");
     if (workspace_bytes < vh_grn_workspace_bytes(batch, height, width, channels))
         return fail(VH_E_ARG, "vh_grn_fwd: workspace too small (%lld < %lld bytes)",
@@ -299,26 +321,26 @@ extern "C" int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, co
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* part = static_cast<float*>(workspace);
     switch (x_dtype) {
-        case VH_F32: return grn_run<float>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
-        case VH_BF16: return grn_run<__nv_bfloat16>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
-        default: return grn_run<__half>(x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+        case VH_F32: return grn_run_y<float>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+        case VH_BF16: return grn_run_y<__nv_bfloat16>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+        default: return grn_run_y<__half>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
     }
 }
 
 extern "C" int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight,
-                                const float* bias, float eps, float* y, float* mean, float* rstd,
-                                int64_t rows, int32_t channels, vh_stream_t stream) {
+                                const float* bias, float eps, void* y, int32_t y_dtype, float* mean,
+                                float* rstd, int64_t rows, int32_t channels, vh_stream_t stream) {
     clear_error();
     if (!x || !weight || !bias || !y) return fail(VH_E_ARG, "vh_layernorm_fwd: null pointer argument");
-    if (!dtype_ok(x_dtype)) return fail(VH_E_DTYPE, "vh_layernorm_fwd: bad dtype");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(VH_E_DTYPE, "vh_layernorm_fwd: bad dtype");
     if (rows <= 0 || channels <= 0) return fail(VH_E_SHAPE, "vh_layernorm_fwd: empty input");
     if (rows > ((int64_t)1 << 40)) return fail(VH_E_RANGE, "vh_layernorm_fwd: too many rows");
-    const bool vec_ok = aligned(x, x_dtype == VH_F32 ? 16 : 8) && aligned(y, 16);
+    const bool vec_ok = aligned(x, x_dtype == VH_F32 ? 16 : 8) && aligned(y, y_dtype == VH_F32 ? 16 : 8);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (x_dtype) {
-        case VH_F32: return ln_run<float>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
-        case VH_BF16: return ln_run<__nv_bfloat16>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
-        default: return ln_run<__half>(x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+        case VH_F32: return ln_run_y<float>(y_dtype, x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+        case VH_BF16: return ln_run_y<__nv_bfloat16>(y_dtype, x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
+        default: return ln_run_y<__half>(y_dtype, x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
     }
 }
 

@@ -78,10 +78,14 @@ struct ScanGeom {
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
 // Shared-memory carve-up (identical on host and device).
+// Number of bf16 parts the tensor-core path splits each fp32 memory row into (hi + mid + lo
+// carry 24 mantissa bits, i.e. fp32-level projections from bf16 x/q operands).
+constexpr int kSplits = 3;
+
 template <int D>
 struct ScanSmem {
-    size_t S, G, K, Dv, EFF, ALP, WS, total;
-    __host__ __device__ ScanSmem(int nch, int tile) {
+    size_t S, G, K, Dv, EFF, ALP, WS, XS, QS, MB, total;
+    __host__ __device__ ScanSmem(int nch, int tile, bool mma = false) {
         using Gm = ScanGeom<D>;
         size_t off = 0;
         S = off;   off += align16(sizeof(float) * nch * Gm::SROWS * Gm::SP);
@@ -91,6 +95,10 @@ struct ScanSmem {
         EFF = off; off += align16(sizeof(float) * nch * tile);
         ALP = off; off += align16(sizeof(float) * nch * tile);
         WS = off;  off += align16(sizeof(float) * nch * 2 * D);
+        // tensor-core path: bf16 x/q tiles (32-byte rows) and split memories [nch][3][3D rows]
+        XS = off;  off += mma ? align16(2 * D * nch * tile) : 0;
+        QS = off;  off += mma ? align16(2 * D * nch * tile) : 0;
+        MB = off;  off += mma ? align16(2 * D * nch * kSplits * 3 * D) : 0;
         total = off;
     }
 };
@@ -157,14 +165,71 @@ struct RowReg {
 
 __device__ __forceinline__ float softplus_f(float p) { return p > 20.f ? p : log1pf(expf(p)); }
 
-template <int D, typename XT, typename QT, int KIND>
+// ---- tensor-core helpers (bf16 m16n8k16, fp32 accumulate) ------------------------------
+// Rows of 16 bf16 (32 bytes) are stored with their two 16-byte halves swapped on rows whose
+// bit 2 is set, so each 8-row ldmatrix phase touches 8 distinct bank groups.
+__device__ __forceinline__ int swz(int row, int half) { return row * 32 + ((half ^ ((row >> 2) & 1)) << 4); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const unsigned char* p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v;
+}
+
+// Writes the three bf16 parts of one 16-value fp32 memory row (row `r` of the stacked state)
+// into the split-memory block of a chain: part k = bf16(v - sum of earlier parts).
+__device__ __forceinline__ void write_splits16(unsigned char* mb_slot, int r, const float* v) {
+    float rem[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) rem[i] = v[i];
+#pragma unroll
+    for (int k = 0; k < kSplits; ++k) {
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(rem[2 * i], rem[2 * i + 1]);
+            const float2 hf = __bfloat1622float2(h);
+            rem[2 * i] -= hf.x;
+            rem[2 * i + 1] -= hf.y;
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        unsigned char* base = mb_slot + k * 48 * 32;
+        *reinterpret_cast<uint4*>(base + swz(r, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(base + swz(r, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// MMA selects the tensor-core token phase (D = 16, bf16 x and raw bf16 q, tile >= 16): the
+// projections k~ = M_k x, v = M_v x and M_m q_raw run as bf16 m16n8k16 MMAs against a three-way
+// bf16 split of the fp32 memories (fp32 accumulate), and y is scaled by 1/||q_raw|| afterwards.
+template <int D, typename XT, typename QT, int KIND, bool MMA = false>
 __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanParams p) {
     using Gm = ScanGeom<D>;
     constexpr int SROWS = Gm::SROWS, SP = Gm::SP;
     constexpr bool kSpatial = KIND != kKindSeq;
+    static_assert(!MMA || (D == 16 && std::is_same<XT, __nv_bfloat16>::value &&
+                           std::is_same<QT, __nv_bfloat16>::value),
+                  "the tensor-core token phase is specialised for D = 16 bf16 inputs");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int nch = p.nch, tile = p.tile, lt = p.log2tile;
-    const ScanSmem<D> lay(nch, tile);
+    const ScanSmem<D> lay(nch, tile, MMA);
     float* S = reinterpret_cast<float*>(smem_raw + lay.S);
     float* Gs = reinterpret_cast<float*>(smem_raw + lay.G);
     float* Kt = reinterpret_cast<float*>(smem_raw + lay.K);
@@ -172,6 +237,9 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
     float* EFF = reinterpret_cast<float*>(smem_raw + lay.EFF);
     float* ALP = reinterpret_cast<float*>(smem_raw + lay.ALP);
     float* WS = reinterpret_cast<float*>(smem_raw + lay.WS);
+    unsigned char* Xs = smem_raw + lay.XS;
+    unsigned char* Qs = smem_raw + lay.QS;
+    unsigned char* Mb = smem_raw + lay.MB;
     const int tid = threadIdx.x;
 
     // ---- initial memories -> stacked state; per-slot fusion weights ---------------------
@@ -199,6 +267,21 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
                 WS[(slot * 2 + 1) * D + i] =
                     ch.valid ? p.skip[(p.skip_per_dir ? ch.dir * p.C : 0) + chn] : 0.f;
             }
+        }
+    }
+
+    if constexpr (MMA) {
+        __syncthreads();  // the stacked state is complete
+        for (int task = tid; task < nch * 3 * D; task += blockDim.x) {
+            const int slot = task / (3 * D), r = task % (3 * D);
+            float v[16];
+            const float* rowp = S + ((size_t)slot * SROWS + r) * SP;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                const float4 f = *reinterpret_cast<const float4*>(rowp + i);
+                v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+            }
+            write_splits16(Mb + (size_t)slot * kSplits * 48 * 32, r, v);
         }
     }
 
@@ -249,6 +332,29 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
     const int p2_slot = tid / D, p2_row = tid % D;
     const bool p2_on = p2_slot < nch && chain_of(p, p2_slot).valid;
 
+    // ---- tensor-core role: warp w owns CTA rows 32w..32w+31 (two 16-row M-tiles) --------
+    const int lane = tid & 31, wrp = tid >> 5, qg = lane >> 2, qt4 = lane & 3;
+    int mt_slot[2];
+    bool mt_on[2];
+    Chain mt_ch[2];
+    float* mt_out[2] = {nullptr, nullptr};
+    XT* mt_y[2] = {nullptr, nullptr};
+    if constexpr (MMA) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            const int rbase = wrp * 32 + mt * 16;
+            mt_slot[mt] = rbase >> lt;
+            mt_ch[mt] = chain_of(p, mt_slot[mt] < nch ? mt_slot[mt] : 0);
+            mt_on[mt] = rbase < nch * tile && mt_ch[mt].valid;
+            if (kSpatial) {
+                mt_out[mt] = p.out + mt_ch[mt].b * p.ob + mt_ch[mt].head * D;
+            } else {
+                const int64_t chain = ((int64_t)mt_ch[mt].b * p.R + mt_ch[mt].dir) * p.heads + mt_ch[mt].head;
+                mt_y[mt] = static_cast<XT*>(p.y) + chain * p.L * D;
+            }
+        }
+    }
+
     RowReg<D, XT> xn;
     RowReg<D, QT> qn;
     auto prefetch = [&](int c, int j) {
@@ -279,7 +385,153 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
         bool deferred = false;
         float4 dv[D / 4];
         float* dptr = nullptr;
-        if (p1_on && p1_tok < count) {
+        unsigned mdef = 0;  // bit (2 mt + h): this thread defers a middle-row write
+        if constexpr (MMA) {
+            // Stage this thread's token row (raw bf16) for the warp's ldmatrix loads.
+            if (p1_slot < nch) {
+                *reinterpret_cast<uint4*>(Xs + swz(tid, 0)) = *reinterpret_cast<const uint4*>(&xc.v[0]);
+                *reinterpret_cast<uint4*>(Xs + swz(tid, 1)) = *reinterpret_cast<const uint4*>(&xc.v[1]);
+                *reinterpret_cast<uint4*>(Qs + swz(tid, 0)) = *reinterpret_cast<const uint4*>(&qc.v[0]);
+                *reinterpret_cast<uint4*>(Qs + swz(tid, 1)) = *reinterpret_cast<const uint4*>(&qc.v[1]);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                if (!mt_on[mt]) continue;  // warp-uniform
+                const int rbase = wrp * 32 + mt * 16, slot = mt_slot[mt];
+                uint32_t ax[4], aq[4];
+                ldsm_x4(ax, Xs + swz(rbase + (lane & 15), lane >> 4));
+                ldsm_x4(aq, Qs + swz(rbase + (lane & 15), lane >> 4));
+                float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {};
+                const unsigned char* mbs = Mb + (size_t)slot * kSplits * 48 * 32;
+                const int brow = (lane & 7) + ((lane >> 4) << 3), bhalf = (lane >> 3) & 1;
+#pragma unroll
+                for (int k = 0; k < kSplits; ++k) {
+                    const unsigned char* mb = mbs + k * 48 * 32;
+                    uint32_t bm[4], bv[4], bk[4];
+                    ldsm_x4(bm, mb + swz(brow, bhalf));            // M_m rows 0-15
+                    ldsm_x4(bv, mb + swz(16 + brow, bhalf));       // M_v rows 16-31
+                    ldsm_x4(bk, mb + swz(32 + brow, bhalf));       // M_k rows 32-47
+                    mma_16816(cy[0], aq, bm[0], bm[1]);
+                    mma_16816(cy[1], aq, bm[2], bm[3]);
+                    mma_16816(cv[0], ax, bv[0], bv[1]);
+                    mma_16816(cv[1], ax, bv[2], bv[3]);
+                    mma_16816(ck[0], ax, bk[0], bk[1]);
+                    mma_16816(ck[1], ax, bk[2], bk[3]);
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    // Thread (qg, qt4) holds channels {2t, 2t+1, 8+2t, 9+2t} of token row qg + 8h.
+                    const int row = rbase + qg + 8 * h;
+                    const int tok = row & (tile - 1);
+                    const int tin = (j << lt) + tok;
+                    const int64_t t = (int64_t)c * Lc + tin;
+                    // Raw k~ and v go to this row's staging slots; the token's own thread
+                    // finishes norms and gates below (in-thread, no shuffles).
+                    float* krow = Kt + (size_t)row * SP + 2 * qt4;
+                    float* drow = Dt + (size_t)row * SP + 2 * qt4;
+                    *reinterpret_cast<float2*>(krow) = make_float2(ck[0][2 * h], ck[0][2 * h + 1]);
+                    *reinterpret_cast<float2*>(krow + 8) = make_float2(ck[1][2 * h], ck[1][2 * h + 1]);
+                    *reinterpret_cast<float2*>(drow) = make_float2(cv[0][2 * h], cv[0][2 * h + 1]);
+                    *reinterpret_cast<float2*>(drow + 8) = make_float2(cv[1][2 * h], cv[1][2 * h + 1]);
+                    const float2 q01 = bf2_to_f2(aq[h]), q23 = bf2_to_f2(aq[2 + h]);
+                    float qs = q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y;
+                    qs = quad_sum(qs);
+                    if (tok >= count) continue;
+                    const float qinv = 1.f / fmaxf(sqrtf(qs), 1e-12f);
+                    const float yv[4] = {cy[0][2 * h] * qinv, cy[0][2 * h + 1] * qinv,
+                                         cy[1][2 * h] * qinv, cy[1][2 * h + 1] * qinv};
+                    if constexpr (kSpatial) {
+                        const float2 x01 = bf2_to_f2(ax[h]), x23 = bf2_to_f2(ax[2 + h]);
+                        const float* wv = WS + (slot * 2) * D;
+                        const float* sv = WS + (slot * 2 + 1) * D;
+                        const float2 w_lo = *reinterpret_cast<const float2*>(wv + 2 * qt4);
+                        const float2 w_hi = *reinterpret_cast<const float2*>(wv + 8 + 2 * qt4);
+                        const float2 s_lo = *reinterpret_cast<const float2*>(sv + 2 * qt4);
+                        const float2 s_hi = *reinterpret_cast<const float2*>(sv + 8 + 2 * qt4);
+                        const float2 o_lo = make_float2(w_lo.x * (yv[0] + s_lo.x * x01.x), w_lo.y * (yv[1] + s_lo.y * x01.y));
+                        const float2 o_hi = make_float2(w_hi.x * (yv[2] + s_hi.x * x23.x), w_hi.y * (yv[3] + s_hi.y * x23.y));
+                        const int dir = mt_ch[mt].dir;
+                        const int pc = nchunks - 1 - c, ptin = Lc - 1 - tin, pj = ptin >> lt;
+                        const bool coincident = pc == c && pj == j;
+                        const bool partner_later = pc > c || (pc == c && pj > j);
+                        float* op = mt_out[mt] + (int64_t)scan_pixel(dir, c, tin, p.H, p.W) * p.C + 2 * qt4;
+                        if (coincident && (dir & 1)) {
+                            // Park the value in this row's (already consumed) x/q staging
+                            // slots: 32 + 32 bytes hold the 16 fp32 outputs of the token.
+                            mdef |= 1u << (2 * mt + h);
+                            *reinterpret_cast<float2*>(Xs + row * 32 + 8 * qt4) = o_lo;
+                            *reinterpret_cast<float2*>(Qs + row * 32 + 8 * qt4) = o_hi;
+                        } else if (KIND == kKindRows && (coincident || partner_later)) {
+                            *reinterpret_cast<float2*>(op) = o_lo;
+                            *reinterpret_cast<float2*>(op + 8) = o_hi;
+                        } else {
+                            const float2 p_lo = *reinterpret_cast<const float2*>(op);
+                            const float2 p_hi = *reinterpret_cast<const float2*>(op + 8);
+                            *reinterpret_cast<float2*>(op) = make_float2(p_lo.x + o_lo.x, p_lo.y + o_lo.y);
+                            *reinterpret_cast<float2*>(op + 8) = make_float2(p_hi.x + o_hi.x, p_hi.y + o_hi.y);
+                        }
+                    } else {
+                        if (t < p.L) {
+                            XT* yo = mt_y[mt] + t * D + 2 * qt4;
+                            *reinterpret_cast<__nv_bfloat162*>(yo) = __floats2bfloat162_rn(yv[0], yv[1]);
+                            *reinterpret_cast<__nv_bfloat162*>(yo + 8) = __floats2bfloat162_rn(yv[2], yv[3]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // raw k~ / v rows of this warp's tokens are staged
+            if (p1_on && p1_tok < count) {
+                const float* Sc = S + (size_t)p1_slot * SROWS * SP;
+                float* krow = Kt + (size_t)tid * SP;
+                float* drow = Dt + (size_t)tid * SP;
+                float xv[D], kr[D], vv[D];
+                xc.to_float(xv);
+                float kn = 0.f;
+#pragma unroll
+                for (int i = 0; i < D; i += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(krow + i);
+                    const float4 v4 = *reinterpret_cast<const float4*>(drow + i);
+                    kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
+                    vv[i] = v4.x; vv[i + 1] = v4.y; vv[i + 2] = v4.z; vv[i + 3] = v4.w;
+                }
+#pragma unroll
+                for (int i = 0; i < D; ++i) kn = fmaf(kr[i], kr[i], kn);
+                const float kinv = 1.f / sqrtf(kn + 1e-6f);
+                float ke = 0.f, dn2 = 0.f, ep = 0.f, ap = 0.f;
+                const float* ev = Sc + 3 * D * SP;
+                const float* avp = Sc + (3 * D + 1) * SP;
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    const float kk = kr[i] * kinv;
+                    const float d = kk - vv[i];
+                    kr[i] = kk;
+                    vv[i] = d;
+                    ke = fmaf(kk, kk, ke);
+                    dn2 = fmaf(d, d, dn2);
+                    ep = fmaf(xv[i], ev[i], ep);
+                    ap = fmaf(xv[i], avp[i], ap);
+                }
+#pragma unroll
+                for (int i = 0; i < D; i += 4) {
+                    *reinterpret_cast<float4*>(krow + i) = make_float4(kr[i], kr[i + 1], kr[i + 2], kr[i + 3]);
+                    *reinterpret_cast<float4*>(drow + i) = make_float4(vv[i], vv[i + 1], vv[i + 2], vv[i + 3]);
+                }
+                ep = fminf(10.f, fmaxf(-10.f, ep));
+                ap = fminf(10.f, fmaxf(-10.f, ap + p.k.retention_bias));
+                const float eta = p.k.step_scale * softplus_f(ep);
+                const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
+                const float dn = sqrtf(dn2 + 1e-12f);
+                const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
+                float eff = cap * (-expm1f(-(eta / cap)));
+                if (p.k.spectral_clamp) {
+                    const float lim = nextafterf(p.k.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f);
+                    eff = fminf(eff, lim);
+                }
+                EFF[tid] = eff;
+                ALP[tid] = alpha;
+            }
+        } else if (p1_on && p1_tok < count) {
             const float* Sc = S + (size_t)p1_slot * SROWS * SP;
             const int row = (p1_slot << lt) + p1_tok;
             const int tin = (j << lt) + p1_tok;
@@ -400,6 +652,25 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
             ALP[row] = alpha;
         }
         __syncthreads();
+        if constexpr (MMA && kSpatial) {
+            if (mdef) {
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        if (mdef & (1u << (2 * mt + h))) {
+                            const int row = wrp * 32 + mt * 16 + qg + 8 * h;
+                            const int tin = (j << lt) + (row & (tile - 1));
+                            float* op = mt_out[mt] + (int64_t)scan_pixel(mt_ch[mt].dir, c, tin, p.H, p.W) * p.C + 2 * qt4;
+                            const float2 o_lo = *reinterpret_cast<const float2*>(Xs + row * 32 + 8 * qt4);
+                            const float2 o_hi = *reinterpret_cast<const float2*>(Qs + row * 32 + 8 * qt4);
+                            const float2 p_lo = *reinterpret_cast<const float2*>(op);
+                            const float2 p_hi = *reinterpret_cast<const float2*>(op + 8);
+                            *reinterpret_cast<float2*>(op) = make_float2(p_lo.x + o_lo.x, p_lo.y + o_lo.y);
+                            *reinterpret_cast<float2*>(op + 8) = make_float2(p_hi.x + o_hi.x, p_hi.y + o_hi.y);
+                        }
+            }
+        }
         if (kSpatial && deferred) {
 #pragma unroll (Unroll<D>::v)
             for (int i = 0; i < D / 4; ++i) {
@@ -489,6 +760,10 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
 #pragma unroll (Unroll<D>::v)
                     for (int jj = 0; jj < D; jj += 4)
                         *reinterpret_cast<float4*>(rowp + jj) = make_float4(acc[jj], acc[jj + 1], acc[jj + 2], acc[jj + 3]);
+                    if constexpr (MMA) {
+                        const int r = task - slot * SROWS;
+                        if (r < 3 * D) write_splits16(Mb + (size_t)slot * kSplits * 48 * 32, r, acc);
+                    }
                 }
             }
             ++c;

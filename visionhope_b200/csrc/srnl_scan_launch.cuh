@@ -4,6 +4,7 @@
 #pragma once
 
 #include <algorithm>
+#include <type_traits>
 
 #include "abi_util.h"
 #include "srnl_scan.cuh"
@@ -26,65 +27,88 @@ inline ScanPlan plan_scan(int D, int max_chunk, bool spatial) {
     return {tile, nch};
 }
 
-template <int D, typename XT, typename QT, int KIND>
+template <int D, typename XT, typename QT, int KIND, bool MMA>
 size_t scan_smem(const ScanPlan& pl) {
-    return ScanSmem<D>(pl.nch, pl.tile).total;
+    return ScanSmem<D>(pl.nch, pl.tile, MMA).total;
+}
+
+// The tensor-core token phase applies to D = 16 with bf16 x and raw bf16 queries.
+template <int D, typename XT, typename QT>
+constexpr bool mma_capable() {
+    return D == 16 && std::is_same<XT, __nv_bfloat16>::value && std::is_same<QT, __nv_bfloat16>::value;
 }
 
 // Halve the token tile (raising chains per CTA only within the thread budget) until the
-// shared-memory carve-up fits comfortably under the 227 KB per-CTA limit.
-template <int D, typename XT, typename QT, int KIND>
+// shared-memory carve-up fits under `limit`; the tensor-core variant aims at <= 56 KB so
+// four CTAs (the register-file limit) share an SM.
+template <int D, typename XT, typename QT, int KIND, bool MMA>
 ScanPlan fit_plan(int max_chunk) {
-    constexpr size_t kLimit = 200 * 1024;
-    ScanPlan pl = plan_scan(D, max_chunk, KIND != kKindSeq);
-    while (scan_smem<D, XT, QT, KIND>(pl) > kLimit && pl.tile > 4) {
+    const size_t limit = MMA ? 56 * 1024 : 200 * 1024;
+    const bool spatial = KIND != kKindSeq;
+    ScanPlan pl = plan_scan(D, max_chunk, spatial);
+    while (scan_smem<D, XT, QT, KIND, MMA>(pl) > limit && pl.tile > (MMA ? 16 : 4)) {
         pl.tile /= 2;
         const int nch = std::min(std::min(kScanThreads / D, kScanThreads / pl.tile), pl.nch);
-        pl.nch = KIND != kKindSeq ? std::max(2, nch & ~1) : nch;
+        pl.nch = spatial ? std::max(2, nch & ~1) : nch;
     }
-    while (scan_smem<D, XT, QT, KIND>(pl) > kLimit && pl.nch > (KIND != kKindSeq ? 2 : 1))
-        pl.nch -= KIND != kKindSeq ? 2 : 1;
+    while (scan_smem<D, XT, QT, KIND, MMA>(pl) > limit && pl.nch > (spatial ? 2 : 1)) pl.nch -= spatial ? 2 : 1;
     return pl;
 }
 
-template <int D, typename XT, typename QT, int KIND>
+template <int D, typename XT, typename QT, int KIND, bool MMA>
 int launch_scan(ScanParams p, const ScanPlan& pl, dim3 grid, cudaStream_t st) {
     p.nch = pl.nch;
     p.tile = pl.tile;
     p.log2tile = 0;
     while ((1 << p.log2tile) < pl.tile) ++p.log2tile;
     p.kind = KIND;
-    const size_t smem = scan_smem<D, XT, QT, KIND>(pl);
-    const void* fn = reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND>);
+    const size_t smem = scan_smem<D, XT, QT, KIND, MMA>(pl);
+    const void* fn = reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND, MMA>);
     if (!ensure_smem_attr(fn, smem))
         return fail(VH_E_DEVICE, "srnl scan: cannot reserve %zu bytes of shared memory", smem);
-    srnl_scan_kernel<D, XT, QT, KIND><<<grid, kScanThreads, smem, st>>>(p);
+    srnl_scan_kernel<D, XT, QT, KIND, MMA><<<grid, kScanThreads, smem, st>>>(p);
     return launch_status("srnl scan");
+}
+
+// Chooses the tensor-core variant when it applies (D = 16, bf16, chunks of 9+ tokens).
+template <int D, typename XT, typename QT, int KIND>
+int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStream_t st) {
+    const bool spatial = KIND != kKindSeq;
+    if constexpr (mma_capable<D, XT, QT>()) {
+        if (max_chunk > 8) {
+            const ScanPlan pl = fit_plan<D, XT, QT, KIND, true>(max_chunk);
+            const int per_cta = spatial ? pl.nch / 2 : pl.nch;
+            dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, spatial ? 1 : p.R);
+            return launch_scan<D, XT, QT, KIND, true>(p, pl, grid, st);
+        }
+    }
+    const ScanPlan pl = fit_plan<D, XT, QT, KIND, false>(max_chunk);
+    const int per_cta = spatial ? pl.nch / 2 : pl.nch;
+    dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, spatial ? 1 : p.R);
+    return launch_scan<D, XT, QT, KIND, false>(p, pl, grid, st);
 }
 
 template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
-    const ScanPlan rows = fit_plan<D, T, T, kKindRows>(p.W), cols = fit_plan<D, T, T, kKindCols>(p.H);
     const int pairs = p.B * p.heads;
-    dim3 grow((pairs + rows.nch / 2 - 1) / (rows.nch / 2)), gcol((pairs + cols.nch / 2 - 1) / (cols.nch / 2));
-    int rc = launch_scan<D, T, T, kKindRows>(p, rows, grow, st);
+    int rc = launch_auto<D, T, T, kKindRows>(p, p.W, pairs, st);
     if (rc) return rc;
-    return launch_scan<D, T, T, kKindCols>(p, cols, gcol, st);
+    return launch_auto<D, T, T, kKindCols>(p, p.H, pairs, st);
 }
 
 template <int D, typename XT, typename QT>
 int run_sequence(const ScanParams& p, cudaStream_t st) {
     int maxc = 1;
     for (int r = 0; r < p.R; ++r) maxc = std::max(maxc, p.chunk[r]);
-    const ScanPlan pl = fit_plan<D, XT, QT, kKindSeq>(maxc);
-    dim3 grid((p.B * p.heads + pl.nch - 1) / pl.nch, p.R);
-    return launch_scan<D, XT, QT, kKindSeq>(p, pl, grid, st);
+    return launch_auto<D, XT, QT, kKindSeq>(p, maxc, p.B * p.heads, st);
 }
 
 template <int D, typename XT, typename QT, int KIND>
 void set_attr_one() {
     // Reserve the opt-in maximum once per device; every launch re-checks its own size.
-    ensure_smem_attr(reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND>), 48 * 1024 + 1);
+    ensure_smem_attr(reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND, false>), 48 * 1024 + 1);
+    if constexpr (mma_capable<D, XT, QT>())
+        ensure_smem_attr(reinterpret_cast<const void*>(&srnl_scan_kernel<D, XT, QT, KIND, true>), 48 * 1024 + 1);
 }
 
 template <int D>

@@ -10,8 +10,12 @@ from .cuda import on_tensor_device
 
 
 @on_tensor_device
-def grn_forward(x, gamma, beta, eps, *, want_stats=False):
-    """x logical [B, C, H, W] stored channels-last -> fp32 channels-last y (and Gx, 1/den)."""
+def grn_forward(x, gamma, beta, eps, *, want_stats=False, out_dtype=torch.float32):
+    """x logical [B, C, H, W] stored channels-last -> channels-last y (and Gx, 1/den).
+
+    out_dtype float32 is the reference's output; bfloat16/float16 return the same fp32 result
+    rounded once, which is exactly what an autocast consumer would cast it to.
+    """
     _lib.ensure_device(x)
     if x.dim() != 4 or not x.is_contiguous(memory_format=torch.channels_last):
         raise RuntimeError("GRN CUDA expects channels-last NCHW input")
@@ -20,14 +24,14 @@ def grn_forward(x, gamma, beta, eps, *, want_stats=False):
     b = beta.detach().reshape(-1).contiguous().float()
     if g.numel() != C or b.numel() != C:
         raise RuntimeError("GRN CUDA requires contiguous FP32 channel parameters on the input device")
-    y = torch.empty_like(x, dtype=torch.float32, memory_format=torch.channels_last)
+    y = torch.empty_like(x, dtype=out_dtype, memory_format=torch.channels_last)
     gx = torch.empty((B, C), device=x.device, dtype=torch.float32) if want_stats else None
     inv = torch.empty((B,), device=x.device, dtype=torch.float32) if want_stats else None
     nbytes = int(_lib.load().vh_grn_workspace_bytes(B, H, W, C))
     ws = torch.empty((max(nbytes, 16) + 3) // 4, device=x.device, dtype=torch.float32)
     _lib.check(_lib.load().vh_grn_fwd(
         x.data_ptr(), _lib.dtype_code(x.dtype), g.data_ptr(), b.data_ptr(), float(eps), y.data_ptr(),
-        _lib.ptr(gx), _lib.ptr(inv), ws.data_ptr(), ws.numel() * 4, B, H, W, C,
+        _lib.dtype_code(out_dtype), _lib.ptr(gx), _lib.ptr(inv), ws.data_ptr(), ws.numel() * 4, B, H, W, C,
         _lib.stream_handle(x.device)), "vh_grn_fwd")
     return (y, gx, inv) if want_stats else y
 

@@ -10,19 +10,23 @@ from .cuda import on_tensor_device
 
 
 @on_tensor_device
-def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False):
-    """x_rows [rows, C] (any float dtype, contiguous) -> fp32 [rows, C] (and mean, rstd)."""
+def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False, out_dtype=torch.float32):
+    """x_rows [rows, C] (any float dtype, contiguous) -> [rows, C] (and mean, rstd).
+
+    out_dtype float32 is the reference's output; bfloat16/float16 round that result once.
+    """
     _lib.ensure_device(x_rows)
     x = x_rows.contiguous()
     rows, C = x.shape
     w = weight.detach().reshape(-1).contiguous().float()
     b = bias.detach().reshape(-1).contiguous().float()
-    y = torch.empty((rows, C), device=x.device, dtype=torch.float32)
+    y = torch.empty((rows, C), device=x.device, dtype=out_dtype)
     mean = torch.empty((rows,), device=x.device, dtype=torch.float32) if want_stats else None
     rstd = torch.empty((rows,), device=x.device, dtype=torch.float32) if want_stats else None
     _lib.check(_lib.load().vh_layernorm_fwd(
         x.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), b.data_ptr(), float(eps), y.data_ptr(),
-        _lib.ptr(mean), _lib.ptr(rstd), rows, C, _lib.stream_handle(x.device)), "vh_layernorm_fwd")
+        _lib.dtype_code(out_dtype), _lib.ptr(mean), _lib.ptr(rstd), rows, C,
+        _lib.stream_handle(x.device)), "vh_layernorm_fwd")
     return (y, mean, rstd) if want_stats else y
 
 
