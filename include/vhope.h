@@ -88,6 +88,17 @@ typedef struct {
  * x and q share dtype (VH_F32 / VH_BF16 / VH_F16).  out: fp32 [B, H, W, C], caller-allocated
  * with out_batch_stride elements per image and C per pixel.
  * skip: C values (shared across directions) or 4*C (skip_per_dir = 1); weight: fp32 [4, C].
+ *
+ * Optional fields (leave zero / NULL when unused):
+ *   aux:       fp32 plane with out's layout (out_batch_stride).  With it the column scans
+ *              run concurrently with the row scans and accumulate here; each (batch, head)
+ *              then adds its aux slice into out (or into final_out).  Its content afterwards
+ *              is unspecified.  Without it the two passes run one after the other in out.
+ *   final_out: final_dtype [B, H, W, C] with final_batch_stride elements per image and C per
+ *              pixel: receives (final_dtype)(sum of the four scans + addend).  out is then
+ *              scratch and its content afterwards unspecified.
+ *   addend:    io_dtype [B, H, W, C] (addend_batch_stride, C per pixel) added before the
+ *              final cast (the block's output position term); requires final_out.
  * -------------------------------------------------------------------------------------*/
 typedef struct {
     vh_srnl_memories mem;
@@ -104,6 +115,12 @@ typedef struct {
     int64_t out_batch_stride;
     int32_t batch, height, width, heads, head_dim;
     vh_srnl_consts consts;
+    float* aux;
+    const void* addend;
+    int64_t addend_batch_stride;
+    void* final_out;
+    int32_t final_dtype;
+    int64_t final_batch_stride;
 } vh_srnl_spatial_args;
 
 int vh_srnl_spatial_fwd(const vh_srnl_spatial_args* args, vh_stream_t stream);
@@ -209,6 +226,10 @@ int vh_init(int32_t device);
 
 /* Thread-local description of the last failure on this thread ("" if none). */
 const char* vh_last_error(void);
+
+/* Number of kernels the last entry point called on this thread launched (0 after a
+ * validation failure).  Lets a host count device launches without knowing each path. */
+int vh_last_launch_count(void);
 
 /* Library version string. */
 const char* vh_version(void);

@@ -18,7 +18,7 @@ def test_header_declares_the_entry_points():
     names = declared_symbols()
     for want in ("vh_srnl_spatial_fwd", "vh_srnl_sequence_fwd", "vh_qnorm_fwd", "vh_dirfuse_fwd",
                  "vh_grn_fwd", "vh_grn_workspace_bytes", "vh_layernorm_fwd", "vh_init",
-                 "vh_last_error", "vh_version"):
+                 "vh_last_error", "vh_last_launch_count", "vh_version"):
         assert want in names
 
 
@@ -38,6 +38,42 @@ def test_struct_layouts_match_header_sizes():
     assert ctypes.sizeof(_lib.VhConsts) == 24
     assert ctypes.sizeof(_lib.VhMemories) == 48
     assert ctypes.sizeof(_lib.VhSequenceArgs) == 48 + 3 * 8 + 8 * 4 + 4 * 4 + 24 + 0
+
+
+def _c_layout(struct, fields):
+    """sizeof and offsetof of `fields` of a header struct, compiled with the host C compiler."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    body = "".join(f'printf("%zu\\n", offsetof({struct}, {f}));\n' for f in fields)
+    src = ("#include <stddef.h>\n#include <stdio.h>\n#include \"vhope.h\"\n"
+           f"int main(void) {{ printf(\"%zu\\n\", sizeof({struct}));\n{body} return 0; }}\n")
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = Path(d) / "layout.c", Path(d) / "layout"
+        c.write_text(src)
+        subprocess.run([cc, "-I", str(ROOT / "include"), str(c), "-o", str(exe)], check=True)
+        vals = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                               text=True).stdout.split()]
+    return vals[0], vals[1:]
+
+
+@pytest.mark.parametrize("struct,cls", [("vh_srnl_spatial_args", "VhSpatialArgs"),
+                                        ("vh_srnl_sequence_args", "VhSequenceArgs"),
+                                        ("vh_srnl_consts", "VhConsts"),
+                                        ("vh_srnl_memories", "VhMemories")])
+def test_ctypes_mirrors_match_the_header(struct, cls):
+    """Every field of the ctypes mirrors sits at the offset the C compiler gives it."""
+    from visionhope_b200 import _lib
+
+    py = getattr(_lib, cls)
+    names = [f[0] for f in py._fields_]
+    size, offsets = _c_layout(struct, names)
+    assert ctypes.sizeof(py) == size
+    assert [getattr(py, n).offset for n in names] == offsets
 
 
 def _err(lib):

@@ -50,7 +50,8 @@ SPATIAL_CASES = [
 
 @pytest.mark.parametrize("case", SPATIAL_CASES, ids=lambda c: "x".join(map(str, c)))
 @pytest.mark.parametrize("layout", ["scans", "image"])
-def test_spatial_operator_matches_oracle(case, layout, oracle, cuda):
+@pytest.mark.parametrize("concurrent", [True, False], ids=["one-launch", "two-pass"])
+def test_spatial_operator_matches_oracle(case, layout, concurrent, oracle, cuda):
     from visionhope_b200.srnl_core.fused import spatial_forward
 
     B, H, W, heads, D, io, kind, per_dir = case
@@ -68,14 +69,16 @@ def test_spatial_operator_matches_oracle(case, layout, oracle, cuda):
         x, q = _t(xs, cuda, TORCH_DT[io]), _t(qs, cuda, TORCH_DT[io])
     else:
         x, q = _t(img, cuda, TORCH_DT[io]), _t(qimg, cuda, TORCH_DT[io])
-    out = spatial_forward(dev_mems, x, q, _t(skip, cuda), _t(weights, cuda), H, W, D, layout=layout)
+    out = spatial_forward(dev_mems, x, q, _t(skip, cuda), _t(weights, cuda), H, W, D, layout=layout,
+                          concurrent=concurrent)
     torch.cuda.synchronize()
     assert out.dtype == torch.float32 and tuple(out.shape) == (B, H, W, C)
     err = rel_err(out.cpu().numpy(), expected)
     assert err < 1e-4, err
 
 
-def test_spatial_is_deterministic(oracle, cuda):
+@pytest.mark.parametrize("concurrent", [True, False], ids=["one-launch", "two-pass"])
+def test_spatial_is_deterministic(concurrent, oracle, cuda):
     from visionhope_b200.srnl_core.fused import spatial_forward
 
     gen = np.random.default_rng(7)
@@ -85,9 +88,41 @@ def test_spatial_is_deterministic(oracle, cuda):
     x = _t(gen.normal(size=(B, H, W, C)), cuda, torch.bfloat16)
     q = _t(gen.normal(size=(B, H, W, C)), cuda, torch.bfloat16)
     skip, wts = _t(gen.normal(size=C), cuda), _t(gen.normal(1, 0.2, size=(4, C)), cuda)
-    a = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image")
-    b = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image")
+    a = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", concurrent=concurrent)
+    b = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", concurrent=concurrent)
     assert torch.equal(a, b)
+
+
+FINAL_CASES = [
+    # (B, H, W, heads, D, io, final dtype)
+    (2, 14, 14, 2, 16, "bf16", "bf16"),   # one launch: the CTA folds planes, addend and cast
+    (1, 9, 17, 3, 16, "bf16", "f32"),
+    (2, 7, 7, 2, 16, "bf16", "f16"),      # small image: two passes + finalize launch
+    (1, 6, 5, 2, 8, "f32", "bf16"),       # CUDA-core scans + finalize launch
+]
+
+
+@pytest.mark.parametrize("case", FINAL_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_spatial_final_output_with_addend(case, oracle, cuda):
+    """(final dtype)(sum of the scans + addend): equal, bit for bit, to the fp32 result plus the
+    addend in fp32 and one cast (the reference's `out + lepe` then autocast's cast)."""
+    from visionhope_b200.srnl_core.fused import spatial_forward
+
+    B, H, W, heads, D, io, fdt = case
+    C = heads * D
+    gen = np.random.default_rng(zlib.crc32(repr(case).encode()))
+    mems = [_t(m, cuda) for m in make_memories(4, heads, D, "stress", gen)]
+    x = _t(gen.normal(size=(B, H, W, C)), cuda, TORCH_DT[io])
+    q = _t(gen.normal(size=(B, H, W, C)), cuda, TORCH_DT[io])
+    add = _t(gen.normal(size=(B, H, W, C)), cuda, TORCH_DT[io])
+    skip, wts = _t(gen.normal(size=C), cuda), _t(gen.normal(1, 0.2, size=(4, C)), cuda)
+    ref = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image")
+    fin = spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", addend=add,
+                          final_dtype=TORCH_DT[fdt])
+    assert fin.dtype == TORCH_DT[fdt] and tuple(fin.shape) == (B, H, W, C)
+    assert torch.equal(fin, (ref + add.float()).to(TORCH_DT[fdt]))
+    with pytest.raises(RuntimeError, match="addend requires"):
+        spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", addend=add)
 
 
 SEQ_CASES = [

@@ -43,7 +43,9 @@ class VhSpatialArgs(ctypes.Structure):
                 ("skip_per_dir", c_int32), ("weight", c_void_p), ("out", c_void_p),
                 ("out_batch_stride", c_int64), ("batch", c_int32), ("height", c_int32),
                 ("width", c_int32), ("heads", c_int32), ("head_dim", c_int32),
-                ("consts", VhConsts)]
+                ("consts", VhConsts), ("aux", c_void_p), ("addend", c_void_p),
+                ("addend_batch_stride", c_int64), ("final_out", c_void_p),
+                ("final_dtype", c_int32), ("final_batch_stride", c_int64)]
 
 
 class VhSequenceArgs(ctypes.Structure):
@@ -90,6 +92,8 @@ def load() -> ctypes.CDLL:
                                              c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                                              c_void_p]
             lib.vh_init.argtypes = [c_int32]
+            lib.vh_last_launch_count.restype = c_int32
+            lib.vh_last_launch_count.argtypes = []
             lib.vh_probe_ffma.restype = c_int32
             lib.vh_probe_ffma.argtypes = [c_void_p, c_int32, c_int32, c_void_p]
             _lib = lib
@@ -100,20 +104,18 @@ def version() -> str:
     return load().vh_version().decode()
 
 
-# Kernels each successful entry-point call launches (the spatial operator runs a rows pass and
-# a columns pass; GRN runs a statistics pass and an apply pass).
-_LAUNCHES_PER_CALL = {"vh_srnl_spatial_fwd": 2, "vh_grn_fwd": 2}
+# Kernels the library launched through this module (the library reports each call's count).
 launch_count = 0
 
 
 def check(rc: int, what: str) -> None:
     """Raise on a non-zero status; otherwise count the kernels the call launched."""
     global launch_count
+    lib = load()
     if rc != 0:
-        msg = load().vh_last_error().decode() or "unknown error"
+        msg = lib.vh_last_error().decode() or "unknown error"
         raise RuntimeError(f"{what} failed ({rc}): {msg}")
-    if what != "vh_init":
-        launch_count += _LAUNCHES_PER_CALL.get(what, 1)
+    launch_count += lib.vh_last_launch_count()
 
 
 def ensure_device(t: torch.Tensor) -> None:

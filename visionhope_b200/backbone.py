@@ -198,9 +198,16 @@ class VisionHOPEBlock(nn.Module):
         if self._inference_prepared:
             path, _ = self.operator._inference_path(x_local)
             if path != "ordinary":
-                out = self.operator._forward_fast(x_local, path)  # fp32 NHWC
+                # The scan launch adds the output position term and writes the dtype the output
+                # projection consumes: (out + lepe) rounded once, as the reference's fp32 add
+                # followed by autocast's cast.
+                lepe = None
                 if self.local_position is not None:
-                    out = out + self.local_position(x_local).permute(0, 2, 3, 1)
+                    lepe = self.local_position(x_local).permute(0, 2, 3, 1)
+                    if lepe.dtype != x_local.dtype:
+                        lepe = lepe.to(x_local.dtype)
+                out = self.operator._forward_fast(x_local, path, addend=lepe,
+                                                  final_dtype=_autocast_dtype() or torch.float32)
                 out = self.proj_out(out)
                 # NHWC storage viewed as NCHW (channels-last); the reference copies it to
                 # contiguous NCHW here, which only costs a layout pass before the residual add.

@@ -15,6 +15,7 @@ namespace vh {
 
 namespace {
 thread_local char g_last_error[512] = {0};
+thread_local int g_launches = 0;
 std::mutex g_attr_mu;
 std::set<std::pair<int, const void*>>& attr_done() {
     static std::set<std::pair<int, const void*>> s;
@@ -30,11 +31,15 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
-void clear_error() { g_last_error[0] = 0; }
+void clear_error() {
+    g_last_error[0] = 0;
+    g_launches = 0;
+}
 
 int launch_status(const char* what) {
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail((int)e, "%s: launch failed: %s", what, cudaGetErrorString(e));
+    ++g_launches;
     return 0;
 }
 
@@ -74,5 +79,7 @@ extern "C" int vh_init(int32_t device) {
 }
 
 extern "C" const char* vh_last_error(void) { return vh::g_last_error; }
+
+extern "C" int vh_last_launch_count(void) { return vh::g_launches; }
 
 extern "C" const char* vh_version(void) { return "vhope-b200 0.1 (sm_100a)"; }

@@ -55,6 +55,47 @@ int row_vec_bytes(int D, int dt) {
 
 }  // namespace
 
+// (final dtype)(out + addend) over [B, H*W*C] in groups of four channels.
+template <typename AT>
+__global__ void spatial_finalize_kernel(const float* __restrict__ out, int64_t ob,
+                                        const AT* __restrict__ addend, int64_t ab, void* fin,
+                                        int fdt, int64_t fb, int64_t groups_per_image, int B) {
+    const int64_t total = groups_per_image * B;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / groups_per_image, r = (i - b * groups_per_image) * 4;
+        float4 v = load4(out + b * ob + r);
+        if (addend) {
+            const float4 e = load4(addend + b * ab + r);
+            v = make_float4(v.x + e.x, v.y + e.y, v.z + e.z, v.w + e.w);
+        }
+        if (fdt == VH_F32) store4(static_cast<float*>(fin) + b * fb + r, v);
+        else if (fdt == VH_BF16) store4(static_cast<__nv_bfloat16*>(fin) + b * fb + r, v);
+        else store4(static_cast<__half*>(fin) + b * fb + r, v);
+    }
+}
+
+int launch_spatial_finalize(const ScanParams& p, int io_dtype, cudaStream_t st) {
+    const int64_t groups = (int64_t)p.L * p.C / 4, total = groups * p.B;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
+    switch (io_dtype) {
+        case VH_F32:
+            spatial_finalize_kernel<float><<<grid, 256, 0, st>>>(p.out, p.ob, static_cast<const float*>(p.addend),
+                                                                 p.ab, p.fin, p.fin_dtype, p.fb, groups, p.B);
+            break;
+        case VH_BF16:
+            spatial_finalize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+                p.out, p.ob, static_cast<const __nv_bfloat16*>(p.addend), p.ab, p.fin, p.fin_dtype, p.fb, groups, p.B);
+            break;
+        default:
+            spatial_finalize_kernel<__half><<<grid, 256, 0, st>>>(p.out, p.ob, static_cast<const __half*>(p.addend),
+                                                                  p.ab, p.fin, p.fin_dtype, p.fb, groups, p.B);
+    }
+    return launch_status("srnl spatial finalize");
+}
+
 int init_scan_kernels() {
     set_attr_d<4>();
     set_attr_d<8>();
@@ -98,6 +139,23 @@ extern "C" int vh_srnl_spatial_fwd(const vh_srnl_spatial_args* a, vh_stream_t st
         a->x_head_stride < a->head_dim || a->q_head_stride < a->head_dim ||
         a->out_batch_stride < L * C)
         return fail(VH_E_SHAPE, "vh_srnl_spatial_fwd: token/head strides smaller than head_dim");
+    if (a->aux && (a->aux == a->out || !aligned(a->aux, 16)))
+        return fail(VH_E_ARG, "vh_srnl_spatial_fwd: aux must be a 16-byte aligned plane distinct from out");
+    if (a->addend && !a->final_out)
+        return fail(VH_E_ARG, "vh_srnl_spatial_fwd: addend requires final_out");
+    if (a->final_out) {
+        if (!dtype_ok(a->final_dtype)) return fail(VH_E_DTYPE, "vh_srnl_spatial_fwd: bad final dtype");
+        if (!aligned(a->final_out, 16) || a->final_batch_stride % 4)
+            return fail(VH_E_ALIGN, "vh_srnl_spatial_fwd: final_out must be 16-byte aligned");
+        if (a->final_batch_stride < L * C)
+            return fail(VH_E_SHAPE, "vh_srnl_spatial_fwd: final_batch_stride smaller than H*W*C");
+    }
+    if (a->addend) {
+        if (!aligned(a->addend, 4 * dtype_size(a->io_dtype)) || a->addend_batch_stride % 4)
+            return fail(VH_E_ALIGN, "vh_srnl_spatial_fwd: addend must be aligned to 4 elements");
+        if (a->addend_batch_stride < L * C)
+            return fail(VH_E_SHAPE, "vh_srnl_spatial_fwd: addend_batch_stride smaller than H*W*C");
+    }
 
     ScanParams p{};
     p.Mm = a->mem.m; p.Mv = a->mem.v; p.Mk = a->mem.k; p.Me = a->mem.eta; p.Ma = a->mem.alpha;
@@ -114,6 +172,12 @@ extern "C" int vh_srnl_spatial_fwd(const vh_srnl_spatial_args* a, vh_stream_t st
     p.chunk[0] = p.chunk[1] = a->width;
     p.chunk[2] = p.chunk[3] = a->height;
     p.k = to_consts(a->consts);
+    p.aux = a->aux;
+    p.addend = a->addend;
+    p.ab = a->addend_batch_stride;
+    p.fin = a->final_out;
+    p.fin_dtype = a->final_dtype;
+    p.fb = a->final_batch_stride;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (a->io_dtype) {
         case VH_F32: return spatial_dispatch_d<float>(a->head_dim, p, st);

@@ -35,7 +35,9 @@
 namespace vh {
 
 constexpr int kScanThreads = 128;
-enum ScanKind { kKindRows = 0, kKindCols = 1, kKindSeq = 2 };
+// kKindBoth: rows and columns passes in one launch (warp-per-chain scan only), the columns
+// pass accumulating in a second fp32 plane that each CTA folds in at its end.
+enum ScanKind { kKindRows = 0, kKindCols = 1, kKindSeq = 2, kKindBoth = 3 };
 
 struct ScanParams {
     const float* Mm;
@@ -60,6 +62,14 @@ struct ScanParams {
     int chunk[4];
     int kind, nch, tile, log2tile;
     SrnlConsts k;
+    // spatial, optional: second accumulation plane (out's layout), final cast target and the
+    // addend folded in before the cast (io dtype, [B, H, W, C]).
+    float* aux;
+    const void* addend;
+    int64_t ab;
+    void* fin;
+    int fin_dtype;
+    int64_t fb;
 };
 
 // Loops over head_dim are fully unrolled up to D = 16 (every shipped model); larger head

@@ -8,6 +8,7 @@
 
 #include "abi_util.h"
 #include "srnl_scan.cuh"
+#include "srnl_warp.cuh"
 
 namespace vh {
 
@@ -70,17 +71,31 @@ int launch_scan(ScanParams p, const ScanPlan& pl, dim3 grid, cudaStream_t st) {
     return launch_status("srnl scan");
 }
 
-// Chooses the tensor-core variant when it applies (D = 16, bf16, chunks of 9+ tokens).
+// Warp-per-chain scan (D = 16, bf16), four warps per CTA: the four scans of one (b, head)
+// (kKindBoth), two scan pairs of one pass (kKindRows / kKindCols) or four sequence chains.
+template <int KIND>
+int launch_warp(ScanParams p, int pairs_or_chains, cudaStream_t st) {
+    p.kind = KIND;
+    p.nch = wpc::kWarps;
+    p.tile = wpc::kTile;
+    p.log2tile = 5;
+    const size_t smem = sizeof(wpc::ChainSmem) * wpc::kWarps;
+    const int per_cta = KIND == kKindBoth ? 1 : KIND == kKindSeq ? wpc::kWarps : 2;
+    const dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, KIND == kKindSeq ? p.R : 1);
+    const void* fn = reinterpret_cast<const void*>(&wpc::srnl_warp_kernel<KIND>);
+    if (!ensure_smem_attr(fn, smem))
+        return fail(VH_E_DEVICE, "srnl warp scan: cannot reserve %zu bytes of shared memory", smem);
+    wpc::srnl_warp_kernel<KIND><<<grid, wpc::kThreads, smem, st>>>(p);
+    return launch_status("srnl warp scan");
+}
+
+// Chooses the warp-per-chain tensor-core scan when it applies (D = 16, bf16, chunks of 9+
+// tokens), else the CTA-lockstep scan.
 template <int D, typename XT, typename QT, int KIND>
 int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStream_t st) {
     const bool spatial = KIND != kKindSeq;
     if constexpr (mma_capable<D, XT, QT>()) {
-        if (max_chunk > 8) {
-            const ScanPlan pl = fit_plan<D, XT, QT, KIND, true>(max_chunk);
-            const int per_cta = spatial ? pl.nch / 2 : pl.nch;
-            dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, spatial ? 1 : p.R);
-            return launch_scan<D, XT, QT, KIND, true>(p, pl, grid, st);
-        }
+        if (max_chunk > 8) return launch_warp<KIND>(p, pairs_or_chains, st);
     }
     const ScanPlan pl = fit_plan<D, XT, QT, KIND, false>(max_chunk);
     const int per_cta = spatial ? pl.nch / 2 : pl.nch;
@@ -88,12 +103,24 @@ int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStr
     return launch_scan<D, XT, QT, KIND, false>(p, pl, grid, st);
 }
 
+// Writes (final dtype)(out + addend) when the scans ran without folding it in (srnl_scan.cu).
+int launch_spatial_finalize(const ScanParams& p, int io_dtype, cudaStream_t st);
+
+// Both passes in one launch when the warp-per-chain scan applies and an aux plane is given
+// (the final cast and addend are then folded in by each CTA); otherwise the rows pass, the
+// columns pass and, if a final output is requested, a finalize launch.
 template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
     const int pairs = p.B * p.heads;
+    if constexpr (mma_capable<D, T, T>()) {
+        if (p.aux && std::max(p.H, p.W) > 8) return launch_warp<kKindBoth>(p, pairs, st);
+    }
     int rc = launch_auto<D, T, T, kKindRows>(p, p.W, pairs, st);
     if (rc) return rc;
-    return launch_auto<D, T, T, kKindCols>(p, p.H, pairs, st);
+    rc = launch_auto<D, T, T, kKindCols>(p, p.H, pairs, st);
+    if (rc || !p.fin) return rc;
+    const int io = std::is_same<T, float>::value ? VH_F32 : std::is_same<T, __half>::value ? VH_F16 : VH_BF16;
+    return launch_spatial_finalize(p, io, st);
 }
 
 template <int D, typename XT, typename QT>

@@ -1,0 +1,623 @@
+// Warp-per-chain SRNL scan for head_dim 16 with bf16 inputs (the inference hot path).
+//
+// One warp owns one chain (a (batch, direction, head) scan) for its whole length.  A CTA holds
+// four warps and never synchronizes all of them before its end, so each warp advances on its
+// own and the SM hides one warp's latency behind the others:
+//   kKindBoth       the four scans of one (batch, head): warps 0/1 (rows pair) accumulate in
+//                   `out`, warps 2/3 (columns pair) in `aux`; the CTA then folds aux into out,
+//                   or writes (final dtype)(out + aux + addend) into `fin`.
+//   kKindRows/Cols  two scan pairs of one pass (the passes run as two launches in `out`).
+//   kKindSeq        four independent packed-sequence chains.
+//
+// Per chunk (chunk-start state S = [M_m; M_v; M_k; e^T; a^T], gain G reset to I):
+//   P1  tokens in steps of 32 (two 16-row MMA tiles):
+//       - x and raw q fragments come from global memory straight into registers, one step
+//         ahead;
+//       - k~ = M_k x, v = M_v x and M_m q_raw run as bf16 m16n8k16 tensor-core MMAs against
+//         the three-way bf16 split of the fp32 memories (fp32 accumulate, 24-bit operands);
+//         y = (M_m q_raw) / ||q_raw|| (models/srnl_core/csrc/inference_recurrence.cuh:40-60);
+//       - each token's own lane finishes the key norm, the eta/alpha gates, the injection
+//         cap and the spectral clamp in-thread (inference_recurrence.cuh:60-90,
+//         memory.cuh:219-233), and k_t . k_{t+1} for the lookahead below.
+//   P2  the gain recurrence r_t = (k_t - v_t) + G k_t, G <- alpha_t G - eta_t r_t k_t^T
+//       (inference_recurrence.cuh:92-106), two lanes per row of G, eight columns each.
+//       r_{t+1} is formed as d_{t+1} + alpha_t (G k_{t+1}) - u_t (k_t . k_{t+1}) with
+//       u_t = eta_t r_t, so the dot product for token t+1 runs beside the update of token t
+//       and the serial dependence per token is one FMA and one multiply.
+//   P3  S <- S G (inference_recurrence.cuh:110-135) as tensor-core MMAs over split operands
+//       (6 of the 9 split products; the dropped ones are below 2^-24 relative).
+// The memories live only as their three bf16 parts (hi + mid + lo reproduce the fp32 value to
+// 2^-24), plus e and a in fp32.
+//
+// Spatial output order (deterministic, no atomics): every pixel is touched once by each scan
+// of a pair; the first touch stores into a fresh plane, the later one adds, and touches of both
+// scans in the same step (middle row/column) are ordered by the pair's named barrier: the even
+// scan writes first.  Reads of a partner's value are issued before P2 so their latency hides
+// behind it; all of a step's writes land before the pair's barrier at the end of the step.
+#pragma once
+
+#include "srnl_scan.cuh"
+
+namespace vh {
+namespace wpc {
+
+constexpr int kD = 16;
+constexpr int kWarps = 4;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTile = 32;  // tokens per step (two 16-row MMA tiles)
+constexpr int kKP = 20;    // padded row stride (floats) of the per-token key rows: 80-byte rows
+                           // keep the one-token-per-lane float4 accesses free of bank conflicts
+
+// Per-warp (per-chain) shared memory.
+struct alignas(16) ChainSmem {
+    unsigned char mb[kSplits][48][32];  // split memory rows: 0-15 M_m, 16-31 M_v, 32-47 M_k
+    float ea[2][kD];                    // e (learning-rate memory) and a (retention memory)
+    float kt[kTile][kKP];               // raw k~, then the normalized key k
+    float dt[kTile][kKP];               // raw v, then d = k - v
+    float4 gate[kTile];                 // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
+    unsigned char gs[kSplits][16][32];  // split gain rows (row-major, k x n)
+};
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const unsigned char* p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Three-way bf16 split of a pair of fp32 values: parts[k] packs (lo, hi) of part k.
+__device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSplits]) {
+#pragma unroll
+    for (int k = 0; k < kSplits; ++k) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+        const float2 f = __bfloat1622float2(h);
+        lo -= f.x;
+        hi -= f.y;
+        parts[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+}
+
+__device__ __forceinline__ void pair_barrier(int id) {
+    asm volatile("bar.sync %0, 64;\n" ::"r"(id) : "memory");
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+
+struct Role {
+    int b, dir, head, valid;
+    float* plane;      // spatial accumulation plane of this warp's pass
+    int bar;           // named barrier of the scan pair
+    bool store_first;  // the pair's first touch of a pixel stores (the plane starts unwritten)
+};
+
+template <int KIND>
+__device__ __forceinline__ Role warp_role(const ScanParams& p, int warp) {
+    Role r;
+    int idx;
+    if (KIND == kKindSeq) {
+        idx = blockIdx.x * kWarps + warp;
+        r.dir = blockIdx.y;
+    } else if (KIND == kKindBoth) {
+        idx = blockIdx.x;
+        r.dir = warp;
+    } else {
+        idx = blockIdx.x * 2 + (warp >> 1);
+        r.dir = 2 * KIND + (warp & 1);
+    }
+    r.valid = idx < p.B * p.heads;
+    r.b = r.valid ? idx / p.heads : 0;
+    r.head = r.valid ? idx % p.heads : 0;
+    r.plane = (KIND == kKindBoth && warp >= 2) ? p.aux : p.out;
+    r.bar = 1 + (warp >> 1);
+    r.store_first = KIND != kKindCols;
+    return r;
+}
+
+// The gain recurrence over the `count` tokens of one step (N > 0: exactly N, unrolled).
+// Lane (row, half) holds G[row][8 half .. 8 half + 7] in g.
+template <int N>
+__device__ __forceinline__ void gain_pass(const ChainSmem& cs, int count, int row, int half, float (&g)[8]) {
+    if (N > 0) count = N;
+    float kc[8];
+    {
+        const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[0][8 * half]);
+        const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[0][8 * half + 4]);
+        kc[0] = lo.x; kc[1] = lo.y; kc[2] = lo.z; kc[3] = lo.w;
+        kc[4] = hi.x; kc[5] = hi.y; kc[6] = hi.z; kc[7] = hi.w;
+    }
+    float4 gt = cs.gate[0];
+    float u;
+    {
+        float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            r0 = fmaf(g[i], kc[i], r0);
+            r1 = fmaf(g[i + 1], kc[i + 1], r1);
+        }
+        float part = r0 + r1;
+        part += __shfl_xor_sync(0xffffffffu, part, 16);
+        u = gt.x * (part + cs.dt[0][row]);
+    }
+#pragma unroll (N > 0 ? N : 1)
+    for (int t = 0; t < count; ++t) {
+        const float alpha = gt.y, kk = gt.z;
+        float kn[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float unext = 0.f;
+        if (t + 1 < count) {
+            const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[t + 1][8 * half]);
+            const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[t + 1][8 * half + 4]);
+            kn[0] = lo.x; kn[1] = lo.y; kn[2] = lo.z; kn[3] = lo.w;
+            kn[4] = hi.x; kn[5] = hi.y; kn[6] = hi.z; kn[7] = hi.w;
+            gt = cs.gate[t + 1];
+            float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                r0 = fmaf(g[i], kn[i], r0);
+                r1 = fmaf(g[i + 1], kn[i + 1], r1);
+            }
+            float part = r0 + r1;
+            part += __shfl_xor_sync(0xffffffffu, part, 16);
+            // r_{t+1} = d_{t+1} + alpha_t (G_{t-1} k_{t+1}) - u_t (k_t . k_{t+1})
+            const float r = fmaf(-u, kk, fmaf(alpha, part, cs.dt[t + 1][row]));
+            unext = gt.x * r;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[i] = fmaf(-u, kc[i], alpha * g[i]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kc[i] = kn[i];
+        u = unext;
+    }
+}
+
+template <bool kSpatial>
+__device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, const Role& ro) {
+    using bf16 = __nv_bfloat16;
+    const int lane = threadIdx.x & 31;
+    const int qg = lane >> 2, qt = lane & 3;  // MMA fragment coordinates
+    const int dir = ro.dir;
+
+    // ---- state set-up: split memories, e/a, and this lane's fusion weights -------------
+    const int64_t sidx = p.mem_per_chain ? ((int64_t)ro.b * p.R + dir) * p.heads + ro.head
+                                         : (int64_t)dir * p.heads + ro.head;
+    for (int r = lane; r < 48; r += 32) {
+        const float* src = r < 16 ? p.Mm + (sidx * kD + r) * kD
+                         : r < 32 ? p.Mv + (sidx * kD + r - 16) * kD
+                                  : p.Mk + (sidx * kD + r - 32) * kD;
+        float v[kD];
+#pragma unroll
+        for (int i = 0; i < kD; i += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(src + i);
+            v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+        }
+        write_splits16(&cs.mb[0][0][0], r, v);
+    }
+    if (lane < kD) {
+        cs.ea[0][lane] = p.Me[sidx * kD + lane];
+        cs.ea[1][lane] = p.Ma[sidx * kD + lane];
+    }
+    float wlo[2] = {0.f, 0.f}, whi[2] = {0.f, 0.f}, slo[2] = {0.f, 0.f}, shi[2] = {0.f, 0.f};
+    if constexpr (kSpatial) {
+        const int c0 = ro.head * kD;
+        const float* wv = p.weight + dir * p.C + c0;
+        const float* sv = p.skip + (p.skip_per_dir ? dir * p.C : 0) + c0;
+        wlo[0] = wv[2 * qt]; wlo[1] = wv[2 * qt + 1]; whi[0] = wv[8 + 2 * qt]; whi[1] = wv[9 + 2 * qt];
+        slo[0] = sv[2 * qt]; slo[1] = sv[2 * qt + 1]; shi[0] = sv[8 + 2 * qt]; shi[1] = sv[9 + 2 * qt];
+    }
+    __syncwarp();
+
+    int Lc, nchunks;
+    if (kSpatial) {
+        Lc = dir < 2 ? p.W : p.H;
+        nchunks = dir < 2 ? p.H : p.W;
+    } else {
+        Lc = p.chunk[dir];
+        nchunks = (p.L + Lc - 1) / Lc;
+    }
+    const int tpc = (Lc + kTile - 1) / kTile;  // steps per chunk
+    const int last_count = Lc - (tpc - 1) * kTile;
+    const int mtiles_last = (last_count + 15) >> 4;
+
+    // ---- input addressing ------------------------------------------------------------
+    const bf16* xbase;
+    const bf16* qbase;
+    int64_t xts, qts;
+    float* obase = nullptr;
+    bf16* ybase = nullptr;
+    if constexpr (kSpatial) {
+        xbase = static_cast<const bf16*>(p.x) + ro.b * p.xb + ro.head * p.xh + (p.remap ? 0 : dir * p.xd);
+        qbase = static_cast<const bf16*>(p.q) + ro.b * p.qb + ro.head * p.qh + (p.remap ? 0 : dir * p.qd);
+        xts = p.xt;
+        qts = p.qt;
+        obase = ro.plane + ro.b * p.ob + ro.head * kD + 2 * qt;
+    } else {
+        const int64_t chain = ((int64_t)ro.b * p.R + dir) * p.heads + ro.head;
+        xbase = static_cast<const bf16*>(p.x) + chain * p.L * kD;
+        qbase = static_cast<const bf16*>(p.q) + ((int64_t)ro.b * p.R + dir) * p.L * p.C + ro.head * kD;
+        xts = kD;
+        qts = p.C;
+        ybase = static_cast<bf16*>(p.y) + chain * p.L * kD + 2 * qt;
+    }
+    // Source index (token or pixel) of token `tin` of chunk `c`.
+    auto src_of = [&](int c, int tin) -> int64_t {
+        if (kSpatial && p.remap) return scan_pixel(dir, c, tin, p.H, p.W);
+        return (int64_t)c * Lc + tin;
+    };
+
+    // A fragments of one step: [mtile][h: row qg / qg+8][lo/hi channel group]
+    uint32_t axn[2][2][2], aqn[2][2][2];
+    auto prefetch = [&](int c, int j) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tin = j * kTile + mt * 16 + qg + 8 * h;
+                const int64_t t = (int64_t)c * Lc + tin;
+                if (tin < Lc && t < p.L) {
+                    const int64_t s = src_of(c, tin);
+                    const bf16* xr = xbase + s * xts + 2 * qt;
+                    const bf16* qr = qbase + s * qts + 2 * qt;
+                    axn[mt][h][0] = __ldg(reinterpret_cast<const uint32_t*>(xr));
+                    axn[mt][h][1] = __ldg(reinterpret_cast<const uint32_t*>(xr + 8));
+                    aqn[mt][h][0] = __ldg(reinterpret_cast<const uint32_t*>(qr));
+                    aqn[mt][h][1] = __ldg(reinterpret_cast<const uint32_t*>(qr + 8));
+                } else {  // tail padding reads as zeros (models/srnl_core/chunk.py:202-206)
+                    axn[mt][h][0] = axn[mt][h][1] = aqn[mt][h][0] = aqn[mt][h][1] = 0u;
+                }
+            }
+    };
+    prefetch(0, 0);
+
+    const int p2_row = lane & 15, p2_half = lane >> 4;
+    float g8[8];
+
+    for (int c = 0; c < nchunks; ++c) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g8[i] = (p2_half * 8 + i == p2_row) ? 1.f : 0.f;
+        for (int j = 0; j < tpc; ++j) {
+            const int count = j + 1 < tpc ? kTile : last_count;
+            const int mtiles = j + 1 < tpc ? 2 : mtiles_last;
+            uint32_t ax[2][2][2], aq[2][2][2];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        ax[mt][h][k] = axn[mt][h][k];
+                        aq[mt][h][k] = aqn[mt][h][k];
+                    }
+            if (j + 1 < tpc) prefetch(c, j + 1);
+            else if (c + 1 < nchunks) prefetch(c + 1, 0);
+
+            // ---------------------------- P1: projections -------------------------------
+            float2 olo[2][2], ohi[2][2];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                olo[mt][0] = olo[mt][1] = ohi[mt][0] = ohi[mt][1] = make_float2(0.f, 0.f);
+                if (mt >= mtiles) break;  // warp-uniform
+                float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {};
+                const uint32_t A_x[4] = {ax[mt][0][0], ax[mt][1][0], ax[mt][0][1], ax[mt][1][1]};
+                const uint32_t A_q[4] = {aq[mt][0][0], aq[mt][1][0], aq[mt][0][1], aq[mt][1][1]};
+                const int brow = (lane & 7) + ((lane >> 4) << 3), bhalf = (lane >> 3) & 1;
+#pragma unroll
+                for (int k = 0; k < kSplits; ++k) {
+                    uint32_t bm[4], bv[4], bk[4];
+                    ldsm_x4(bm, &cs.mb[k][0][0] + swz(brow, bhalf));
+                    ldsm_x4(bv, &cs.mb[k][0][0] + swz(16 + brow, bhalf));
+                    ldsm_x4(bk, &cs.mb[k][0][0] + swz(32 + brow, bhalf));
+                    mma_16816(cy[0], A_q, bm[0], bm[1]);
+                    mma_16816(cy[1], A_q, bm[2], bm[3]);
+                    mma_16816(cv[0], A_x, bv[0], bv[1]);
+                    mma_16816(cv[1], A_x, bv[2], bv[3]);
+                    mma_16816(ck[0], A_x, bk[0], bk[1]);
+                    mma_16816(ck[1], A_x, bk[2], bk[3]);
+                }
+                const float2 e_lo = *reinterpret_cast<const float2*>(&cs.ea[0][2 * qt]);
+                const float2 e_hi = *reinterpret_cast<const float2*>(&cs.ea[0][8 + 2 * qt]);
+                const float2 a_lo = *reinterpret_cast<const float2*>(&cs.ea[1][2 * qt]);
+                const float2 a_hi = *reinterpret_cast<const float2*>(&cs.ea[1][8 + 2 * qt]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    // Lane (qg, qt) holds channels {2qt, 2qt+1, 8+2qt, 9+2qt} of token row qg + 8h.
+                    const int row = mt * 16 + qg + 8 * h;
+                    const float2 x01 = bf2_to_f2(ax[mt][h][0]), x23 = bf2_to_f2(ax[mt][h][1]);
+                    const float2 q01 = bf2_to_f2(aq[mt][h][0]), q23 = bf2_to_f2(aq[mt][h][1]);
+                    *reinterpret_cast<float2*>(&cs.kt[row][2 * qt]) = make_float2(ck[0][2 * h], ck[0][2 * h + 1]);
+                    *reinterpret_cast<float2*>(&cs.kt[row][8 + 2 * qt]) = make_float2(ck[1][2 * h], ck[1][2 * h + 1]);
+                    *reinterpret_cast<float2*>(&cs.dt[row][2 * qt]) = make_float2(cv[0][2 * h], cv[0][2 * h + 1]);
+                    *reinterpret_cast<float2*>(&cs.dt[row][8 + 2 * qt]) = make_float2(cv[1][2 * h], cv[1][2 * h + 1]);
+                    float qs = q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y;
+                    float ep = x01.x * e_lo.x + x01.y * e_lo.y + x23.x * e_hi.x + x23.y * e_hi.y;
+                    float ap = x01.x * a_lo.x + x01.y * a_lo.y + x23.x * a_hi.x + x23.y * a_hi.y;
+                    qs = quad_sum(qs);
+                    ep = quad_sum(ep);
+                    ap = quad_sum(ap);
+                    if (qt == 0) *reinterpret_cast<float2*>(&cs.gate[row]) = make_float2(ep, ap);
+                    const float qinv = 1.f / fmaxf(sqrtf(qs), 1e-12f);
+                    const float y0 = cy[0][2 * h] * qinv, y1 = cy[0][2 * h + 1] * qinv;
+                    const float y2 = cy[1][2 * h] * qinv, y3 = cy[1][2 * h + 1] * qinv;
+                    if constexpr (kSpatial) {
+                        olo[mt][h] = make_float2(wlo[0] * (y0 + slo[0] * x01.x), wlo[1] * (y1 + slo[1] * x01.y));
+                        ohi[mt][h] = make_float2(whi[0] * (y2 + shi[0] * x23.x), whi[1] * (y3 + shi[1] * x23.y));
+                    } else {
+                        const int64_t t = (int64_t)c * Lc + j * kTile + row;
+                        if (row < count && t < p.L) {
+                            bf16* yo = ybase + t * kD;
+                            *reinterpret_cast<uint32_t*>(yo) = pack_bf2(y0, y1);
+                            *reinterpret_cast<uint32_t*>(yo + 8) = pack_bf2(y2, y3);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+
+            // ------------------ P1: per-token gates (one lane per token) ---------------------
+            float kr[kD];
+            if (lane < count) {
+                float vv[kD];
+#pragma unroll
+                for (int i = 0; i < kD; i += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane][i]);
+                    const float4 v4 = *reinterpret_cast<const float4*>(&cs.dt[lane][i]);
+                    kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
+                    vv[i] = v4.x; vv[i + 1] = v4.y; vv[i + 2] = v4.z; vv[i + 3] = v4.w;
+                }
+                float kn = 0.f;
+#pragma unroll
+                for (int i = 0; i < kD; ++i) kn = fmaf(kr[i], kr[i], kn);
+                const float kinv = 1.f / sqrtf(kn + 1e-6f);
+                float ke = 0.f, dn2 = 0.f;
+#pragma unroll
+                for (int i = 0; i < kD; ++i) {
+                    const float kk = kr[i] * kinv;
+                    const float d = kk - vv[i];
+                    kr[i] = kk;
+                    vv[i] = d;
+                    ke = fmaf(kk, kk, ke);
+                    dn2 = fmaf(d, d, dn2);
+                }
+#pragma unroll
+                for (int i = 0; i < kD; i += 4) {
+                    *reinterpret_cast<float4*>(&cs.kt[lane][i]) = make_float4(kr[i], kr[i + 1], kr[i + 2], kr[i + 3]);
+                    *reinterpret_cast<float4*>(&cs.dt[lane][i]) = make_float4(vv[i], vv[i + 1], vv[i + 2], vv[i + 3]);
+                }
+                const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[lane]);
+                const float ep = fminf(10.f, fmaxf(-10.f, raw.x));
+                const float ap = fminf(10.f, fmaxf(-10.f, raw.y + p.k.retention_bias));
+                const float eta = p.k.step_scale * softplus_f(ep);
+                const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
+                const float dn = sqrtf(dn2 + 1e-12f);
+                const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
+                float eff = cap * (-expm1f(-(eta / cap)));
+                if (p.k.spectral_clamp) {
+                    const float lim = nextafterf(p.k.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f);
+                    eff = fminf(eff, lim);
+                }
+                *reinterpret_cast<float2*>(&cs.gate[lane]) = make_float2(eff, alpha);
+            }
+            __syncwarp();
+            if (lane + 1 < count) {  // k_t . k_{t+1} for the lookahead of the gain recurrence
+                float kk = 0.f;
+#pragma unroll
+                for (int i = 0; i < kD; i += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane + 1][i]);
+                    kk = fmaf(kr[i], k4.x, kk);
+                    kk = fmaf(kr[i + 1], k4.y, kk);
+                    kk = fmaf(kr[i + 2], k4.z, kk);
+                    kk = fmaf(kr[i + 3], k4.w, kk);
+                }
+                cs.gate[lane].z = kk;
+            }
+
+            // ------------- spatial output: pixels, and read-backs of a partner's value ---------
+            int pix[2][2] = {{0, 0}, {0, 0}};
+            unsigned live = 0, rmw = 0, defer = 0;
+            float2 plo[2][2], phi[2][2];
+            if constexpr (kSpatial) {
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        plo[mt][h] = phi[mt][h] = make_float2(0.f, 0.f);
+                        const int row = mt * 16 + qg + 8 * h;
+                        if (row >= count) continue;
+                        const int tin = j * kTile + row;
+                        // The pair's partner visits this pixel at chunk nchunks-1-c, token Lc-1-tin.
+                        const int pc = nchunks - 1 - c, pj = (Lc - 1 - tin) / kTile;
+                        const bool coincident = pc == c && pj == j;
+                        const bool partner_later = pc > c || (pc == c && pj > j);
+                        const unsigned bit = 1u << (2 * mt + h);
+                        pix[mt][h] = scan_pixel(dir, c, tin, p.H, p.W);
+                        live |= bit;
+                        if (coincident && (dir & 1)) {
+                            defer |= bit;
+                        } else if (!(ro.store_first && (coincident || partner_later))) {
+                            rmw |= bit;
+                            const float* op = obase + (int64_t)pix[mt][h] * p.C;
+                            plo[mt][h] = *reinterpret_cast<const float2*>(op);
+                            phi[mt][h] = *reinterpret_cast<const float2*>(op + 8);
+                        }
+                    }
+            }
+            __syncwarp();
+
+            // ------------------ P2: gain recurrence ---------------------------------------------
+            if (count == kTile) gain_pass<kTile>(cs, count, p2_row, p2_half, g8);
+            else gain_pass<0>(cs, count, p2_row, p2_half, g8);
+
+            if constexpr (kSpatial) {
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const unsigned bit = 1u << (2 * mt + h);
+                        if (!(live & bit) || (defer & bit)) continue;
+                        float* op = obase + (int64_t)pix[mt][h] * p.C;
+                        const bool add = rmw & bit;
+                        *reinterpret_cast<float2*>(op) = add ? add2(plo[mt][h], olo[mt][h]) : olo[mt][h];
+                        *reinterpret_cast<float2*>(op + 8) = add ? add2(phi[mt][h], ohi[mt][h]) : ohi[mt][h];
+                    }
+                // Pair lockstep: every write of this step lands before either scan moves on; a
+                // pixel both scans touch in this step is then added by the odd scan.
+                pair_barrier(ro.bar);
+                if (defer) {
+#pragma unroll
+                    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            if (defer & (1u << (2 * mt + h))) {
+                                float* op = obase + (int64_t)pix[mt][h] * p.C;
+                                const float2 a = *reinterpret_cast<const float2*>(op);
+                                const float2 b = *reinterpret_cast<const float2*>(op + 8);
+                                *reinterpret_cast<float2*>(op) = add2(a, olo[mt][h]);
+                                *reinterpret_cast<float2*>(op + 8) = add2(b, ohi[mt][h]);
+                            }
+                }
+            }
+            __syncwarp();  // P1 of the next step overwrites kt/dt/gate
+        }
+
+        if (c + 1 == nchunks) break;
+        // ------------------ P3: S <- S G on tensor cores ------------------------------------
+        {
+            uint32_t gp[kSplits][2][2];  // this lane's G row segment, split (8 values = 4 pairs)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint32_t parts[kSplits];
+                split3(g8[2 * i], g8[2 * i + 1], parts);
+#pragma unroll
+                for (int k = 0; k < kSplits; ++k) gp[k][i >> 1][i & 1] = parts[k];
+            }
+#pragma unroll
+            for (int k = 0; k < kSplits; ++k)
+                *reinterpret_cast<uint4*>(&cs.gs[k][0][0] + swz(p2_row, p2_half)) =
+                    make_uint4(gp[k][0][0], gp[k][0][1], gp[k][1][0], gp[k][1][1]);
+            __syncwarp();
+            uint32_t bg[kSplits][4];
+#pragma unroll
+            for (int k = 0; k < kSplits; ++k) ldsm_x4_trans(bg[k], &cs.gs[k][0][0] + swz(lane & 15, lane >> 4));
+            // Products kept: (A part, G part) in {(0,0),(0,1),(1,0),(0,2),(2,0),(1,1)}.
+            constexpr int kPa[6] = {0, 0, 1, 0, 2, 1};
+            constexpr int kPg[6] = {0, 1, 0, 2, 0, 1};
+            float acc[4][2][4] = {};
+#pragma unroll
+            for (int mt = 0; mt < 3; ++mt) {
+                uint32_t am[kSplits][4];
+#pragma unroll
+                for (int k = 0; k < kSplits; ++k)
+                    ldsm_x4(am[k], &cs.mb[k][0][0] + swz(mt * 16 + (lane & 15), lane >> 4));
+#pragma unroll
+                for (int q = 0; q < 6; ++q) {
+                    mma_16816(acc[mt][0], am[kPa[q]], bg[kPg[q]][0], bg[kPg[q]][1]);
+                    mma_16816(acc[mt][1], am[kPa[q]], bg[kPg[q]][2], bg[kPg[q]][3]);
+                }
+            }
+            {  // e and a: rows 0 and 1 of a fourth tile, split in registers
+                uint32_t ae[kSplits][4] = {};
+                if (qg < 2) {
+                    uint32_t lo[kSplits], hi[kSplits];
+                    split3(cs.ea[qg][2 * qt], cs.ea[qg][2 * qt + 1], lo);
+                    split3(cs.ea[qg][8 + 2 * qt], cs.ea[qg][9 + 2 * qt], hi);
+#pragma unroll
+                    for (int k = 0; k < kSplits; ++k) {
+                        ae[k][0] = lo[k];
+                        ae[k][2] = hi[k];
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 6; ++q) {
+                    mma_16816(acc[3][0], ae[kPa[q]], bg[kPg[q]][0], bg[kPg[q]][1]);
+                    mma_16816(acc[3][1], ae[kPa[q]], bg[kPg[q]][2], bg[kPg[q]][3]);
+                }
+            }
+            __syncwarp();  // every lane has read the old memory parts
+#pragma unroll
+            for (int mt = 0; mt < 3; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = mt * 16 + qg + 8 * h;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        uint32_t parts[kSplits];
+                        split3(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1], parts);
+#pragma unroll
+                        for (int k = 0; k < kSplits; ++k)
+                            *reinterpret_cast<uint32_t*>(&cs.mb[k][0][0] + swz(r, nt) + 4 * qt) = parts[k];
+                    }
+                }
+            if (qg < 2) {
+                *reinterpret_cast<float2*>(&cs.ea[qg][2 * qt]) = make_float2(acc[3][0][0], acc[3][0][1]);
+                *reinterpret_cast<float2*>(&cs.ea[qg][8 + 2 * qt]) = make_float2(acc[3][1][0], acc[3][1][1]);
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Stores four consecutive channels of the final output in its dtype.
+__device__ __forceinline__ void store_final4(void* base, int dtype, int64_t off, float4 v) {
+    if (dtype == VH_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(base) + off) = v;
+    } else if (dtype == VH_BF16) {
+        store4(static_cast<__nv_bfloat16*>(base) + off, v);
+    } else {
+        store4(static_cast<__half*>(base) + off, v);
+    }
+}
+
+// End of a kKindBoth CTA: fold the columns plane of (b, head) into the rows plane, or write
+// the final output (sum + addend, cast).  Four loads are issued before any store.
+__device__ __forceinline__ void fold_planes(const ScanParams& p, int b, int head) {
+    constexpr int kU = 4;
+    const int n = p.H * p.W * 4;  // float4 groups of this head's 16 channels
+    float* A = p.out + b * p.ob + head * kD;
+    const float* Bp = p.aux + b * p.ob + head * kD;
+    const __nv_bfloat16* add =
+        p.addend ? static_cast<const __nv_bfloat16*>(p.addend) + b * p.ab + head * kD : nullptr;
+    for (int i0 = threadIdx.x; i0 < n; i0 += kThreads * kU) {
+        float4 s[kU];
+        int64_t off[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int i = i0 + u * kThreads;
+            off[u] = (int64_t)(i >> 2) * p.C + (i & 3) * 4;
+            s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n) {
+                const float4 a = *reinterpret_cast<const float4*>(A + off[u]);
+                const float4 c = *reinterpret_cast<const float4*>(Bp + off[u]);
+                s[u] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+                if (add) {
+                    const float4 e = load4(add + off[u]);
+                    s[u] = make_float4(s[u].x + e.x, s[u].y + e.y, s[u].z + e.z, s[u].w + e.w);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (i0 + u * kThreads >= n) break;
+            if (p.fin) store_final4(p.fin, p.fin_dtype, b * p.fb + head * kD + off[u], s[u]);
+            else *reinterpret_cast<float4*>(A + off[u]) = s[u];
+        }
+    }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 4) srnl_warp_kernel(const ScanParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5;
+    ChainSmem& cs = reinterpret_cast<ChainSmem*>(smem_raw)[warp];
+    const Role ro = warp_role<KIND>(p, warp);
+    // A scan pair is valid or invalid as a whole, so each pair barrier sees both its warps.
+    if (ro.valid) scan_chain<KIND != kKindSeq>(p, cs, ro);
+    if constexpr (KIND == kKindBoth) {
+        __syncthreads();  // both planes of this (b, head) are complete
+        fold_planes(p, ro.b, ro.head);
+    }
+}
+
+}  // namespace wpc
+}  // namespace vh

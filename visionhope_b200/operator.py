@@ -134,8 +134,12 @@ class VisionHOPEOperator(nn.Module):
         return self.direction_weights().detach().float()
 
     @on_tensor_device
-    def _forward_fast(self, x, path):
-        """Inference-only fusion, returning contiguous NHWC fp32 for the output projection."""
+    def _forward_fast(self, x, path, *, addend=None, final_dtype=None):
+        """Inference-only fusion, returning contiguous NHWC fp32 for the output projection.
+
+        On the spatial path, ``final_dtype`` makes the scan launch itself write
+        ``(final_dtype)(out + addend)`` (``addend``: NHWC in x's dtype, e.g. the block's output
+        position term) instead of the fp32 sum."""
         if torch.jit.is_tracing():
             raise RuntimeError("SRNL TorchScript tracing is unsupported; use eager or CUDA Graph inference.")
         if x.ndim != 4 or not x.is_cuda or x.shape[1] != self.dim or min(x.shape) <= 0:
@@ -149,7 +153,10 @@ class VisionHOPEOperator(nn.Module):
             if scale is not None and (scale.shape != (4, self.dim) or scale.device != x.device):
                 raise ValueError("Directional fusion weights have an invalid shape or device")
         if path == "sequence":
-            return self._sequence_forward(x, True, memories=memories).permute(0, 2, 3, 1).contiguous()
+            out = self._sequence_forward(x, True, memories=memories).permute(0, 2, 3, 1).contiguous()
+            if addend is not None:
+                out = out + addend
+            return out if final_dtype is None else out.to(final_dtype)
         from .srnl_core.fused import spatial_forward
 
         x_img = x.permute(0, 2, 3, 1)  # [B, H, W, C]; a view when x is channels-last
@@ -159,4 +166,5 @@ class VisionHOPEOperator(nn.Module):
         if q_img.dtype != x_img.dtype:
             q_img = q_img.to(x_img.dtype)
         return spatial_forward(memories, x_img, q_img, self.d_skip, self._fusion_weights(),
-                               int(height), int(width), self.head_dim, layout="image")
+                               int(height), int(width), self.head_dim, layout="image",
+                               addend=addend, final_dtype=final_dtype)

@@ -20,13 +20,18 @@ def _f32(t, device):
 
 
 def spatial_forward(states, x, q, d_skip, weights, height, width, head_dim, *, layout,
-                    out=None):
-    """Fused four-scan operator; returns fp32 [B, H, W, C].
+                    out=None, concurrent=True, addend=None, final_dtype=None):
+    """Fused four-scan operator; returns fp32 [B, H, W, C] (or final_dtype, see below).
 
     layout "scans":  x, q are the four serialized scans [B, 4, L, C].
     layout "packed": x is [B, 4, heads, L, D], q is [B, 4, L, C].
     layout "image":  x, q are one channels-last image each ([B, H, W, C] or any tensor whose
                      pixel p / channel c element sits at b*sB + p*sP + c); scans are index maps.
+    concurrent:      give the library a second fp32 plane so the row and column scans run in
+                     one launch (used where the warp-per-chain scan applies).
+    final_dtype:     return a new [B, H, W, C] tensor of this dtype holding the sum plus
+                     `addend` (x's dtype, [B, H, W, C] with unit channel stride), written by the
+                     scan launch itself when it runs concurrently; `out` is then scratch.
     """
     _lib.ensure_device(x)
     H, W, D = int(height), int(width), int(head_dim)
@@ -80,12 +85,30 @@ def spatial_forward(states, x, q, d_skip, weights, height, width, head_dim, *, l
         raise RuntimeError("direction weights must be fp32 [4, C]")
     if out is None:
         out = torch.empty((B, H, W, C), device=dev, dtype=torch.float32)
+    aux = torch.empty_like(out) if concurrent else None
+    final = None
+    if final_dtype is not None:
+        final = torch.empty((B, H, W, C), device=dev, dtype=final_dtype)
+    if addend is not None:
+        if final is None:
+            raise RuntimeError("an addend requires final_dtype")
+        if addend.dtype != x.dtype or addend.device != dev:
+            raise RuntimeError("the addend must match x's dtype and device")
+        addend = addend.reshape(B, L, C)
+        if addend.stride(2) != 1 or addend.stride(1) != C:
+            addend = addend.contiguous()
     args = _lib.VhSpatialArgs(
         _lib.memories(mems), x.data_ptr(), q.data_ptr(), *xs, *qs, _lib.dtype_code(x.dtype), remap,
         skip.data_ptr(), int(skip.numel() == 4 * C), wts.data_ptr(), out.data_ptr(),
-        out.stride(0), B, H, W, heads, D, recurrence_constants())
+        out.stride(0), B, H, W, heads, D, recurrence_constants(),
+        aux.data_ptr() if aux is not None else None,
+        addend.data_ptr() if addend is not None else None,
+        addend.stride(0) if addend is not None else 0,
+        final.data_ptr() if final is not None else None,
+        _lib.dtype_code(final_dtype) if final is not None else 0,
+        final.stride(0) if final is not None else 0)
     _lib.check(_lib.load().vh_srnl_spatial_fwd(args, _lib.stream_handle(dev)), "vh_srnl_spatial_fwd")
-    return out
+    return final if final is not None else out
 
 
 class _FusedModule:
