@@ -95,7 +95,7 @@ def cpu_reference_patches():
     def grn_forward(self, x):
         return grn_mod.grn_reference(x, self.gamma, self.beta, self.eps)
 
-    def fast(self, x, path):
+    def fast(self, x, path, *, addend=None, final_dtype=None):
         H, W = x.shape[-2:]
         seq_hw = x.flatten(2).transpose(1, 2)
         xs = self.serialize(x, seq_hw)
@@ -103,7 +103,10 @@ def cpu_reference_patches():
         out = orc.srnl_spatial([m.detach() for m in self.srnl.initial_memories], xs, q,
                                self.d_skip.detach(), self._fusion_weights(), H, W, self.head_dim,
                                use_f32=True)
-        return torch.from_numpy(out.astype(np.float32))
+        out = torch.from_numpy(out.astype(np.float32))
+        if addend is not None:
+            out = out + addend
+        return out if final_dtype is None else out.to(final_dtype)
 
     backbone.LayerNorm2d.forward = ln_forward
     grn_mod.GlobalResponseNorm.forward = grn_forward
