@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-scan", action="store_true",
                     help="time only the fused SRNL operator at the stage-1 shape (profiling aid)")
+    ap.add_argument("--only-norms", action="store_true",
+                    help="time only GRN and LayerNorm at the GRN/LN configuration's shapes")
     return ap.parse_args()
 
 
@@ -315,6 +317,51 @@ def roofline_scan(args, device, steps):
     }
 
 
+def roofline_norms(device, iters=10):
+    """GRN and LayerNorm alone at the GRN/LN configuration's shapes (channels-last
+    [128, 56, 56, 96] and [128, 7, 7, 768], fp32 and bf16 in, fp32 out): achieved HBM GB/s of
+    the algorithmic bytes (one read of x, one write of y) against the measured copy bandwidth.
+    A 256 MiB buffer is rewritten before every timed launch (outside the events)."""
+    from visionhope_b200 import _lib
+    from visionhope_b200.utils.grn_cuda import grn_forward
+    from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs")
+    flush = torch.empty(64 * 1024 * 1024, device=device)
+    g = torch.Generator(device=device).manual_seed(2)
+    rows = []
+    for (B, H, W, C) in ((128, 56, 56, 96), (128, 7, 7, 768)):
+        for dt in (torch.float32, torch.bfloat16):
+            x = torch.randn(B, H, W, C, device=device, generator=g).to(dt).permute(0, 3, 1, 2)
+            gam = torch.randn(C, device=device, generator=g) * 0.02
+            bet = torch.randn(C, device=device, generator=g) * 0.02
+            w = 1 + torch.randn(C, device=device, generator=g) * 0.02
+            xr = x.permute(0, 2, 3, 1).reshape(-1, C)
+            for name, fn in (("grn", lambda: grn_forward(x, gam, bet, 1e-6)),
+                             ("layernorm", lambda: layernorm_rows(xr, w, bet, 1e-6))):
+                for _ in range(3):
+                    fn()
+                times = []
+                n0 = _lib.launch_count
+                for _ in range(iters):
+                    flush.fill_(1.0)
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    b.synchronize()
+                    times.append(a.elapsed_time(b))
+                ms = statistics.median(times)
+                nbytes = x.numel() * (x.element_size() + 4)
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                rows.append({"kernel": name, "shape": [B, H, W, C], "dtype_in": str(dt).split(".")[-1],
+                             "dtype_out": "float32", "ms": ms, "alg_bytes": nbytes, "achieved_gbs": gbs,
+                             "launches": (_lib.launch_count - n0) // iters,
+                             "frac_of_measured_hbm": gbs / hbm if hbm else None})
+    return {"norms_roofline": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+
+
 def run_ours(args, world, rank, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -443,10 +490,12 @@ def main():
                     "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
             return
-        if args.only_scan:
+        if args.only_scan or args.only_norms:
             if rank == 0:
                 torch.cuda.set_device(local)
-                print(json.dumps(roofline_scan(args, torch.device("cuda", local), args.steps)), flush=True)
+                dev = torch.device("cuda", local)
+                res = roofline_scan(args, dev, args.steps) if args.only_scan else roofline_norms(dev, args.steps)
+                print(json.dumps(res), flush=True)
             return
         result = run_ours(args, world, rank, local)
         if rank == 0:

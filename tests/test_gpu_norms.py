@@ -53,7 +53,10 @@ def test_direction_fusion(dt, channels_last, per_dir, oracle, cuda):
 
 
 GRN_CASES = [(4, 14, 14, 96, "f32"), (3, 7, 7, 768, "bf16"), (2, 5, 3, 2048, "f16"),
-             (1, 56, 56, 32, "bf16"), (6, 1, 1, 12, "f32"), (2, 9, 9, 4100, "f32")]
+             (1, 56, 56, 32, "bf16"), (6, 1, 1, 12, "f32"), (2, 9, 9, 4100, "f32"),
+             (2, 56, 56, 256, "bf16"),   # stage-1 FFN width: a 16-CTA cluster per image
+             (2, 6, 6, 12, "bf16"),      # rows not 16-byte multiples: two-pass kernels
+             (1, 128, 128, 256, "f32")]  # image beyond any cluster's shared memory: two-pass
 
 
 @pytest.mark.parametrize("case", GRN_CASES, ids=lambda c: "x".join(map(str, c)))
@@ -87,7 +90,8 @@ def test_grn_stats_outputs(oracle, cuda):
 
 LN_CASES = [(4, 14, 14, 96, "f32"), (3, 7, 7, 768, "bf16"), (2, 56, 56, 64, "bf16"),
             (2, 5, 5, 32, "f16"), (2, 3, 3, 2048, "f32"), (2, 4, 4, 100, "f32"),
-            (1, 3, 3, 4099, "bf16"), (1, 2, 2, 30, "f32")]
+            (1, 3, 3, 4099, "bf16"), (1, 2, 2, 30, "f32"), (1, 3, 7, 64, "f32"),
+            (3, 5, 7, 256, "f32"), (1, 1, 1, 8, "bf16")]
 
 
 @pytest.mark.parametrize("case", LN_CASES, ids=lambda c: "x".join(map(str, c)))
@@ -103,3 +107,22 @@ def test_layernorm(case, oracle, cuda):
     exp = oracle.layernorm_rows(x.permute(0, 2, 3, 1).reshape(-1, C), w, b)
     assert y.dtype == torch.float32 and y.shape == (B, C, H, W)
     assert rel_err(y.permute(0, 2, 3, 1).reshape(-1, C).cpu().numpy(), exp) < 1e-5
+
+
+@pytest.mark.parametrize("out", ["bf16", "f16"])
+def test_norms_emit_half_outputs(out, oracle, cuda):
+    """GRN and LN written in a 16-bit dtype equal their fp32 result rounded once."""
+    from visionhope_b200.utils.grn_cuda import grn_forward
+    from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
+
+    gen = np.random.default_rng(11)
+    x = _dev(gen.normal(size=(2, 28, 28, 512)), cuda, torch.bfloat16).permute(0, 3, 1, 2)
+    g, b = _dev(gen.normal(0, 0.02, size=512), cuda), _dev(gen.normal(0, 0.02, size=512), cuda)
+    y32 = grn_forward(x, g, b, 1e-6)
+    y16 = grn_forward(x, g, b, 1e-6, out_dtype=DT[out])
+    assert y16.dtype == DT[out] and torch.equal(y16, y32.to(DT[out]))
+    rows = _dev(gen.normal(size=(777, 256)) * 2, cuda)
+    w, bb = _dev(gen.normal(1, 0.02, size=256), cuda), _dev(gen.normal(0, 0.02, size=256), cuda)
+    l32 = layernorm_rows(rows, w, bb, 1e-6)
+    l16 = layernorm_rows(rows, w, bb, 1e-6, out_dtype=DT[out])
+    assert l16.dtype == DT[out] and torch.equal(l16, l32.to(DT[out]))

@@ -37,6 +37,17 @@ MODEL_CONFIGS = {
 }
 
 
+def pointwise(conv, x):
+    """A 1x1 convolution of a channels-last NCHW tensor as a GEMM over its NHWC view.
+
+    The GEMM applies the bias in its epilogue; a convolution of a channels-last tensor adds
+    the bias in a separate broadcast pass.  Other layouts use the convolution itself."""
+    if x.is_cuda and x.is_contiguous(memory_format=torch.channels_last) and x.shape[1] > 1:
+        y = F.linear(x.permute(0, 2, 3, 1), conv.weight[:, :, 0, 0], conv.bias)
+        return y.permute(0, 3, 1, 2)
+    return conv(x)
+
+
 class LayerNorm2d(nn.Module):
     """LayerNorm over the channels of an NCHW tensor; fp32 output in channels-last storage.
 
@@ -94,7 +105,7 @@ class FeedForwardNetwork(nn.Module):
         self.drop = nn.Dropout(drop)
 
     def forward(self, x):
-        x = self.act(self.fc1(x))
+        x = self.act(pointwise(self.fc1, x))
         if self.use_dwconv:
             x = self.dwconv_act(x + self.dwconv(x))
         ac = _autocast_dtype()
@@ -105,7 +116,7 @@ class FeedForwardNetwork(nn.Module):
             x = grn_forward(x, self.grn.gamma, self.grn.beta, self.grn.eps, out_dtype=ac)
         else:
             x = self.grn(x)
-        return self.drop(self.fc2(self.drop(x)))
+        return self.drop(pointwise(self.fc2, self.drop(x)))
 
 
 class PatchEmbedding(nn.Module):
@@ -186,9 +197,9 @@ class VisionHOPEBlock(nn.Module):
             self.gamma2 = None
 
     def _local_features(self, x):
-        inner = self.proj_in(x)
+        inner = pointwise(self.proj_in, x)
         if self.local_mode == "gated_dwconv7":
-            return inner + torch.sigmoid(self.local_gate(inner)) * self.local_conv(inner)
+            return inner + torch.sigmoid(pointwise(self.local_gate, inner)) * self.local_conv(inner)
         conv = self.local_act(self.local_conv(inner))
         return conv if self.local_mode == "silu_dwconv" else inner + conv
 

@@ -55,6 +55,53 @@ __device__ __forceinline__ void store4(__half* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = u;
 }
 
+// Load / store 8 consecutive elements as floats (16-byte aligned).
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename H2>
+__device__ __forceinline__ float2 h2_to_f2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 h2_to_f2<__nv_bfloat162>(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+template <>
+__device__ __forceinline__ float2 h2_to_f2<__half2>(uint32_t u) {
+    return __half22float2(*reinterpret_cast<__half2*>(&u));
+}
+template <typename H2>
+__device__ __forceinline__ void load8_h(const void* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const float2 a = h2_to_f2<H2>(u.x), b = h2_to_f2<H2>(u.y), c = h2_to_f2<H2>(u.z), d = h2_to_f2<H2>(u.w);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) { load8_h<__nv_bfloat162>(p, v); }
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) { load8_h<__half2>(p, v); }
+
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162 h;
+    h = __floats2bfloat162_rn(v[0], v[1]); u.x = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2bfloat162_rn(v[2], v[3]); u.y = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2bfloat162_rn(v[4], v[5]); u.z = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2bfloat162_rn(v[6], v[7]); u.w = *reinterpret_cast<uint32_t*>(&h);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
+    uint4 u;
+    __half2 h;
+    h = __floats2half2_rn(v[0], v[1]); u.x = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[2], v[3]); u.y = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[4], v[5]); u.z = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[6], v[7]); u.w = *reinterpret_cast<uint32_t*>(&h);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
 // ---- asynchronous global -> shared copies (LDGSTS) ---------------------------------------
 template <int BYTES>
 __device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {

@@ -2,6 +2,8 @@
 // Both are HBM-bound: every load/store is a 4-channel vector and grids cover all SMs.
 #include <algorithm>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "abi_util.h"
 #include "common.cuh"
@@ -113,6 +115,143 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
     }
 }
 
+// ============ GRN in one read: a thread-block cluster per image (grn_cuda.cu:46-124) ============
+// The K CTAs of image b each copy a contiguous slice of its pixels (all channels) into shared
+// memory with asynchronous 16-byte copies, sum x^2 per channel over the slice, and read the K
+// partial sums of every channel from the cluster's shared memory.  Each CTA then forms
+// Gx = sqrt(sum), inv_den = 1 / (mean_c Gx + eps) and f[c] = 1 + gamma[c] Gx[c] inv_den, and
+// writes y = x f[c] + beta[c] from its resident slice: x is read from HBM once.
+constexpr int kGrnClusterMax = 16;
+
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(r));
+    return r;
+}
+// Reads a float at the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(a), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// Shared memory: part[C], fac[C], beta[C], red[4 * kGrnThreads], scratch[32], then the slice.
+__host__ __device__ inline size_t grn_cluster_head_bytes(int C) {
+    return ((size_t)3 * C * 4 + 4 * kGrnThreads * 4 + 32 * 4 + 15) & ~size_t(15);
+}
+
+template <typename T, typename YT>
+__global__ void __launch_bounds__(kGrnThreads) grn_cluster_kernel(
+    const T* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+    YT* __restrict__ y, float* __restrict__ gx_out, float* __restrict__ inv_out, int C, int S) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* part = reinterpret_cast<float*>(smem);
+    float* fac = part + C;
+    float* bet = fac + C;
+    float* red = bet + C;
+    float* scratch = red + 4 * kGrnThreads;
+    T* xs = reinterpret_cast<T*>(smem + grn_cluster_head_bytes(C));
+    const uint32_t K = cluster_size(), rank = cluster_rank();
+    const int b = blockIdx.y, tid = threadIdx.x;
+    const int s0 = (int)((int64_t)S * rank / K), s1 = (int)((int64_t)S * (rank + 1) / K);
+    const int rows = s1 - s0;
+
+    // 1. the slice [s0, s1) x C is contiguous: asynchronous 16-byte copies, all in flight.
+    {
+        const char* src = reinterpret_cast<const char*>(x + ((int64_t)b * S + s0) * C);
+        char* dst = reinterpret_cast<char*>(xs);
+        const int nvec = (int)((int64_t)rows * C * (int)sizeof(T) / 16);
+        for (int i = tid; i < nvec; i += kGrnThreads) cp_async<16>(dst + 16 * (size_t)i, src + 16 * (size_t)i);
+        cp_async_commit();
+    }
+    for (int c = tid; c < C; c += kGrnThreads) bet[c] = beta[c];
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // 2. per-channel sums of squares over the slice; thread (qi, ri) owns channel quad qi and
+    //    the pixel phase ri (rph phases).
+    const int Q = C / 4;
+    for (int q0 = 0; q0 < Q; q0 += kGrnThreads) {
+        const int qn = min(Q - q0, kGrnThreads), rph = kGrnThreads / qn;
+        const int qi = tid % qn, ri = tid / qn;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ri < rph) {
+            for (int r = ri; r < rows; r += rph) {
+                const float4 v = load4(xs + (size_t)r * C + 4 * (q0 + qi));
+                acc.x = fmaf(v.x, v.x, acc.x);
+                acc.y = fmaf(v.y, v.y, acc.y);
+                acc.z = fmaf(v.z, v.z, acc.z);
+                acc.w = fmaf(v.w, v.w, acc.w);
+            }
+            *reinterpret_cast<float4*>(red + 4 * (ri * qn + qi)) = acc;
+        }
+        __syncthreads();
+        for (int it = tid; it < qn * 4; it += kGrnThreads) {
+            float sum = 0.f;
+            for (int k = 0; k < rph; ++k) sum += red[k * qn * 4 + it];
+            part[q0 * 4 + it] = sum;
+        }
+        __syncthreads();
+    }
+
+    // 3. exchange the partial sums across the cluster.
+    cluster_arrive();
+    cluster_wait();
+    float local = 0.f;
+    for (int c = tid; c < C; c += kGrnThreads) {
+        float sum = 0.f;
+        for (uint32_t k = 0; k < K; ++k) sum += ld_cluster_f32(part + c, k);
+        const float g = sqrtf(sum);
+        fac[c] = g;
+        local += g;
+    }
+    cluster_arrive();  // this CTA has finished reading the others' partial sums
+    local = warp_sum(local);
+    if ((tid & 31) == 0) scratch[tid >> 5] = local;
+    __syncthreads();
+    if (tid < 32) {
+        float v = tid < kGrnThreads / 32 ? scratch[tid] : 0.f;
+        v = warp_sum(v);
+        if (tid == 0) scratch[0] = 1.f / (v / (float)C + eps);
+    }
+    __syncthreads();
+    const float inv_den = scratch[0];
+    for (int c = tid; c < C; c += kGrnThreads) {
+        const float g = fac[c];
+        if (rank == 0 && gx_out) gx_out[(int64_t)b * C + c] = g;
+        fac[c] = 1.f + gamma[c] * (g * inv_den);
+    }
+    if (rank == 0 && inv_out && tid == 0) inv_out[b] = inv_den;
+    __syncthreads();
+
+    // 4. y = x f + beta from the resident slice.
+    YT* dst = y + ((int64_t)b * S + s0) * C;
+    for (int q0 = 0; q0 < Q; q0 += kGrnThreads) {
+        const int qn = min(Q - q0, kGrnThreads), rph = kGrnThreads / qn;
+        const int qi = tid % qn, ri = tid / qn;
+        if (ri >= rph) continue;
+        const int c = 4 * (q0 + qi);
+        const float4 f = *reinterpret_cast<const float4*>(fac + c);
+        const float4 be = *reinterpret_cast<const float4*>(bet + c);
+        for (int r = ri; r < rows; r += rph) {
+            const float4 v = load4(xs + (size_t)r * C + c);
+            store4(dst + (size_t)r * C + c,
+                   make_float4(fmaf(v.x, f.x, be.x), fmaf(v.y, f.y, be.y), fmaf(v.z, f.z, be.z), fmaf(v.w, f.w, be.w)));
+        }
+    }
+    cluster_wait();  // no CTA leaves while another may still read its partial sums
+}
+
 // ====================== LayerNorm over channels (layer_norm_cuda.py:31-57) ======================
 // SW lanes per row (SW in {8, 16, 32}), each lane holds NV 4-channel vectors in registers;
 // mean and biased variance by two in-register passes (the Triton kernel's order).
@@ -178,6 +317,93 @@ __global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
     }
 }
 
+// C a multiple of 8: SW lanes per row, each lane holds NV 8-channel vectors of R rows in
+// registers (all R * NV 16-byte loads are issued before any arithmetic), so enough bytes are
+// in flight per SM to run at HBM speed.  Same two in-register passes as ln_kernel.
+template <typename T, typename YT, int SW, int NV, int R>
+__global__ void __launch_bounds__(kLnThreads) ln8_kernel(const T* __restrict__ x,
+                                                         const float* __restrict__ w,
+                                                         const float* __restrict__ bias, float eps,
+                                                         YT* __restrict__ y, float* __restrict__ mean_out,
+                                                         float* __restrict__ rstd_out, int64_t rows, int C) {
+    constexpr int GPC = kLnThreads / SW;  // row groups per CTA
+    const int lane = threadIdx.x % SW, grp = threadIdx.x / SW;
+    const int64_t base = (int64_t)blockIdx.x * GPC * R + grp;
+    const int G8 = C / 8;
+    float v[R][NV][8];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t row = base + (int64_t)r * GPC;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int g = lane + k * SW;
+            if (row < rows && g < G8) {
+                load8(x + row * C + 8 * g, v[r][k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[r][k][e] = 0.f;
+            }
+        }
+    }
+    const float invC = 1.f / (float)C;
+    float mean[R], rstd[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+            s += ((v[r][k][0] + v[r][k][1]) + (v[r][k][2] + v[r][k][3])) +
+                 ((v[r][k][4] + v[r][k][5]) + (v[r][k][6] + v[r][k][7]));
+#pragma unroll
+        for (int o = SW / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o, SW);
+        mean[r] = s / (float)C;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int g = lane + k * SW;
+            if (g < G8) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float d = v[r][k][e] - mean[r];
+                    q = fmaf(d, d, q);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = SW / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o, SW);
+        rstd[r] = 1.f / sqrtf(q * invC + eps);
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int g = lane + k * SW;
+        if (g >= G8) continue;
+        float wv[8], bv[8];
+        load8(w + 8 * g, wv);
+        load8(bias + 8 * g, bv);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int64_t row = base + (int64_t)r * GPC;
+            if (row >= rows) continue;
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = (v[r][k][e] - mean[r]) * rstd[r] * wv[e] + bv[e];
+            store8(y + row * C + 8 * g, o);
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int64_t row = base + (int64_t)r * GPC;
+            if (row >= rows) continue;
+            if (mean_out) mean_out[row] = mean[r];
+            if (rstd_out) rstd_out[row] = rstd[r];
+        }
+    }
+}
+
 // Any C: one warp per row, scalar accesses, two passes over global memory.
 template <typename T, typename YT>
 __global__ void __launch_bounds__(kLnThreads) ln_generic_kernel(const T* __restrict__ x,
@@ -210,10 +436,80 @@ __global__ void __launch_bounds__(kLnThreads) ln_generic_kernel(const T* __restr
     }
 }
 
+// Cluster size for the single-read GRN, or 0 when the two-pass form must be used: the
+// smallest K <= 16 whose per-CTA slice fits 110 KB (two CTAs per SM), else 200 KB.
+template <typename T>
+int grn_cluster_plan(const void* x, int64_t S, int C, size_t* smem_out) {
+    if (S > (1 << 30) || ((size_t)C * sizeof(T)) % 16 || !aligned(x, 16)) return 0;
+    const size_t head = grn_cluster_head_bytes(C);
+    for (size_t budget : {(size_t)110 * 1024, (size_t)200 * 1024}) {
+        for (int K = 1; K <= kGrnClusterMax; ++K) {
+            const size_t smem = head + (size_t)((S + K - 1) / K) * C * sizeof(T);
+            if (smem <= budget) {
+                *smem_out = smem;
+                return K;
+            }
+        }
+    }
+    return 0;
+}
+
+// Whether a cluster of K CTAs with `smem` bytes each can be resident (queried once per shape).
+template <typename T, typename YT>
+bool grn_cluster_ok(int K, size_t smem) {
+    static std::mutex mu;
+    static std::set<std::tuple<int, int, size_t>> good, bad;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const auto key = std::make_tuple(dev, K, smem);
+    std::lock_guard<std::mutex> lock(mu);
+    if (good.count(key)) return true;
+    if (bad.count(key)) return false;
+    const void* fn = reinterpret_cast<const void*>(&grn_cluster_kernel<T, YT>);
+    bool ok = ensure_smem_attr(fn, smem);
+    if (ok && K > 8) ok = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    if (ok) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(K, 1, 1);
+        cfg.blockDim = dim3(kGrnThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = K;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
+    }
+    cudaGetLastError();  // a refused query leaves no sticky error behind
+    (ok ? good : bad).insert(key);
+    return ok;
+}
+
 template <typename T, typename YT>
 int grn_run(const void* xv, const float* gamma, const float* beta, float eps, YT* y, float* gx,
             float* inv, float* part, int B, int64_t S, int C, cudaStream_t st) {
     const T* x = static_cast<const T*>(xv);
+    size_t csmem = 0;
+    const int K = aligned(y, 8 * sizeof(YT) / 2) ? grn_cluster_plan<T>(xv, S, C, &csmem) : 0;
+    if (K > 0 && grn_cluster_ok<T, YT>(K, csmem)) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(K, B, 1);
+        cfg.blockDim = dim3(kGrnThreads, 1, 1);
+        cfg.dynamicSmemBytes = csmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = K;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, grn_cluster_kernel<T, YT>, x, gamma, beta, eps, y, gx, inv, C, (int)S);
+        return launch_status("grn (cluster)");
+    }
     const int splits = grn_splits(B, S);
     const int G = C / 4;
     const int Geff = std::min(G, kGrnThreads);
@@ -253,10 +549,31 @@ int ln_launch(const void* x, const float* w, const float* b, float eps, YT* y, f
     return launch_status("layernorm");
 }
 
+template <typename T, typename YT, int SW, int NV, int R>
+int ln8_launch(const void* x, const float* w, const float* b, float eps, YT* y, float* m, float* r,
+               int64_t rows, int C, cudaStream_t st) {
+    const int64_t rows_per_cta = (int64_t)(kLnThreads / SW) * R;
+    const int64_t blocks = (rows + rows_per_cta - 1) / rows_per_cta;
+    ln8_kernel<T, YT, SW, NV, R><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps,
+                                                                          y, m, r, rows, C);
+    return launch_status("layernorm");
+}
+
 template <typename T, typename YT>
 int ln_run(const void* x, const float* w, const float* b, float eps, YT* y, float* m, float* r,
            int64_t rows, int C, bool vec_ok, cudaStream_t st) {
     const int G = C / 4;
+    const bool vec8 = C % 8 == 0 && aligned(x, 16) && aligned(y, 16) && aligned(w, 16) && aligned(b, 16);
+    if (vec8) {
+        const int G8 = C / 8;
+        if (G8 <= 4) return ln8_launch<T, YT, 4, 1, 4>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 8) return ln8_launch<T, YT, 8, 1, 4>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 16) return ln8_launch<T, YT, 16, 1, 2>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 32) return ln8_launch<T, YT, 32, 1, 2>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 64) return ln8_launch<T, YT, 32, 2, 2>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 128) return ln8_launch<T, YT, 32, 4, 1>(x, w, b, eps, y, m, r, rows, C, st);
+        if (G8 <= 256) return ln8_launch<T, YT, 32, 8, 1>(x, w, b, eps, y, m, r, rows, C, st);
+    }
     if (vec_ok && C % 4 == 0) {
         if (G <= 8) return ln_launch<T, YT, 8, 1>(x, w, b, eps, y, m, r, rows, C, st);
         if (G <= 16) return ln_launch<T, YT, 16, 1>(x, w, b, eps, y, m, r, rows, C, st);
