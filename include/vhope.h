@@ -216,6 +216,39 @@ int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight, const 
                      float eps, void* y, int32_t y_dtype, float* mean, float* rstd, int64_t rows,
                      int32_t channels, vh_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Depthwise KxK convolution (stride 1, zero padding K/2, one filter per channel) of a
+ * channels-last image with the elementwise work that follows it in the VisionHOPE block
+ * fused into the same pass; replaces the nn.Conv2d(groups=C) calls of models/block.py
+ * (cpe :100, local_conv :57-62, local_position :78) and of the FFN's depthwise stage
+ * (models/layers.py, FeedForward), together with their bias, activation, gate and residual
+ * operations:
+ *   VH_DW_BIAS   y = conv(x) + b
+ *   VH_DW_RESID  y = x + (conv(x) + b)
+ *   VH_DW_GATE   y = x + sigmoid(gate) * (conv(x) + b)
+ *   VH_DW_GELU   h = gelu(x);  y = gelu(h + conv(h) + b)      (gelu: exact erf form)
+ * x, gate, y: dense [B, H, W, C] of `dtype` (VH_F32 or VH_BF16), 16-byte aligned, y distinct
+ * from the inputs; weight fp32 [C, K, K] (nn.Conv2d's [C, 1, K, K]); bias fp32 [C];
+ * C a multiple of 8.  The convolution reads input, weight and bias rounded to bf16 and sums in
+ * fp32 (a bf16 convolution under autocast); the residual and gate terms use x and gate as
+ * given; y is rounded once.
+ * -------------------------------------------------------------------------------------*/
+enum vh_dw_mode { VH_DW_BIAS = 0, VH_DW_RESID = 1, VH_DW_GATE = 2, VH_DW_GELU = 3 };
+
+typedef struct {
+    const void* x;
+    const void* gate;
+    const float* weight;
+    const float* bias;
+    void* y;
+    int32_t dtype;
+    int32_t mode;
+    int32_t ksize;
+    int32_t batch, height, width, channels;
+} vh_dwconv_args;
+
+int vh_dwconv_fwd(const vh_dwconv_args* args, vh_stream_t stream);
+
 /* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
  * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it
  * to measure the device's FP32 (non-tensor) FMA peak. */

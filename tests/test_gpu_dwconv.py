@@ -1,0 +1,97 @@
+"""GPU parity of the fused depthwise convolutions (vh_dwconv_fwd) against a float64 PyTorch
+statement of the same arithmetic: convolution of the bf16-rounded input with bf16-rounded
+weights and bias, the mode's epilogue, one rounding to the output dtype.  Tolerances: bf16
+outputs within 4e-3 normwise (one bf16 rounding is <= 2^-9 relative), fp32 outputs 1e-5.
+The GELU mode rounds its intermediate gelu(x) to bf16 (the dtype autocast gives it); the
+kernel's erf (within 1.5e-7 of the exact one) moves that rounding for about 1 element in
+5000, each by one bf16 step, so fp32 outputs of that mode are held to 1e-3."""
+import zlib
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@torch.no_grad()
+def _expected(x, conv, mode, gate):
+    bf = lambda t: t.to(torch.bfloat16).double()
+    k = conv.kernel_size[0]
+    xin = bf(x)
+    if mode == "gelu":
+        xin = bf(F.gelu(x.double()))
+    conv_out = F.conv2d(xin, bf(conv.weight), bf(conv.bias), padding=k // 2, groups=x.shape[1])
+    if mode == "bias":
+        return conv_out
+    if mode == "resid":
+        return x.double() + conv_out
+    if mode == "gate":
+        return x.double() + torch.sigmoid(gate.double()) * conv_out
+    return F.gelu(xin + conv_out)
+
+
+CASES = [
+    # (B, C, H, W, k, mode, dtype)
+    (2, 64, 14, 14, 3, "resid", torch.float32),
+    (2, 32, 56, 56, 7, "gate", torch.bfloat16),
+    (3, 128, 14, 14, 5, "bias", torch.bfloat16),
+    (2, 256, 7, 7, 3, "gelu", torch.bfloat16),
+    (1, 40, 9, 13, 7, "gate", torch.bfloat16),    # channels not a multiple of 32, odd sizes
+    (1, 8, 1, 17, 5, "bias", torch.float32),      # one row
+    (2, 96, 23, 5, 3, "gelu", torch.float32),
+    (1, 64, 33, 31, 7, "resid", torch.bfloat16),  # several 16 x 16 tiles with ragged edges
+    (1, 512, 28, 28, 3, "gelu", torch.bfloat16),
+    (1, 16, 16, 32, 5, "resid", torch.bfloat16),  # 16 x 16 tiles
+    (2, 64, 28, 42, 7, "bias", torch.bfloat16),   # 14 x 14 tiles, several per image
+    (1, 8, 7, 7, 7, "gate", torch.float32),       # kernel wider than half the image
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(str(v).replace("torch.", "") for v in c))
+def test_dwconv_matches_reference(case, cuda):
+    from visionhope_b200.utils.dwconv import depthwise_fused
+
+    B, C, H, W, k, mode, dt = case
+    torch.manual_seed(zlib.crc32(repr(case).encode()))
+    conv = torch.nn.Conv2d(C, C, k, padding=k // 2, groups=C).to(cuda)
+    with torch.no_grad():
+        conv.bias.normal_(0, 0.3)
+    x = torch.randn(B, C, H, W, device=cuda).to(dt).contiguous(memory_format=torch.channels_last)
+    gate = torch.randn_like(x) if mode == "gate" else None
+    with torch.inference_mode():
+        y = depthwise_fused(x, conv, mode, gate=gate)
+    assert y.dtype == dt and y.shape == x.shape and y.is_contiguous(memory_format=torch.channels_last)
+    exp = _expected(x, conv, mode, gate)
+    tol = 4e-3 if dt == torch.bfloat16 else (1e-3 if mode == "gelu" else 1e-5)
+    assert rel_err(y.float().cpu().numpy(), exp.cpu().numpy()) < tol
+
+
+def test_dwconv_fusable_rules(cuda):
+    from visionhope_b200.utils.dwconv import fusable
+
+    conv = torch.nn.Conv2d(16, 16, 3, padding=1, groups=16).to(cuda)
+    x = torch.randn(1, 16, 8, 8, device=cuda).contiguous(memory_format=torch.channels_last)
+    with torch.inference_mode():
+        assert not fusable(x, conv)  # no autocast: fp32 convolution arithmetic stays with PyTorch
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            assert fusable(x, conv)
+            assert not fusable(x.contiguous(), conv)
+            assert not fusable(x, torch.nn.Conv2d(16, 16, 3, padding=1, groups=16, bias=False).to(cuda))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        assert not fusable(x, conv)  # autograd on
+
+
+def test_dwconv_rejects_bad_arguments(cuda):
+    from visionhope_b200.utils.dwconv import depthwise_fused
+
+    conv = torch.nn.Conv2d(12, 12, 3, padding=1, groups=12).to(cuda)
+    x = torch.randn(1, 12, 8, 8, device=cuda).contiguous(memory_format=torch.channels_last)
+    with pytest.raises(RuntimeError, match="multiple of 8"):
+        depthwise_fused(x, conv, "bias")
+    conv = torch.nn.Conv2d(16, 16, 3, padding=1, groups=16).to(cuda)
+    x = torch.randn(1, 16, 8, 8, device=cuda).contiguous(memory_format=torch.channels_last)
+    with pytest.raises(RuntimeError, match="gate"):
+        depthwise_fused(x, conv, "gate")

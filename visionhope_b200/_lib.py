@@ -55,6 +55,12 @@ class VhSequenceArgs(ctypes.Structure):
                 ("head_dim", c_int32), ("chunk", c_int32 * 4), ("consts", VhConsts)]
 
 
+class VhDwconvArgs(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("gate", c_void_p), ("weight", c_void_p), ("bias", c_void_p),
+                ("y", c_void_p), ("dtype", c_int32), ("mode", c_int32), ("ksize", c_int32),
+                ("batch", c_int32), ("height", c_int32), ("width", c_int32), ("channels", c_int32)]
+
+
 _lib = None
 _lock = threading.Lock()
 _inited = set()
@@ -92,6 +98,8 @@ def load() -> ctypes.CDLL:
                                              c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_int32,
                                              c_void_p]
             lib.vh_init.argtypes = [c_int32]
+            lib.vh_dwconv_fwd.restype = c_int32
+            lib.vh_dwconv_fwd.argtypes = [ctypes.POINTER(VhDwconvArgs), c_void_p]
             lib.vh_last_launch_count.restype = c_int32
             lib.vh_last_launch_count.argtypes = []
             lib.vh_probe_ffma.restype = c_int32

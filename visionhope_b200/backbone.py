@@ -19,6 +19,7 @@ from torch.nn import functional as F
 from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
+from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_forward
 from .utils.layer_norm_cuda import layernorm_rows
 
@@ -46,6 +47,10 @@ def pointwise(conv, x):
         y = F.linear(x.permute(0, 2, 3, 1), conv.weight[:, :, 0, 0], conv.bias)
         return y.permute(0, 3, 1, 2)
     return conv(x)
+
+
+def _is_exact_gelu(m):
+    return isinstance(m, nn.GELU) and m.approximate == "none"
 
 
 class LayerNorm2d(nn.Module):
@@ -105,9 +110,15 @@ class FeedForwardNetwork(nn.Module):
         self.drop = nn.Dropout(drop)
 
     def forward(self, x):
-        x = self.act(pointwise(self.fc1, x))
-        if self.use_dwconv:
-            x = self.dwconv_act(x + self.dwconv(x))
+        x = pointwise(self.fc1, x)
+        if (self.use_dwconv and _is_exact_gelu(self.act) and _is_exact_gelu(self.dwconv_act)
+                and fusable(x, self.dwconv)):
+            # gelu(fc1), the depthwise convolution, its residual and the second gelu in one pass
+            x = depthwise_fused(x, self.dwconv, "gelu")
+        else:
+            x = self.act(x)
+            if self.use_dwconv:
+                x = self.dwconv_act(x + self.dwconv(x))
         ac = _autocast_dtype()
         if isinstance(self.grn, GlobalResponseNorm) and ac in (torch.bfloat16, torch.float16) and x.is_cuda:
             # fc2 runs under autocast and casts GRN's fp32 output to `ac`; emit it directly.
@@ -199,7 +210,10 @@ class VisionHOPEBlock(nn.Module):
     def _local_features(self, x):
         inner = pointwise(self.proj_in, x)
         if self.local_mode == "gated_dwconv7":
-            return inner + torch.sigmoid(pointwise(self.local_gate, inner)) * self.local_conv(inner)
+            gate = pointwise(self.local_gate, inner)
+            if fusable(inner, self.local_conv) and gate.dtype == inner.dtype:
+                return depthwise_fused(inner, self.local_conv, "gate", gate=gate)
+            return inner + torch.sigmoid(gate) * self.local_conv(inner)
         conv = self.local_act(self.local_conv(inner))
         return conv if self.local_mode == "silu_dwconv" else inner + conv
 
@@ -214,7 +228,10 @@ class VisionHOPEBlock(nn.Module):
                 # followed by autocast's cast.
                 lepe = None
                 if self.local_position is not None:
-                    lepe = self.local_position(x_local).permute(0, 2, 3, 1)
+                    if fusable(x_local, self.local_position):
+                        lepe = depthwise_fused(x_local, self.local_position, "bias").permute(0, 2, 3, 1)
+                    else:
+                        lepe = self.local_position(x_local).permute(0, 2, 3, 1)
                     if lepe.dtype != x_local.dtype:
                         lepe = lepe.to(x_local.dtype)
                 out = self.operator._forward_fast(x_local, path, addend=lepe,
@@ -238,7 +255,7 @@ class VisionHOPEBlock(nn.Module):
         if self.training and self._inference_prepared:
             raise RuntimeError("A block with folded LayerScale weights cannot be trained")
         if self.cpe is not None:
-            x = x + self.cpe(x)
+            x = depthwise_fused(x, self.cpe, "resid") if fusable(x, self.cpe) else x + self.cpe(x)
         x = self._residual(x, self.spatial_branch(self.norm1(x)), self.gamma1)
         return self._residual(x, self.ffn(self.norm2(x)), self.gamma2)
 

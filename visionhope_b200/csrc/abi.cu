@@ -64,6 +64,7 @@ bool ensure_smem_attr(const void* func, size_t bytes) {
 // Defined in the kernel translation units: set every kernel's attributes for `device`.
 int init_scan_kernels();
 int init_norm_kernels();
+int init_dw_kernels();
 
 }  // namespace vh
 
@@ -74,6 +75,7 @@ extern "C" int vh_init(int32_t device) {
         return vh::fail(VH_E_DEVICE, "vh_init: cannot select device %d", device);
     int rc = vh::init_scan_kernels();
     if (rc == 0) rc = vh::init_norm_kernels();
+    if (rc == 0) rc = vh::init_dw_kernels();
     cudaSetDevice(prev);
     return rc;
 }

@@ -1,0 +1,323 @@
+// Depthwise KxK convolutions of the VisionHOPE block with fused epilogues (sm_100a).
+//
+// The block (models/block.py) runs four depthwise convolutions per layer, each followed by
+// elementwise work that PyTorch issues as separate passes over HBM:
+//   cpe             x + (conv3x3(x) + b)                          block.py:100
+//   local features  inner + sigmoid(gate) * (conv7x7(inner) + b)  block.py:57-62
+//   output position conv5x5(x_local) + b                          block.py:78
+//   FFN             h = gelu(fc1); gelu(h + conv3x3(h) + b)        layers.py (FeedForward)
+// One kernel per call does the convolution and its epilogue.  A CTA owns a TH x TC pixel tile
+// of 32 channels: it stages the tile plus its halo in shared memory as fp32 (one read of the
+// input, the loads of a batch issued together), each thread accumulates R output rows of one
+// column for 4 channels with packed two-lane FMAs, holding the column's K weights in
+// registers so every staged input vector feeds up to K rows, and the epilogue writes each
+// output once.  Eight threads cover a pixel's 32 channels, so the 16-byte shared-memory
+// reads of a warp are contiguous and free of bank conflicts.
+//
+// Arithmetic matches a bf16 convolution under autocast: the convolution reads its input,
+// weights and bias rounded to bf16 and accumulates in fp32; residual and gate terms use the
+// input as given; the result is rounded once to the output dtype (the input dtype).  GELU is
+// the exact (erf) form, with erf from Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7, far below
+// the bf16 rounding of every GELU output here).
+#include <algorithm>
+#include <type_traits>
+
+#include "abi_util.h"
+#include "common.cuh"
+#include "f32x2.cuh"
+
+namespace vh {
+namespace {
+
+constexpr int kDwCG = 32;  // channels per CTA (a staged pixel is 32 floats)
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// gelu(x) = x/2 (1 + erf(x / sqrt 2)) for two lanes.  With a = |z|, t = 1 / (1 + p a),
+// erfc(a) ~= t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2)  (A&S 7.1.26), and
+// 1 + erf(z) = 2 - erfc(a) for z >= 0, erfc(a) for z < 0.
+__device__ __forceinline__ float2 gelu2(float2 x) {
+    constexpr float kP = 0.3275911f, kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f,
+                    kA4 = -1.453152027f, kA5 = 1.061405429f;
+    const float2 z = fmul2(x, splat2(0.70710678118654752f));
+    const float2 d = ffma2(make_float2(fabsf(z.x), fabsf(z.y)), splat2(kP), splat2(1.f));
+    const float2 t = make_float2(__fdividef(1.f, d.x), __fdividef(1.f, d.y));
+    float2 q = ffma2(t, splat2(kA5), splat2(kA4));
+    q = ffma2(q, t, splat2(kA3));
+    q = ffma2(q, t, splat2(kA2));
+    q = ffma2(q, t, splat2(kA1));
+    q = fmul2(q, t);
+    const float2 zz = fmul2(z, z);
+    const float2 c = fmul2(q, make_float2(__expf(-zz.x), __expf(-zz.y)));
+    const float2 s = make_float2(z.x >= 0.f ? 2.f - c.x : c.x, z.y >= 0.f ? 2.f - c.y : c.y);
+    return fmul2(fmul2(x, splat2(0.5f)), s);
+}
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
+
+// Eight consecutive elements held raw in registers between their load and their use.
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<float> {
+    float4 a, b;
+    __device__ __forceinline__ void load(const float* p) {
+        a = __ldg(reinterpret_cast<const float4*>(p));
+        b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    }
+    __device__ __forceinline__ void to_float(float (&f)[8]) const {
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+};
+template <>
+struct Raw8<__nv_bfloat16> {
+    uint4 u;
+    __device__ __forceinline__ void load(const __nv_bfloat16* p) { u = __ldg(reinterpret_cast<const uint4*>(p)); }
+    __device__ __forceinline__ void to_float(float (&f)[8]) const { load8(reinterpret_cast<const __nv_bfloat16*>(&u), f); }
+};
+
+// Four channels as two lane pairs.
+__device__ __forceinline__ void lds4(const float* p, float2 (&v)[2]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+}
+
+template <int K, int TC, int RG, int R>
+struct DwGeom {
+    static constexpr int TH = RG * R, P = K / 2, IH = TH + K - 1, IW = TC + K - 1, NT = 8 * TC * RG;
+    static constexpr int XS = IH * IW * kDwCG;  // floats of the staged tile
+    static constexpr size_t kSmem = sizeof(float) * ((size_t)XS + K * K * kDwCG + kDwCG);
+};
+
+template <int K, int MODE, typename T, int TC, int RG, int R>
+__global__ void __launch_bounds__(8 * TC * RG, K == 7 ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const T* __restrict__ gate,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias, T* __restrict__ y,
+                                                                int H, int W, int C, int tiles_w) {
+    using G = DwGeom<K, TC, RG, R>;
+    constexpr int TH = G::TH, P = G::P, IW = G::IW, NT = G::NT;
+    extern __shared__ __align__(16) float dw_smem[];
+    float* xs = dw_smem;                  // [IH][IW][32]
+    float* ws = dw_smem + G::XS;          // [K*K][32]
+    float* bs = ws + K * K * kDwCG;       // [32]
+    const int tid = threadIdx.x;
+    const int b = blockIdx.z, c0 = blockIdx.y * kDwCG;
+    const int oy0 = (blockIdx.x / tiles_w) * TH, ox0 = (blockIdx.x % tiles_w) * TC;
+    const int64_t img = (int64_t)b * H * W * C;
+
+    for (int i = tid; i < K * K * kDwCG; i += NT) {
+        const int tap = i / kDwCG, cc = i % kDwCG, c = c0 + cc;
+        ws[i] = c < C ? round_bf16(w[(int64_t)c * K * K + tap]) : 0.f;
+    }
+    if (tid < kDwCG) bs[tid] = c0 + tid < C ? round_bf16(bias[c0 + tid]) : 0.f;
+    // Input tile with halo, in 8-channel vectors; zero outside the image (the convolution's
+    // zero padding).  The loads of a batch are all issued before any of them is converted.
+    constexpr int NV = G::IH * IW * 4, IT = (NV + NT - 1) / NT, BATCH = 4;
+#pragma unroll
+    for (int i0 = 0; i0 < IT; i0 += BATCH) {
+        Raw8<T> raw[BATCH];
+        bool live[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+            const int i = (i0 + u) * NT + tid;
+            const int v = i & 3, pix = i >> 2;
+            const int gy = oy0 + pix / IW - P, gx = ox0 + pix % IW - P, c = c0 + 8 * v;
+            live[u] = i0 + u < IT && i < NV && gy >= 0 && gy < H && gx >= 0 && gx < W && c < C;
+            if (live[u]) raw[u].load(x + img + ((int64_t)gy * W + gx) * C + c);
+        }
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+            const int i = (i0 + u) * NT + tid;
+            if (i0 + u >= IT || i >= NV) continue;
+            float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (live[u]) {
+                raw[u].to_float(f);
+                if (MODE == VH_DW_GELU) {
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        const float2 g = gelu2(make_float2(f[e], f[e + 1]));
+                        f[e] = g.x;
+                        f[e + 1] = g.y;
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = round_bf16(f[e]);
+            }
+            float* d = xs + (i >> 2) * kDwCG + 8 * (i & 3);
+            reinterpret_cast<float4*>(d)[0] = make_float4(f[0], f[1], f[2], f[3]);
+            reinterpret_cast<float4*>(d)[1] = make_float4(f[4], f[5], f[6], f[7]);
+        }
+    }
+    __syncthreads();
+
+    const int q = tid & 7, col = (tid >> 3) % TC, r0 = ((tid >> 3) / TC) * R;
+    const int c = c0 + 4 * q, ox = ox0 + col;
+    const bool out_ok = c < C && ox < W;
+    float2 acc[R][2];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int kx = 0; kx < K; ++kx) {
+        float2 wk[K][2];
+#pragma unroll
+        for (int ky = 0; ky < K; ++ky) lds4(ws + (ky * K + kx) * kDwCG + 4 * q, wk[ky]);
+#pragma unroll
+        for (int iy = 0; iy < R + K - 1; ++iy) {
+            float2 in[2];
+            lds4(xs + ((r0 + iy) * IW + col + kx) * kDwCG + 4 * q, in);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int ky = iy - r;
+                if (ky >= 0 && ky < K) {
+                    acc[r][0] = ffma2(wk[ky][0], in[0], acc[r][0]);
+                    acc[r][1] = ffma2(wk[ky][1], in[1], acc[r][1]);
+                }
+            }
+        }
+    }
+
+    if (!out_ok) return;
+    float2 bv[2];
+    lds4(bs + 4 * q, bv);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int oy = oy0 + r0 + r;
+        if (oy >= H) break;
+        const int64_t off = img + ((int64_t)oy * W + ox) * C + c;
+        float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
+        if (MODE == VH_DW_RESID || MODE == VH_DW_GATE) {
+            // The centre value itself: from the staged tile when the input is bf16 (staged
+            // exactly), else from global memory (the tile holds it rounded to bf16).
+            float2 xc[2];
+            if (std::is_same<T, __nv_bfloat16>::value) {
+                lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, xc);
+            } else {
+                const float4 t4 = load4(x + off);
+                xc[0] = make_float2(t4.x, t4.y);
+                xc[1] = make_float2(t4.z, t4.w);
+            }
+            if (MODE == VH_DW_RESID) {
+                o[0] = fadd2(xc[0], o[0]);
+                o[1] = fadd2(xc[1], o[1]);
+            } else {
+                const float4 g = load4(gate + off);
+                o[0] = ffma2(make_float2(sigmoid_f(g.x), sigmoid_f(g.y)), o[0], xc[0]);
+                o[1] = ffma2(make_float2(sigmoid_f(g.z), sigmoid_f(g.w)), o[1], xc[1]);
+            }
+        } else if (MODE == VH_DW_GELU) {
+            float2 h[2];  // gelu(x) at the centre, as staged
+            lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, h);
+            o[0] = gelu2(fadd2(h[0], o[0]));
+            o[1] = gelu2(fadd2(h[1], o[1]));
+        }
+        store4(y + off, make_float4(o[0].x, o[0].y, o[1].x, o[1].y));
+    }
+}
+
+template <int K, int MODE, typename T, int TC, int RG, int R>
+int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
+    using G = DwGeom<K, TC, RG, R>;
+    const int tiles_w = (a.width + TC - 1) / TC, tiles_h = (a.height + G::TH - 1) / G::TH;
+    const dim3 grid(tiles_w * tiles_h, (a.channels + kDwCG - 1) / kDwCG, a.batch);
+    const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, TC, RG, R>);
+    if (!ensure_smem_attr(fn, G::kSmem))
+        return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", G::kSmem);
+    dwconv_kernel<K, MODE, T, TC, RG, R><<<grid, G::NT, G::kSmem, st>>>(
+        static_cast<const T*>(a.x), static_cast<const T*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
+        a.height, a.width, a.channels, tiles_w);
+    return launch_status("depthwise conv");
+}
+
+// Tile: the shape among 14 x 14 (224 threads, 7 rows each; divides every VisionHOPE stage
+// size from 14 up), 16 x 16 (256 threads, 8 rows each) and 8 x 8 (256 threads, 2 rows each)
+// that covers the image with the least padding, in that order of preference.
+template <int K, int MODE, typename T>
+int dw_tile(const vh_dwconv_args& a, cudaStream_t st) {
+    auto area = [&](int th, int tc) {
+        return (int64_t)((a.height + th - 1) / th) * th * (int64_t)((a.width + tc - 1) / tc) * tc;
+    };
+    const int64_t a14 = area(14, 14), a16 = area(16, 16), a8 = area(8, 8);
+    if (a14 <= a16 && a14 <= a8) return dw_launch<K, MODE, T, 14, 2, 7>(a, st);
+    if (a16 <= a8) return dw_launch<K, MODE, T, 16, 2, 8>(a, st);
+    return dw_launch<K, MODE, T, 8, 4, 2>(a, st);
+}
+
+template <int MODE, typename T>
+int dw_k(const vh_dwconv_args& a, cudaStream_t st) {
+    switch (a.ksize) {
+        case 3: return dw_tile<3, MODE, T>(a, st);
+        case 5: return dw_tile<5, MODE, T>(a, st);
+        default: return dw_tile<7, MODE, T>(a, st);
+    }
+}
+
+template <typename T>
+int dw_mode(const vh_dwconv_args& a, cudaStream_t st) {
+    switch (a.mode) {
+        case VH_DW_BIAS: return dw_k<VH_DW_BIAS, T>(a, st);
+        case VH_DW_RESID: return dw_k<VH_DW_RESID, T>(a, st);
+        case VH_DW_GATE: return dw_k<VH_DW_GATE, T>(a, st);
+        default: return dw_k<VH_DW_GELU, T>(a, st);
+    }
+}
+
+template <int K, int MODE, typename T>
+void dw_attr_k() {
+    ensure_smem_attr(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 14, 2, 7>), DwGeom<K, 14, 2, 7>::kSmem);
+    ensure_smem_attr(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 16, 2, 8>), DwGeom<K, 16, 2, 8>::kSmem);
+    ensure_smem_attr(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 8, 4, 2>), DwGeom<K, 8, 4, 2>::kSmem);
+}
+
+template <int MODE, typename T>
+void dw_attr_mode() {
+    dw_attr_k<3, MODE, T>();
+    dw_attr_k<5, MODE, T>();
+    dw_attr_k<7, MODE, T>();
+}
+
+template <typename T>
+void dw_attr_t() {
+    dw_attr_mode<VH_DW_BIAS, T>();
+    dw_attr_mode<VH_DW_RESID, T>();
+    dw_attr_mode<VH_DW_GATE, T>();
+    dw_attr_mode<VH_DW_GELU, T>();
+}
+
+}  // namespace
+
+// Shared-memory limits of every depthwise kernel on the current device (from vh_init, so a
+// first call inside a CUDA-graph capture sets no attribute).
+int init_dw_kernels() {
+    dw_attr_t<float>();
+    dw_attr_t<__nv_bfloat16>();
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(VH_E_DEVICE, "vh_init: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+}  // namespace vh
+
+using namespace vh;
+
+extern "C" int vh_dwconv_fwd(const vh_dwconv_args* a, vh_stream_t stream) {
+    clear_error();
+    if (!a) return fail(VH_E_ARG, "vh_dwconv_fwd: null args");
+    if (!a->x || !a->weight || !a->bias || !a->y || (a->mode == VH_DW_GATE && !a->gate))
+        return fail(VH_E_ARG, "vh_dwconv_fwd: null pointer argument");
+    if (a->mode < VH_DW_BIAS || a->mode > VH_DW_GELU) return fail(VH_E_ARG, "vh_dwconv_fwd: bad mode %d", a->mode);
+    if (a->ksize != 3 && a->ksize != 5 && a->ksize != 7)
+        return fail(VH_E_SHAPE, "vh_dwconv_fwd: kernel size must be 3, 5 or 7 (got %d)", a->ksize);
+    if (a->dtype != VH_F32 && a->dtype != VH_BF16)
+        return fail(VH_E_DTYPE, "vh_dwconv_fwd: dtype must be fp32 or bf16");
+    if (a->batch <= 0 || a->height <= 0 || a->width <= 0 || a->channels <= 0)
+        return fail(VH_E_SHAPE, "vh_dwconv_fwd: sizes must be positive");
+    if (a->channels % 8) return fail(VH_E_SHAPE, "vh_dwconv_fwd: channels must be a multiple of 8");
+    if (a->batch > 65535 || (int64_t)a->height * a->width > ((int64_t)1 << 30))
+        return fail(VH_E_RANGE, "vh_dwconv_fwd: sizes exceed the supported range");
+    if (!aligned(a->x, 16) || !aligned(a->y, 16) || (a->gate && !aligned(a->gate, 16)))
+        return fail(VH_E_ALIGN, "vh_dwconv_fwd: x, gate and y must be 16-byte aligned");
+    if (a->x == a->y || (a->gate && a->gate == a->y))
+        return fail(VH_E_ARG, "vh_dwconv_fwd: y must not alias the inputs");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return a->dtype == VH_F32 ? dw_mode<float>(*a, st) : dw_mode<__nv_bfloat16>(*a, st);
+}

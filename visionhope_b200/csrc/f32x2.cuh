@@ -1,0 +1,38 @@
+// Packed two-lane fp32 arithmetic of sm_100 (add/mul/fma.rn.f32x2).  Each lane is rounded
+// exactly as the scalar instruction would round it; one instruction does two lanes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vh {
+
+__device__ __forceinline__ uint64_t f2_bits(float2 v) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+    return r;
+}
+__device__ __forceinline__ float2 bits_f2(uint64_t b) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(b));
+    return v;
+}
+// a * b + c per lane
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+
+}  // namespace vh

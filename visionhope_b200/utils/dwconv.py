@@ -1,0 +1,50 @@
+"""Depthwise convolutions of the VisionHOPE block with their elementwise epilogues fused
+(``vh_dwconv_fwd``): one pass over HBM instead of a convolution, a bias pass and the
+activation / gate / residual passes that follow it in models/block.py and the FFN.
+
+Inference only (no autograd); channels-last CUDA tensors of fp32 or bf16.
+"""
+import torch
+
+from .. import _lib
+from .cuda import on_tensor_device
+
+MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3}
+
+
+def fusable(x, conv):
+    """Whether ``conv`` applied to ``x`` can run as a fused depthwise call: a depthwise
+    3/5/7 stride-1 'same' convolution with bias of a channels-last fp32/bf16 CUDA tensor whose
+    channel count is a multiple of 8, with autograd off and bf16 autocast on (the kernel's
+    arithmetic is that of a bf16 convolution)."""
+    k = conv.kernel_size[0]
+    return (x.is_cuda and x.dim() == 4 and not torch.is_grad_enabled()
+            and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+            and x.dtype in (torch.float32, torch.bfloat16)
+            and x.is_contiguous(memory_format=torch.channels_last) and x.shape[1] % 8 == 0
+            and conv.groups == conv.in_channels == conv.out_channels == x.shape[1]
+            and conv.kernel_size == (k, k) and k in (3, 5, 7) and conv.stride == (1, 1)
+            and conv.padding == (k // 2, k // 2) and conv.dilation == (1, 1) and conv.bias is not None)
+
+
+@on_tensor_device
+def depthwise_fused(x, conv, mode, gate=None):
+    """Apply depthwise ``conv`` to channels-last NCHW ``x`` with epilogue ``mode``:
+    "bias": conv(x) + b;  "resid": x + (conv(x) + b);  "gate": x + sigmoid(gate) * (conv(x) + b);
+    "gelu": h = gelu(x), gelu(h + conv(h) + b).  Returns a channels-last tensor of x's dtype."""
+    _lib.ensure_device(x)
+    B, C, H, W = x.shape
+    if mode not in MODES:
+        raise ValueError(f"unknown depthwise epilogue {mode!r}")
+    if mode == "gate":
+        if gate is None or gate.shape != x.shape or gate.dtype != x.dtype:
+            raise RuntimeError("the gated epilogue needs a gate of x's shape and dtype")
+        gate = gate.contiguous(memory_format=torch.channels_last)
+    x = x.contiguous(memory_format=torch.channels_last)
+    w = conv.weight.detach().float().contiguous()
+    b = conv.bias.detach().float().contiguous()
+    y = torch.empty_like(x, memory_format=torch.channels_last)
+    args = _lib.VhDwconvArgs(x.data_ptr(), _lib.ptr(gate), w.data_ptr(), b.data_ptr(), y.data_ptr(),
+                             _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C)
+    _lib.check(_lib.load().vh_dwconv_fwd(args, _lib.stream_handle(x.device)), "vh_dwconv_fwd")
+    return y
