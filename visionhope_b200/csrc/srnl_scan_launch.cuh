@@ -113,7 +113,7 @@ template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
     const int pairs = p.B * p.heads;
     if constexpr (mma_capable<D, T, T>()) {
-        if (p.aux && std::max(p.H, p.W) > 8) return launch_warp<kKindBoth>(p, pairs, st);
+        if (p.aux) return launch_warp<kKindBoth>(p, pairs, st);
     }
     int rc = launch_auto<D, T, T, kKindRows>(p, p.W, pairs, st);
     if (rc) return rc;

@@ -36,10 +36,15 @@
 // behind it; all of a step's writes land before the pair's barrier at the end of the step.
 #pragma once
 
+#include "f32x2.cuh"
 #include "srnl_scan.cuh"
 
 namespace vh {
 namespace wpc {
+
+#ifndef VH_WPC_MIN_BLOCKS
+#define VH_WPC_MIN_BLOCKS 4
+#endif
 
 constexpr int kD = 16;
 constexpr int kWarps = 4;
@@ -56,6 +61,7 @@ struct alignas(16) ChainSmem {
     float dt[kTile][kKP];               // raw v, then d = k - v
     float4 gate[kTile];                 // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
     unsigned char gs[kSplits][16][32];  // split gain rows (row-major, k x n)
+    float fw[2][kD];                    // spatial: this scan's fusion weight and skip per channel
 };
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const unsigned char* p) {
@@ -69,15 +75,18 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Three-way bf16 split of a pair of fp32 values: parts[k] packs (lo, hi) of part k.
+// Exact three-way bf16 split of a pair of fp32 values by truncation: part k packs (lo, hi) of
+// the top 8 significant bits left after parts 0..k-1, so x = part0 + part1 + part2 exactly.
+// A part is the upper half of an fp32 word, so one byte permute packs a pair.
 __device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSplits]) {
 #pragma unroll
     for (int k = 0; k < kSplits; ++k) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-        const float2 f = __bfloat1622float2(h);
-        lo -= f.x;
-        hi -= f.y;
-        parts[k] = *reinterpret_cast<const uint32_t*>(&h);
+        const uint32_t ul = __float_as_uint(lo), uh = __float_as_uint(hi);
+        parts[k] = __byte_perm(ul, uh, 0x7632);
+        if (k + 1 < kSplits) {
+            lo -= __uint_as_float(ul & 0xffff0000u);
+            hi -= __uint_as_float(uh & 0xffff0000u);
+        }
     }
 }
 
@@ -118,58 +127,68 @@ __device__ __forceinline__ Role warp_role(const ScanParams& p, int warp) {
 }
 
 // The gain recurrence over the `count` tokens of one step (N > 0: exactly N, unrolled).
-// Lane (row, half) holds G[row][8 half .. 8 half + 7] in g.
+// Lane (row, half) holds G[row][8 half .. 8 half + 7] in g as four column pairs; the dot
+// products and the update run as packed two-lane FMAs (lane pair (2i, 2i+1) of g[i]).
+__device__ __forceinline__ void load_key_half(const ChainSmem& cs, int t, int half, float2 (&k)[4]) {
+    const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[t][8 * half]);
+    const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[t][8 * half + 4]);
+    k[0] = make_float2(lo.x, lo.y);
+    k[1] = make_float2(lo.z, lo.w);
+    k[2] = make_float2(hi.x, hi.y);
+    k[3] = make_float2(hi.z, hi.w);
+}
+
+// G[row] . k over the whole row: this lane's eight columns, then the partner half's.
+__device__ __forceinline__ float row_dot(const float2 (&g)[4], const float2 (&k)[4]) {
+    float2 a = fmul2(g[0], k[0]);
+    a = ffma2(g[1], k[1], a);
+    a = ffma2(g[2], k[2], a);
+    a = ffma2(g[3], k[3], a);
+    float part = a.x + a.y;
+    part += __shfl_xor_sync(0xffffffffu, part, 16);
+    return part;
+}
+
 template <int N>
-__device__ __forceinline__ void gain_pass(const ChainSmem& cs, int count, int row, int half, float (&g)[8]) {
+__device__ __forceinline__ void gain_pass(const ChainSmem& cs, int count, int row, int half, float2 (&g)[4]) {
     if (N > 0) count = N;
-    float kc[8];
-    {
-        const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[0][8 * half]);
-        const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[0][8 * half + 4]);
-        kc[0] = lo.x; kc[1] = lo.y; kc[2] = lo.z; kc[3] = lo.w;
-        kc[4] = hi.x; kc[5] = hi.y; kc[6] = hi.z; kc[7] = hi.w;
-    }
+    float2 kc[4];
+    load_key_half(cs, 0, half, kc);
     float4 gt = cs.gate[0];
-    float u;
-    {
-        float r0 = 0.f, r1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-            r0 = fmaf(g[i], kc[i], r0);
-            r1 = fmaf(g[i + 1], kc[i + 1], r1);
-        }
-        float part = r0 + r1;
-        part += __shfl_xor_sync(0xffffffffu, part, 16);
-        u = gt.x * (part + cs.dt[0][row]);
-    }
+    float u = gt.x * (row_dot(g, kc) + cs.dt[0][row]);
 #pragma unroll (N > 0 ? N : 1)
     for (int t = 0; t < count; ++t) {
         const float alpha = gt.y, kk = gt.z;
-        float kn[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float2 kn[4];
         float unext = 0.f;
         if (t + 1 < count) {
-            const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[t + 1][8 * half]);
-            const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[t + 1][8 * half + 4]);
-            kn[0] = lo.x; kn[1] = lo.y; kn[2] = lo.z; kn[3] = lo.w;
-            kn[4] = hi.x; kn[5] = hi.y; kn[6] = hi.z; kn[7] = hi.w;
+            load_key_half(cs, t + 1, half, kn);
             gt = cs.gate[t + 1];
-            float r0 = 0.f, r1 = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                r0 = fmaf(g[i], kn[i], r0);
-                r1 = fmaf(g[i + 1], kn[i + 1], r1);
-            }
-            float part = r0 + r1;
-            part += __shfl_xor_sync(0xffffffffu, part, 16);
             // r_{t+1} = d_{t+1} + alpha_t (G_{t-1} k_{t+1}) - u_t (k_t . k_{t+1})
-            const float r = fmaf(-u, kk, fmaf(alpha, part, cs.dt[t + 1][row]));
+            const float r = fmaf(-u, kk, fmaf(alpha, row_dot(g, kn), cs.dt[t + 1][row]));
             unext = gt.x * r;
         }
+        const float2 a2 = splat2(alpha), nu2 = splat2(-u);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) g[i] = fmaf(-u, kc[i], alpha * g[i]);
+        for (int i = 0; i < 4; ++i) g[i] = ffma2(nu2, kc[i], fmul2(a2, g[i]));
+        if (t + 1 < count) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) kc[i] = kn[i];
+            for (int i = 0; i < 4; ++i) kc[i] = kn[i];
+        }
         u = unext;
+    }
+}
+
+// Dispatches the gain recurrence to a fully unrolled body for the step lengths the
+// VisionHOPE stages produce (chunks of 56, 28, 14 and 7 tokens in steps of at most 32).
+__device__ __forceinline__ void gain_step(const ChainSmem& cs, int count, int row, int half, float2 (&g)[4]) {
+    switch (count) {
+        case 32: gain_pass<32>(cs, count, row, half, g); break;
+        case 28: gain_pass<28>(cs, count, row, half, g); break;
+        case 24: gain_pass<24>(cs, count, row, half, g); break;
+        case 14: gain_pass<14>(cs, count, row, half, g); break;
+        case 7: gain_pass<7>(cs, count, row, half, g); break;
+        default: gain_pass<0>(cs, count, row, half, g);
     }
 }
 
@@ -199,13 +218,12 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
         cs.ea[0][lane] = p.Me[sidx * kD + lane];
         cs.ea[1][lane] = p.Ma[sidx * kD + lane];
     }
-    float wlo[2] = {0.f, 0.f}, whi[2] = {0.f, 0.f}, slo[2] = {0.f, 0.f}, shi[2] = {0.f, 0.f};
     if constexpr (kSpatial) {
-        const int c0 = ro.head * kD;
-        const float* wv = p.weight + dir * p.C + c0;
-        const float* sv = p.skip + (p.skip_per_dir ? dir * p.C : 0) + c0;
-        wlo[0] = wv[2 * qt]; wlo[1] = wv[2 * qt + 1]; whi[0] = wv[8 + 2 * qt]; whi[1] = wv[9 + 2 * qt];
-        slo[0] = sv[2 * qt]; slo[1] = sv[2 * qt + 1]; shi[0] = sv[8 + 2 * qt]; shi[1] = sv[9 + 2 * qt];
+        if (lane < kD) {
+            const int c = ro.head * kD + lane;
+            cs.fw[0][lane] = p.weight[dir * p.C + c];
+            cs.fw[1][lane] = p.skip[(p.skip_per_dir ? dir * p.C : 0) + c];
+        }
     }
     __syncwarp();
 
@@ -241,23 +259,33 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
         qts = p.C;
         ybase = static_cast<bf16*>(p.y) + chain * p.L * kD + 2 * qt;
     }
-    // Source index (token or pixel) of token `tin` of chunk `c`.
-    auto src_of = [&](int c, int tin) -> int64_t {
-        if (kSpatial && p.remap) return scan_pixel(dir, c, tin, p.H, p.W);
-        return (int64_t)c * Lc + tin;
-    };
+    // Pixel visited at token `tin` of chunk `c` is pb + c * pc_step + tin * pt_step (the four
+    // scan orders of models/operator.py:79-86 as linear maps); the source element read is the
+    // pixel when the input is one image (remap) and the scan position c * Lc + tin otherwise.
+    int pb = 0, pc_step = 0, pt_step = 0;
+    if constexpr (kSpatial) {
+        const int last = p.H * p.W - 1;
+        switch (dir) {
+            case 0: pb = 0; pc_step = p.W; pt_step = 1; break;
+            case 1: pb = last; pc_step = -p.W; pt_step = -1; break;
+            case 2: pb = 0; pc_step = 1; pt_step = p.W; break;
+            default: pb = last; pc_step = -1; pt_step = -p.W; break;
+        }
+    }
+    const bool img_src = kSpatial && p.remap;
+    const int sb = img_src ? pb : 0, sc_step = img_src ? pc_step : Lc, st_step = img_src ? pt_step : 1;
 
     // A fragments of one step: [mtile][h: row qg / qg+8][lo/hi channel group]
     uint32_t axn[2][2][2], aqn[2][2][2];
     auto prefetch = [&](int c, int j) {
+        const int cb = sb + c * sc_step;
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int tin = j * kTile + mt * 16 + qg + 8 * h;
-                const int64_t t = (int64_t)c * Lc + tin;
-                if (tin < Lc && t < p.L) {
-                    const int64_t s = src_of(c, tin);
+                if (tin < Lc && (kSpatial || (int64_t)c * Lc + tin < p.L)) {
+                    const int64_t s = cb + tin * st_step;
                     const bf16* xr = xbase + s * xts + 2 * qt;
                     const bf16* qr = qbase + s * qts + 2 * qt;
                     axn[mt][h][0] = __ldg(reinterpret_cast<const uint32_t*>(xr));
@@ -272,11 +300,12 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
     prefetch(0, 0);
 
     const int p2_row = lane & 15, p2_half = lane >> 4;
-    float g8[8];
+    float2 g8[4];  // this lane's half row of G as column pairs
 
     for (int c = 0; c < nchunks; ++c) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) g8[i] = (p2_half * 8 + i == p2_row) ? 1.f : 0.f;
+        for (int i = 0; i < 4; ++i)
+            g8[i] = make_float2(p2_half * 8 + 2 * i == p2_row ? 1.f : 0.f, p2_half * 8 + 2 * i + 1 == p2_row ? 1.f : 0.f);
         for (int j = 0; j < tpc; ++j) {
             const int count = j + 1 < tpc ? kTile : last_count;
             const int mtiles = j + 1 < tpc ? 2 : mtiles_last;
@@ -341,8 +370,12 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                     const float y0 = cy[0][2 * h] * qinv, y1 = cy[0][2 * h + 1] * qinv;
                     const float y2 = cy[1][2 * h] * qinv, y3 = cy[1][2 * h + 1] * qinv;
                     if constexpr (kSpatial) {
-                        olo[mt][h] = make_float2(wlo[0] * (y0 + slo[0] * x01.x), wlo[1] * (y1 + slo[1] * x01.y));
-                        ohi[mt][h] = make_float2(whi[0] * (y2 + shi[0] * x23.x), whi[1] * (y3 + shi[1] * x23.y));
+                        const float2 wl = *reinterpret_cast<const float2*>(&cs.fw[0][2 * qt]);
+                        const float2 wh = *reinterpret_cast<const float2*>(&cs.fw[0][8 + 2 * qt]);
+                        const float2 sl = *reinterpret_cast<const float2*>(&cs.fw[1][2 * qt]);
+                        const float2 sh = *reinterpret_cast<const float2*>(&cs.fw[1][8 + 2 * qt]);
+                        olo[mt][h] = make_float2(wl.x * (y0 + sl.x * x01.x), wl.y * (y1 + sl.y * x01.y));
+                        ohi[mt][h] = make_float2(wh.x * (y2 + sh.x * x23.x), wh.y * (y3 + sh.y * x23.y));
                     } else {
                         const int64_t t = (int64_t)c * Lc + j * kTile + row;
                         if (row < count && t < p.L) {
@@ -431,7 +464,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                         const bool coincident = pc == c && pj == j;
                         const bool partner_later = pc > c || (pc == c && pj > j);
                         const unsigned bit = 1u << (2 * mt + h);
-                        pix[mt][h] = scan_pixel(dir, c, tin, p.H, p.W);
+                        pix[mt][h] = pb + c * pc_step + tin * pt_step;
                         live |= bit;
                         if (coincident && (dir & 1)) {
                             defer |= bit;
@@ -446,8 +479,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
             __syncwarp();
 
             // ------------------ P2: gain recurrence ---------------------------------------------
-            if (count == kTile) gain_pass<kTile>(cs, count, p2_row, p2_half, g8);
-            else gain_pass<0>(cs, count, p2_row, p2_half, g8);
+            gain_step(cs, count, p2_row, p2_half, g8);
 
             if constexpr (kSpatial) {
 #pragma unroll
@@ -488,7 +520,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 uint32_t parts[kSplits];
-                split3(g8[2 * i], g8[2 * i + 1], parts);
+                split3(g8[i].x, g8[i].y, parts);
 #pragma unroll
                 for (int k = 0; k < kSplits; ++k) gp[k][i >> 1][i & 1] = parts[k];
             }
@@ -606,7 +638,7 @@ __device__ __forceinline__ void fold_planes(const ScanParams& p, int b, int head
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, 4) srnl_warp_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(kThreads, VH_WPC_MIN_BLOCKS) srnl_warp_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5;
     ChainSmem& cs = reinterpret_cast<ChainSmem*>(smem_raw)[warp];
