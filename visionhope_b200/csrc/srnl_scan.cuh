@@ -173,7 +173,8 @@ struct RowReg {
     }
 };
 
-__device__ __forceinline__ float softplus_f(float p) { return p > 20.f ? p : log1pf(expf(p)); }
+// softplus as the reference writes it (models/srnl_core/csrc/inference_recurrence.cuh:74).
+__device__ __forceinline__ float softplus_f(float p) { return p > 20.f ? p : logf(1.f + expf(p)); }
 
 // ---- tensor-core helpers (bf16 m16n8k16, fp32 accumulate) ------------------------------
 // Rows of 16 bf16 (32 bytes) are stored with their two 16-byte halves swapped on rows whose

@@ -11,8 +11,8 @@
 //
 // Per chunk (chunk-start state S = [M_m; M_v; M_k; e^T; a^T], gain G reset to I):
 //   P1  tokens in steps of 32 (two 16-row MMA tiles):
-//       - x and raw q fragments come from global memory straight into registers, one step
-//         ahead;
+//       - the step's x and raw q token rows arrive in shared memory by asynchronous copies
+//         issued during the previous step, and feed the MMAs through ldmatrix;
 //       - k~ = M_k x, v = M_v x and M_m q_raw run as bf16 m16n8k16 tensor-core MMAs against
 //         the three-way bf16 split of the fp32 memories (fp32 accumulate, 24-bit operands);
 //         y = (M_m q_raw) / ||q_raw|| (models/srnl_core/csrc/inference_recurrence.cuh:40-60);
@@ -62,6 +62,7 @@ struct alignas(16) ChainSmem {
     float4 gate[kTile];                 // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
     unsigned char gs[kSplits][16][32];  // split gain rows (row-major, k x n)
     float fw[2][kD];                    // spatial: this scan's fusion weight and skip per channel
+    unsigned char xq[2][kTile][32];     // the step's x and raw q token rows (bf16, swizzled)
 };
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const unsigned char* p) {
@@ -275,27 +276,22 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
     const bool img_src = kSpatial && p.remap;
     const int sb = img_src ? pb : 0, sc_step = img_src ? pc_step : Lc, st_step = img_src ? pt_step : 1;
 
-    // A fragments of one step: [mtile][h: row qg / qg+8][lo/hi channel group]
-    uint32_t axn[2][2][2], aqn[2][2][2];
+    // The x and raw q rows of a step go to shared memory as 16-byte asynchronous copies (two
+    // per token row, zeros past the chunk or sequence end, as the reference pads:
+    // models/srnl_core/chunk.py:202-206); the MMA fragments are then read with ldmatrix.
     auto prefetch = [&](int c, int j) {
         const int cb = sb + c * sc_step;
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int tin = j * kTile + mt * 16 + qg + 8 * h;
-                if (tin < Lc && (kSpatial || (int64_t)c * Lc + tin < p.L)) {
-                    const int64_t s = cb + tin * st_step;
-                    const bf16* xr = xbase + s * xts + 2 * qt;
-                    const bf16* qr = qbase + s * qts + 2 * qt;
-                    axn[mt][h][0] = __ldg(reinterpret_cast<const uint32_t*>(xr));
-                    axn[mt][h][1] = __ldg(reinterpret_cast<const uint32_t*>(xr + 8));
-                    aqn[mt][h][0] = __ldg(reinterpret_cast<const uint32_t*>(qr));
-                    aqn[mt][h][1] = __ldg(reinterpret_cast<const uint32_t*>(qr + 8));
-                } else {  // tail padding reads as zeros (models/srnl_core/chunk.py:202-206)
-                    axn[mt][h][0] = axn[mt][h][1] = aqn[mt][h][0] = aqn[mt][h][1] = 0u;
-                }
-            }
+        for (int u = 0; u < 4; ++u) {
+            const int id = u * 32 + lane;  // 128 chunks: tensor, token, half
+            const int tensor = id >> 6, tok = (id >> 1) & 31, half = id & 1;
+            const int tin = j * kTile + tok;
+            const bool ok = tin < Lc && (kSpatial || (int64_t)c * Lc + tin < p.L);
+            const int64_t s = cb + tin * st_step;
+            const bf16* src = tensor ? qbase + s * qts : xbase + s * xts;
+            cp_async16_zfill(&cs.xq[tensor][0][0] + swz(tok, half), ok ? src + 8 * half : xbase, ok);
+        }
+        cp_async_commit();
     };
     prefetch(0, 0);
 
@@ -309,18 +305,8 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
         for (int j = 0; j < tpc; ++j) {
             const int count = j + 1 < tpc ? kTile : last_count;
             const int mtiles = j + 1 < tpc ? 2 : mtiles_last;
-            uint32_t ax[2][2][2], aq[2][2][2];
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        ax[mt][h][k] = axn[mt][h][k];
-                        aq[mt][h][k] = aqn[mt][h][k];
-                    }
-            if (j + 1 < tpc) prefetch(c, j + 1);
-            else if (c + 1 < nchunks) prefetch(c + 1, 0);
+            cp_async_wait<0>();
+            __syncwarp();
 
             // ---------------------------- P1: projections -------------------------------
             float2 olo[2][2], ohi[2][2];
@@ -329,8 +315,10 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                 olo[mt][0] = olo[mt][1] = ohi[mt][0] = ohi[mt][1] = make_float2(0.f, 0.f);
                 if (mt >= mtiles) break;  // warp-uniform
                 float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {};
-                const uint32_t A_x[4] = {ax[mt][0][0], ax[mt][1][0], ax[mt][0][1], ax[mt][1][1]};
-                const uint32_t A_q[4] = {aq[mt][0][0], aq[mt][1][0], aq[mt][0][1], aq[mt][1][1]};
+                // A fragments: {row qg, row qg+8} x {channels 2qt.., 8+2qt..}
+                uint32_t A_x[4], A_q[4];
+                ldsm_x4(A_x, &cs.xq[0][0][0] + swz(mt * 16 + (lane & 15), lane >> 4));
+                ldsm_x4(A_q, &cs.xq[1][0][0] + swz(mt * 16 + (lane & 15), lane >> 4));
                 const int brow = (lane & 7) + ((lane >> 4) << 3), bhalf = (lane >> 3) & 1;
 #pragma unroll
                 for (int k = 0; k < kSplits; ++k) {
@@ -353,8 +341,8 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                 for (int h = 0; h < 2; ++h) {
                     // Lane (qg, qt) holds channels {2qt, 2qt+1, 8+2qt, 9+2qt} of token row qg + 8h.
                     const int row = mt * 16 + qg + 8 * h;
-                    const float2 x01 = bf2_to_f2(ax[mt][h][0]), x23 = bf2_to_f2(ax[mt][h][1]);
-                    const float2 q01 = bf2_to_f2(aq[mt][h][0]), q23 = bf2_to_f2(aq[mt][h][1]);
+                    const float2 x01 = bf2_to_f2(A_x[h]), x23 = bf2_to_f2(A_x[2 + h]);
+                    const float2 q01 = bf2_to_f2(A_q[h]), q23 = bf2_to_f2(A_q[2 + h]);
                     *reinterpret_cast<float2*>(&cs.kt[row][2 * qt]) = make_float2(ck[0][2 * h], ck[0][2 * h + 1]);
                     *reinterpret_cast<float2*>(&cs.kt[row][8 + 2 * qt]) = make_float2(ck[1][2 * h], ck[1][2 * h + 1]);
                     *reinterpret_cast<float2*>(&cs.dt[row][2 * qt]) = make_float2(cv[0][2 * h], cv[0][2 * h + 1]);
@@ -386,44 +374,48 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                     }
                 }
             }
-            __syncwarp();
+            __syncwarp();  // every lane's fragments of this step are read: refill the tile
+            if (j + 1 < tpc) prefetch(c, j + 1);
+            else if (c + 1 < nchunks) prefetch(c + 1, 0);
 
             // ------------------ P1: per-token gates (one lane per token) ---------------------
-            float kr[kD];
+            float2 kr[kD / 2];
             if (lane < count) {
-                float vv[kD];
+                float2 vv[kD / 2];
 #pragma unroll
                 for (int i = 0; i < kD; i += 4) {
                     const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane][i]);
                     const float4 v4 = *reinterpret_cast<const float4*>(&cs.dt[lane][i]);
-                    kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
-                    vv[i] = v4.x; vv[i + 1] = v4.y; vv[i + 2] = v4.z; vv[i + 3] = v4.w;
+                    kr[i / 2] = make_float2(k4.x, k4.y);
+                    kr[i / 2 + 1] = make_float2(k4.z, k4.w);
+                    vv[i / 2] = make_float2(v4.x, v4.y);
+                    vv[i / 2 + 1] = make_float2(v4.z, v4.w);
                 }
-                float kn = 0.f;
+                float2 kn2 = fmul2(kr[0], kr[0]);
 #pragma unroll
-                for (int i = 0; i < kD; ++i) kn = fmaf(kr[i], kr[i], kn);
-                const float kinv = 1.f / sqrtf(kn + 1e-6f);
-                float ke = 0.f, dn2 = 0.f;
+                for (int i = 1; i < kD / 2; ++i) kn2 = ffma2(kr[i], kr[i], kn2);
+                const float kinv = 1.f / sqrtf((kn2.x + kn2.y) + 1e-6f);
+                const float2 kinv2 = splat2(kinv);
+                float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
 #pragma unroll
-                for (int i = 0; i < kD; ++i) {
-                    const float kk = kr[i] * kinv;
-                    const float d = kk - vv[i];
-                    kr[i] = kk;
-                    vv[i] = d;
-                    ke = fmaf(kk, kk, ke);
-                    dn2 = fmaf(d, d, dn2);
+                for (int i = 0; i < kD / 2; ++i) {
+                    kr[i] = fmul2(kr[i], kinv2);
+                    vv[i] = fadd2(kr[i], make_float2(-vv[i].x, -vv[i].y));  // d = k - v
+                    ke2 = ffma2(kr[i], kr[i], ke2);
+                    dn2 = ffma2(vv[i], vv[i], dn2);
                 }
 #pragma unroll
                 for (int i = 0; i < kD; i += 4) {
-                    *reinterpret_cast<float4*>(&cs.kt[lane][i]) = make_float4(kr[i], kr[i + 1], kr[i + 2], kr[i + 3]);
-                    *reinterpret_cast<float4*>(&cs.dt[lane][i]) = make_float4(vv[i], vv[i + 1], vv[i + 2], vv[i + 3]);
+                    *reinterpret_cast<float4*>(&cs.kt[lane][i]) = make_float4(kr[i / 2].x, kr[i / 2].y, kr[i / 2 + 1].x, kr[i / 2 + 1].y);
+                    *reinterpret_cast<float4*>(&cs.dt[lane][i]) = make_float4(vv[i / 2].x, vv[i / 2].y, vv[i / 2 + 1].x, vv[i / 2 + 1].y);
                 }
+                const float ke = ke2.x + ke2.y;
                 const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[lane]);
                 const float ep = fminf(10.f, fmaxf(-10.f, raw.x));
                 const float ap = fminf(10.f, fmaxf(-10.f, raw.y + p.k.retention_bias));
                 const float eta = p.k.step_scale * softplus_f(ep);
                 const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
-                const float dn = sqrtf(dn2 + 1e-12f);
+                const float dn = sqrtf((dn2.x + dn2.y) + 1e-12f);
                 const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
                 float eff = cap * (-expm1f(-(eta / cap)));
                 if (p.k.spectral_clamp) {
@@ -434,16 +426,14 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
             }
             __syncwarp();
             if (lane + 1 < count) {  // k_t . k_{t+1} for the lookahead of the gain recurrence
-                float kk = 0.f;
+                float2 kk2 = splat2(0.f);
 #pragma unroll
                 for (int i = 0; i < kD; i += 4) {
                     const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane + 1][i]);
-                    kk = fmaf(kr[i], k4.x, kk);
-                    kk = fmaf(kr[i + 1], k4.y, kk);
-                    kk = fmaf(kr[i + 2], k4.z, kk);
-                    kk = fmaf(kr[i + 3], k4.w, kk);
+                    kk2 = ffma2(kr[i / 2], make_float2(k4.x, k4.y), kk2);
+                    kk2 = ffma2(kr[i / 2 + 1], make_float2(k4.z, k4.w), kk2);
                 }
-                cs.gate[lane].z = kk;
+                cs.gate[lane].z = kk2.x + kk2.y;
             }
 
             // ------------- spatial output: pixels, and read-backs of a partner's value ---------
