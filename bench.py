@@ -304,13 +304,21 @@ def roofline_scan(args, device, steps):
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     if peaks_path.exists():
         peaks = json.loads(peaks_path.read_text())
+    traffic = None
+    prof = ROOT / "profiles" / "srnl_warp_kernel_stage1_b256.md"
+    if prof.exists() and B == 256:
+        for line in prof.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1])
     return {
-        "kernel": "srnl_scan_kernel (fused 4-direction SRNL operator: rows + columns pass)",
+        "kernel": "srnl_warp_kernel<kKindBoth> (fused 4-direction SRNL operator, one launch)",
         "shape": f"B={B} H={H} W={W} C={C} heads={heads} D={D} bf16 in, fp32 out",
         "bound": "fp32", "unit": "TFLOP/s", "achieved": achieved, "peak": peak,
         "frac": achieved / peak if peak else None,
         "peak_source": "measured FP32 FFMA probe on this GPU (vh_probe_ffma), no tensor cores",
-        "traffic": None, "launch_ms": ms, "flops_per_launch": flops,
+        "traffic": traffic, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+        "of this workload (profiles/srnl_warp_kernel_stage1_b256.md)" if traffic else None,
+        "launch_ms": ms, "flops_per_launch": flops,
         "alg_bytes_per_launch": alg_bytes,
         "hbm_frac_of_measured": (alg_bytes / (ms * 1e-3) / 1e9) / peaks["hbm_gbs"] if "hbm_gbs" in peaks else None,
         "tensor_frac_of_measured": (achieved / peaks["bf16_tflops"]) if "bf16_tflops" in peaks else None,
