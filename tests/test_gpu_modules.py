@@ -171,7 +171,7 @@ def test_tiny_backbone_graph_and_paths(cuda):
     with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
         ordinary = model(x).float()
     counts = prepare_for_inference(model)
-    assert counts["srnl"] == 29 and counts["layerscale"] == 58
+    assert counts["srnl"] == 29 and counts["layerscale"] == 58 and counts["batchnorm_folded"] == 7
     with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
         eager = model(x).float()
         g = torch.cuda.CUDAGraph()

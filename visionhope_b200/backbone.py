@@ -21,6 +21,7 @@ from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
 from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_forward
+from .utils.inference import cache_half_weights, linear_cached
 from .utils.layer_norm_cuda import layernorm_rows
 
 
@@ -44,8 +45,7 @@ def pointwise(conv, x):
     The GEMM applies the bias in its epilogue; a convolution of a channels-last tensor adds
     the bias in a separate broadcast pass.  Other layouts use the convolution itself."""
     if x.is_cuda and x.is_contiguous(memory_format=torch.channels_last) and x.shape[1] > 1:
-        y = F.linear(x.permute(0, 2, 3, 1), conv.weight[:, :, 0, 0], conv.bias)
-        return y.permute(0, 3, 1, 2)
+        return linear_cached(conv, x.permute(0, 2, 3, 1)).permute(0, 3, 1, 2)
     return conv(x)
 
 
@@ -130,6 +130,18 @@ class FeedForwardNetwork(nn.Module):
         return self.drop(pointwise(self.fc2, self.drop(x)))
 
 
+def _fold_conv_bn(conv, bn):
+    """conv followed by eval-mode bn -> conv with w * g / sqrt(var + eps), (b - mean) * that + beta."""
+    scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
+    conv.weight.mul_(scale.view(-1, 1, 1, 1).to(conv.weight.dtype))
+    bias = conv.bias if conv.bias is not None else torch.zeros_like(bn.running_mean)
+    folded = (bias - bn.running_mean) * scale + bn.bias
+    if conv.bias is None:
+        conv.bias = nn.Parameter(folded.to(conv.weight.dtype))
+    else:
+        conv.bias.copy_(folded)
+
+
 class PatchEmbedding(nn.Module):
     """Stride-4 convolutional stem: conv/BN/GELU x3 then conv/BN (layers.py:85-107)."""
 
@@ -153,6 +165,18 @@ class PatchEmbedding(nn.Module):
     def forward(self, x):
         return self.norm(self.proj(x))
 
+    @torch.no_grad()
+    def fold_batchnorm(self):
+        """Inference: fold each eval-mode BatchNorm into the convolution before it."""
+        layers, n = list(self.proj), 0
+        for i in range(len(layers) - 1):
+            if isinstance(layers[i], nn.Conv2d) and isinstance(layers[i + 1], nn.BatchNorm2d):
+                _fold_conv_bn(layers[i], layers[i + 1])
+                layers[i + 1] = nn.Identity()
+                n += 1
+        self.proj = nn.Sequential(*layers)
+        return n
+
 
 class Downsample(nn.Module):
     def __init__(self, in_dim, out_dim):
@@ -162,6 +186,15 @@ class Downsample(nn.Module):
 
     def forward(self, x):
         return self.norm(self.proj(x))
+
+    @torch.no_grad()
+    def fold_batchnorm(self):
+        """Inference: fold the eval-mode BatchNorm into the convolution."""
+        if not isinstance(self.norm, nn.BatchNorm2d):
+            return 0
+        _fold_conv_bn(self.proj, self.norm)
+        self.norm = nn.Identity()
+        return 1
 
 
 class VisionHOPEBlock(nn.Module):
@@ -236,7 +269,7 @@ class VisionHOPEBlock(nn.Module):
                         lepe = lepe.to(x_local.dtype)
                 out = self.operator._forward_fast(x_local, path, addend=lepe,
                                                   final_dtype=_autocast_dtype() or torch.float32)
-                out = self.proj_out(out)
+                out = linear_cached(self.proj_out, out)
                 # NHWC storage viewed as NCHW (channels-last); the reference copies it to
                 # contiguous NCHW here, which only costs a layout pass before the residual add.
                 out = out.permute(0, 3, 1, 2)
@@ -378,6 +411,14 @@ def prepare_for_inference(model):
                 setattr(block, gname, None)
                 counts["layerscale"] += 1
             block._inference_prepared = True
+        for m in model.modules():
+            if isinstance(m, PatchEmbedding) or isinstance(m, Downsample):
+                counts["batchnorm_folded"] = counts.get("batchnorm_folded", 0) + m.fold_batchnorm()
+        for block in blocks:
+            for lin in (block.proj_in, block.local_gate, block.operator.W_q, block.proj_out,
+                        block.ffn.fc1, block.ffn.fc2):
+                if lin is not None:
+                    cache_half_weights(lin)
     if blocks:
         model._inference_prepared = True
     return counts

@@ -12,6 +12,7 @@ from torch import nn
 from .srnl import SRNL, trunc_normal_
 from .utils.cuda import on_tensor_device
 from .utils.direction_fusion import visionhope_postprocess_scale
+from .utils.inference import linear_cached
 
 
 class VisionHOPEOperator(nn.Module):
@@ -162,7 +163,7 @@ class VisionHOPEOperator(nn.Module):
         x_img = x.permute(0, 2, 3, 1)  # [B, H, W, C]; a view when x is channels-last
         if not x_img.is_contiguous():
             x_img = x_img.contiguous()
-        q_img = self.W_q(x_img)
+        q_img = linear_cached(self.W_q, x_img)
         if q_img.dtype != x_img.dtype:
             q_img = q_img.to(x_img.dtype)
         return spatial_forward(memories, x_img, q_img, self.d_skip, self._fusion_weights(),
