@@ -90,10 +90,12 @@ typedef struct {
  * skip: C values (shared across directions) or 4*C (skip_per_dir = 1); weight: fp32 [4, C].
  *
  * Optional fields (leave zero / NULL when unused):
- *   aux:       fp32 plane with out's layout (out_batch_stride).  With it the column scans
- *              run concurrently with the row scans and accumulate here; each (batch, head)
- *              then adds its aux slice into out (or into final_out).  Its content afterwards
- *              is unspecified.  Without it the two passes run one after the other in out.
+ *   aux:       fp32 workspace of three planes with out's layout, plane k at
+ *              aux + k * batch * out_batch_stride.  With it (head_dim 16, bf16) the four scans
+ *              of a (batch, head) run concurrently in one launch, each into its own plane
+ *              (scan 0 into out), and the four planes are summed at the end.  Its content
+ *              afterwards is unspecified.  Without it a rows pass and a columns pass run one
+ *              after the other, accumulating in out.
  *   final_out: final_dtype [B, H, W, C] with final_batch_stride elements per image and C per
  *              pixel: receives (final_dtype)(sum of the four scans + addend).  out is then
  *              scratch and its content afterwards unspecified.

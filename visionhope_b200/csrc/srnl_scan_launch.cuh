@@ -72,7 +72,7 @@ int launch_scan(ScanParams p, const ScanPlan& pl, dim3 grid, cudaStream_t st) {
 }
 
 // Warp-per-chain scan (D = 16, bf16), four warps per CTA: the four scans of one (b, head)
-// (kKindBoth), two scan pairs of one pass (kKindRows / kKindCols) or four sequence chains.
+// (kKindBoth, needs the three aux planes) or four sequence chains (kKindSeq).
 template <int KIND>
 int launch_warp(ScanParams p, int pairs_or_chains, cudaStream_t st) {
     p.kind = KIND;
@@ -80,7 +80,7 @@ int launch_warp(ScanParams p, int pairs_or_chains, cudaStream_t st) {
     p.tile = wpc::kTile;
     p.log2tile = 5;
     const size_t smem = sizeof(wpc::ChainSmem) * wpc::kWarps;
-    const int per_cta = KIND == kKindBoth ? 1 : KIND == kKindSeq ? wpc::kWarps : 2;
+    const int per_cta = KIND == kKindBoth ? 1 : wpc::kWarps;
     const dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, KIND == kKindSeq ? p.R : 1);
     const void* fn = reinterpret_cast<const void*>(&wpc::srnl_warp_kernel<KIND>);
     if (!ensure_smem_attr(fn, smem))
@@ -89,13 +89,19 @@ int launch_warp(ScanParams p, int pairs_or_chains, cudaStream_t st) {
     return launch_status("srnl warp scan");
 }
 
-// Chooses the warp-per-chain tensor-core scan when it applies (D = 16, bf16, chunks of 9+
-// tokens), else the CTA-lockstep scan.
+// Sequences: the warp-per-chain scan when it applies (D = 16, bf16, chunks of 9+ tokens).
+// Spatial passes without the aux planes: the CTA-lockstep scan, with its tensor-core token
+// phase where it applies.
 template <int D, typename XT, typename QT, int KIND>
 int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStream_t st) {
     const bool spatial = KIND != kKindSeq;
     if constexpr (mma_capable<D, XT, QT>()) {
-        if (max_chunk > 8) return launch_warp<KIND>(p, pairs_or_chains, st);
+        if (max_chunk > 8) {
+            if (!spatial) return launch_warp<kKindSeq>(p, pairs_or_chains, st);
+            const ScanPlan pl = fit_plan<D, XT, QT, KIND, true>(max_chunk);
+            dim3 grid((pairs_or_chains + pl.nch / 2 - 1) / (pl.nch / 2), 1);
+            return launch_scan<D, XT, QT, KIND, true>(p, pl, grid, st);
+        }
     }
     const ScanPlan pl = fit_plan<D, XT, QT, KIND, false>(max_chunk);
     const int per_cta = spatial ? pl.nch / 2 : pl.nch;
@@ -106,9 +112,6 @@ int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStr
 // Writes (final dtype)(out + addend) when the scans ran without folding it in (srnl_scan.cu).
 int launch_spatial_finalize(const ScanParams& p, int io_dtype, cudaStream_t st);
 
-// Both passes in one launch when the warp-per-chain scan applies and an aux plane is given
-// (the final cast and addend are then folded in by each CTA); otherwise the rows pass, the
-// columns pass and, if a final output is requested, a finalize launch.
 template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
     const int pairs = p.B * p.heads;

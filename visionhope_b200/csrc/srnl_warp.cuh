@@ -1,13 +1,12 @@
 // Warp-per-chain SRNL scan for head_dim 16 with bf16 inputs (the inference hot path).
 //
 // One warp owns one chain (a (batch, direction, head) scan) for its whole length.  A CTA holds
-// four warps and never synchronizes all of them before its end, so each warp advances on its
-// own and the SM hides one warp's latency behind the others:
-//   kKindBoth       the four scans of one (batch, head): warps 0/1 (rows pair) accumulate in
-//                   `out`, warps 2/3 (columns pair) in `aux`; the CTA then folds aux into out,
-//                   or writes (final dtype)(out + aux + addend) into `fin`.
-//   kKindRows/Cols  two scan pairs of one pass (the passes run as two launches in `out`).
-//   kKindSeq        four independent packed-sequence chains.
+// four warps and never synchronizes them before its end, so each warp advances on its own and
+// the SM hides one warp's latency behind the others:
+//   kKindBoth  the four scans of one (batch, head), each writing its own fp32 plane (scan 0
+//              `out`, scans 1-3 the three planes of `aux`); the CTA then sums the four planes
+//              of its (batch, head) into `out`, or writes (final dtype)(sum + addend) to `fin`.
+//   kKindSeq   four independent packed-sequence chains.
 //
 // Per chunk (chunk-start state S = [M_m; M_v; M_k; e^T; a^T], gain G reset to I):
 //   P1  tokens in steps of 32 (two 16-row MMA tiles):
@@ -29,11 +28,9 @@
 // The memories live only as their three bf16 parts (hi + mid + lo reproduce the fp32 value to
 // 2^-24), plus e and a in fp32.
 //
-// Spatial output order (deterministic, no atomics): every pixel is touched once by each scan
-// of a pair; the first touch stores into a fresh plane, the later one adds, and touches of both
-// scans in the same step (middle row/column) are ordered by the pair's named barrier: the even
-// scan writes first.  Reads of a partner's value are issued before P2 so their latency hides
-// behind it; all of a step's writes land before the pair's barrier at the end of the step.
+// Spatial output: every scan stores w_d (y + s_d x) for each pixel it visits into its own
+// plane (one plain store per pixel and scan, no read-back, no ordering between scans); the
+// four planes are summed in a fixed order at the CTA's end, so results are deterministic.
 #pragma once
 
 #include "f32x2.cuh"
@@ -91,17 +88,9 @@ __device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSp
     }
 }
 
-__device__ __forceinline__ void pair_barrier(int id) {
-    asm volatile("bar.sync %0, 64;\n" ::"r"(id) : "memory");
-}
-
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
-
 struct Role {
     int b, dir, head, valid;
-    float* plane;      // spatial accumulation plane of this warp's pass
-    int bar;           // named barrier of the scan pair
-    bool store_first;  // the pair's first touch of a pixel stores (the plane starts unwritten)
+    float* plane;  // spatial: this scan's output plane
 };
 
 template <int KIND>
@@ -111,19 +100,14 @@ __device__ __forceinline__ Role warp_role(const ScanParams& p, int warp) {
     if (KIND == kKindSeq) {
         idx = blockIdx.x * kWarps + warp;
         r.dir = blockIdx.y;
-    } else if (KIND == kKindBoth) {
+    } else {
         idx = blockIdx.x;
         r.dir = warp;
-    } else {
-        idx = blockIdx.x * 2 + (warp >> 1);
-        r.dir = 2 * KIND + (warp & 1);
     }
     r.valid = idx < p.B * p.heads;
     r.b = r.valid ? idx / p.heads : 0;
     r.head = r.valid ? idx % p.heads : 0;
-    r.plane = (KIND == kKindBoth && warp >= 2) ? p.aux : p.out;
-    r.bar = 1 + (warp >> 1);
-    r.store_first = KIND != kKindCols;
+    r.plane = warp == 0 || KIND == kKindSeq ? p.out : p.aux + (int64_t)(warp - 1) * p.B * p.ob;
     return r;
 }
 
@@ -309,10 +293,8 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
             __syncwarp();
 
             // ---------------------------- P1: projections -------------------------------
-            float2 olo[2][2], ohi[2][2];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
-                olo[mt][0] = olo[mt][1] = ohi[mt][0] = ohi[mt][1] = make_float2(0.f, 0.f);
                 if (mt >= mtiles) break;  // warp-uniform
                 float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {};
                 // A fragments: {row qg, row qg+8} x {channels 2qt.., 8+2qt..}
@@ -362,8 +344,13 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                         const float2 wh = *reinterpret_cast<const float2*>(&cs.fw[0][8 + 2 * qt]);
                         const float2 sl = *reinterpret_cast<const float2*>(&cs.fw[1][2 * qt]);
                         const float2 sh = *reinterpret_cast<const float2*>(&cs.fw[1][8 + 2 * qt]);
-                        olo[mt][h] = make_float2(wl.x * (y0 + sl.x * x01.x), wl.y * (y1 + sl.y * x01.y));
-                        ohi[mt][h] = make_float2(wh.x * (y2 + sh.x * x23.x), wh.y * (y3 + sh.y * x23.y));
+                        if (row < count) {  // this scan's plane: w_d (y + s_d x) for the pixel
+                            float* op = obase + (int64_t)(pb + c * pc_step + (j * kTile + row) * pt_step) * p.C;
+                            *reinterpret_cast<float2*>(op) =
+                                make_float2(wl.x * (y0 + sl.x * x01.x), wl.y * (y1 + sl.y * x01.y));
+                            *reinterpret_cast<float2*>(op + 8) =
+                                make_float2(wh.x * (y2 + sh.x * x23.x), wh.y * (y3 + sh.y * x23.y));
+                        }
                     } else {
                         const int64_t t = (int64_t)c * Lc + j * kTile + row;
                         if (row < count && t < p.L) {
@@ -436,70 +423,10 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                 cs.gate[lane].z = kk2.x + kk2.y;
             }
 
-            // ------------- spatial output: pixels, and read-backs of a partner's value ---------
-            int pix[2][2] = {{0, 0}, {0, 0}};
-            unsigned live = 0, rmw = 0, defer = 0;
-            float2 plo[2][2], phi[2][2];
-            if constexpr (kSpatial) {
-#pragma unroll
-                for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        plo[mt][h] = phi[mt][h] = make_float2(0.f, 0.f);
-                        const int row = mt * 16 + qg + 8 * h;
-                        if (row >= count) continue;
-                        const int tin = j * kTile + row;
-                        // The pair's partner visits this pixel at chunk nchunks-1-c, token Lc-1-tin.
-                        const int pc = nchunks - 1 - c, pj = (Lc - 1 - tin) / kTile;
-                        const bool coincident = pc == c && pj == j;
-                        const bool partner_later = pc > c || (pc == c && pj > j);
-                        const unsigned bit = 1u << (2 * mt + h);
-                        pix[mt][h] = pb + c * pc_step + tin * pt_step;
-                        live |= bit;
-                        if (coincident && (dir & 1)) {
-                            defer |= bit;
-                        } else if (!(ro.store_first && (coincident || partner_later))) {
-                            rmw |= bit;
-                            const float* op = obase + (int64_t)pix[mt][h] * p.C;
-                            plo[mt][h] = *reinterpret_cast<const float2*>(op);
-                            phi[mt][h] = *reinterpret_cast<const float2*>(op + 8);
-                        }
-                    }
-            }
             __syncwarp();
 
             // ------------------ P2: gain recurrence ---------------------------------------------
             gain_step(cs, count, p2_row, p2_half, g8);
-
-            if constexpr (kSpatial) {
-#pragma unroll
-                for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const unsigned bit = 1u << (2 * mt + h);
-                        if (!(live & bit) || (defer & bit)) continue;
-                        float* op = obase + (int64_t)pix[mt][h] * p.C;
-                        const bool add = rmw & bit;
-                        *reinterpret_cast<float2*>(op) = add ? add2(plo[mt][h], olo[mt][h]) : olo[mt][h];
-                        *reinterpret_cast<float2*>(op + 8) = add ? add2(phi[mt][h], ohi[mt][h]) : ohi[mt][h];
-                    }
-                // Pair lockstep: every write of this step lands before either scan moves on; a
-                // pixel both scans touch in this step is then added by the odd scan.
-                pair_barrier(ro.bar);
-                if (defer) {
-#pragma unroll
-                    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            if (defer & (1u << (2 * mt + h))) {
-                                float* op = obase + (int64_t)pix[mt][h] * p.C;
-                                const float2 a = *reinterpret_cast<const float2*>(op);
-                                const float2 b = *reinterpret_cast<const float2*>(op + 8);
-                                *reinterpret_cast<float2*>(op) = add2(a, olo[mt][h]);
-                                *reinterpret_cast<float2*>(op + 8) = add2(b, ohi[mt][h]);
-                            }
-                }
-            }
             __syncwarp();  // P1 of the next step overwrites kt/dt/gate
         }
 
@@ -591,13 +518,15 @@ __device__ __forceinline__ void store_final4(void* base, int dtype, int64_t off,
     }
 }
 
-// End of a kKindBoth CTA: fold the columns plane of (b, head) into the rows plane, or write
-// the final output (sum + addend, cast).  Four loads are issued before any store.
+// End of a kKindBoth CTA: sum the four scans' planes of (b, head) in a fixed order into `out`,
+// or write (final dtype)(sum + addend).  The loads of four pixel groups are issued before any
+// store.
 __device__ __forceinline__ void fold_planes(const ScanParams& p, int b, int head) {
     constexpr int kU = 4;
     const int n = p.H * p.W * 4;  // float4 groups of this head's 16 channels
+    const int64_t ps = (int64_t)p.B * p.ob;  // elements between the aux planes
     float* A = p.out + b * p.ob + head * kD;
-    const float* Bp = p.aux + b * p.ob + head * kD;
+    const float* P1 = p.aux + b * p.ob + head * kD;
     const __nv_bfloat16* add =
         p.addend ? static_cast<const __nv_bfloat16*>(p.addend) + b * p.ab + head * kD : nullptr;
     for (int i0 = threadIdx.x; i0 < n; i0 += kThreads * kU) {
@@ -610,8 +539,11 @@ __device__ __forceinline__ void fold_planes(const ScanParams& p, int b, int head
             s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i < n) {
                 const float4 a = *reinterpret_cast<const float4*>(A + off[u]);
-                const float4 c = *reinterpret_cast<const float4*>(Bp + off[u]);
-                s[u] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+                const float4 c1 = *reinterpret_cast<const float4*>(P1 + off[u]);
+                const float4 c2 = *reinterpret_cast<const float4*>(P1 + ps + off[u]);
+                const float4 c3 = *reinterpret_cast<const float4*>(P1 + 2 * ps + off[u]);
+                s[u] = make_float4(((a.x + c1.x) + c2.x) + c3.x, ((a.y + c1.y) + c2.y) + c3.y,
+                                   ((a.z + c1.z) + c2.z) + c3.z, ((a.w + c1.w) + c2.w) + c3.w);
                 if (add) {
                     const float4 e = load4(add + off[u]);
                     s[u] = make_float4(s[u].x + e.x, s[u].y + e.y, s[u].z + e.z, s[u].w + e.w);
@@ -633,10 +565,9 @@ __global__ void __launch_bounds__(kThreads, VH_WPC_MIN_BLOCKS) srnl_warp_kernel(
     const int warp = threadIdx.x >> 5;
     ChainSmem& cs = reinterpret_cast<ChainSmem*>(smem_raw)[warp];
     const Role ro = warp_role<KIND>(p, warp);
-    // A scan pair is valid or invalid as a whole, so each pair barrier sees both its warps.
     if (ro.valid) scan_chain<KIND != kKindSeq>(p, cs, ro);
     if constexpr (KIND == kKindBoth) {
-        __syncthreads();  // both planes of this (b, head) are complete
+        __syncthreads();  // the four planes of this (b, head) are complete
         fold_planes(p, ro.b, ro.head);
     }
 }

@@ -27,8 +27,9 @@ def spatial_forward(states, x, q, d_skip, weights, height, width, head_dim, *, l
     layout "packed": x is [B, 4, heads, L, D], q is [B, 4, L, C].
     layout "image":  x, q are one channels-last image each ([B, H, W, C] or any tensor whose
                      pixel p / channel c element sits at b*sB + p*sP + c); scans are index maps.
-    concurrent:      give the library a second fp32 plane so the row and column scans run in
-                     one launch (used where the warp-per-chain scan applies).
+    concurrent:      give the library three fp32 workspace planes so the four scans run in one
+                     launch, each into its own plane (used where the warp-per-chain scan
+                     applies).
     final_dtype:     return a new [B, H, W, C] tensor of this dtype holding the sum plus
                      `addend` (x's dtype, [B, H, W, C] with unit channel stride), written by the
                      scan launch itself when it runs concurrently; `out` is then scratch.
@@ -85,7 +86,7 @@ def spatial_forward(states, x, q, d_skip, weights, height, width, head_dim, *, l
         raise RuntimeError("direction weights must be fp32 [4, C]")
     if out is None:
         out = torch.empty((B, H, W, C), device=dev, dtype=torch.float32)
-    aux = torch.empty_like(out) if concurrent else None
+    aux = torch.empty(3 * B * out.stride(0), device=dev, dtype=torch.float32) if concurrent else None
     final = None
     if final_dtype is not None:
         final = torch.empty((B, H, W, C), device=dev, dtype=final_dtype)
