@@ -25,8 +25,9 @@
 //       and the serial dependence per token is one FMA and one multiply.
 //   P3  S <- S G (inference_recurrence.cuh:110-135) as tensor-core MMAs over split operands
 //       (6 of the 9 split products; the dropped ones are below 2^-24 relative).
-// The memories live only as their three bf16 parts (hi + mid + lo reproduce the fp32 value to
-// 2^-24), plus e and a in fp32.
+// The memories, e and a live only as their three exact bf16 parts (the truncation split: the
+// parts sum to the fp32 value exactly); x.e and x.a come out of the projection MMA as an extra
+// column tile.
 //
 // Spatial output: every scan stores w_d (y + s_d x) for each pixel it visits into its own
 // plane (one plain store per pixel and scan, no read-back, no ordering between scans); the
@@ -52,15 +53,27 @@ constexpr int kKP = 20;    // padded row stride (floats) of the per-token key ro
 
 // Per-warp (per-chain) shared memory.
 struct alignas(16) ChainSmem {
-    unsigned char mb[kSplits][48][32];  // split memory rows: 0-15 M_m, 16-31 M_v, 32-47 M_k
-    float ea[2][kD];                    // e (learning-rate memory) and a (retention memory)
+    // The stacked state as three exact bf16 parts: rows 0-15 M_m, 16-31 M_v, 32-47 M_k,
+    // 48 e (learning-rate memory), 49 a (retention memory), 50-63 zero.
+    unsigned char mb[kSplits][64][32];
     float kt[kTile][kKP];               // raw k~, then the normalized key k
     float dt[kTile][kKP];               // raw v, then d = k - v
     float4 gate[kTile];                 // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
-    unsigned char gs[kSplits][16][32];  // split gain rows (row-major, k x n)
     float fw[2][kD];                    // spatial: this scan's fusion weight and skip per channel
     unsigned char xq[2][kTile][32];     // the step's x and raw q token rows (bf16, swizzled)
 };
+static_assert(kSplits * 16 * 32 <= (int)sizeof(float) * kTile * kKP, "gain parts must fit the key rows");
+
+// The three bf16 parts of G (row-major, k x n) live in the key rows during the boundary
+// refresh, when no token data is held there.
+__device__ __forceinline__ unsigned char* gain_parts(ChainSmem& cs, int k) {
+    return reinterpret_cast<unsigned char*>(&cs.kt[0][0]) + k * 16 * 32;
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const unsigned char* p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r[0]), "=r"(r[1]) : "r"(a));
+}
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const unsigned char* p) {
     const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -85,6 +98,23 @@ __device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSp
             lo -= __uint_as_float(ul & 0xffff0000u);
             hi -= __uint_as_float(uh & 0xffff0000u);
         }
+    }
+}
+
+// Stores one 16-value row of the stacked state as its three bf16 parts.
+__device__ __forceinline__ void put_row_splits(ChainSmem& cs, int r, const float* v) {
+    uint32_t w[kSplits][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t parts[kSplits];
+        split3(v[2 * i], v[2 * i + 1], parts);
+#pragma unroll
+        for (int k = 0; k < kSplits; ++k) w[k][i] = parts[k];
+    }
+#pragma unroll
+    for (int k = 0; k < kSplits; ++k) {
+        *reinterpret_cast<uint4*>(&cs.mb[k][0][0] + swz(r, 0)) = make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]);
+        *reinterpret_cast<uint4*>(&cs.mb[k][0][0] + swz(r, 1)) = make_uint4(w[k][4], w[k][5], w[k][6], w[k][7]);
     }
 }
 
@@ -187,21 +217,23 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
     // ---- state set-up: split memories, e/a, and this lane's fusion weights -------------
     const int64_t sidx = p.mem_per_chain ? ((int64_t)ro.b * p.R + dir) * p.heads + ro.head
                                          : (int64_t)dir * p.heads + ro.head;
-    for (int r = lane; r < 48; r += 32) {
-        const float* src = r < 16 ? p.Mm + (sidx * kD + r) * kD
-                         : r < 32 ? p.Mv + (sidx * kD + r - 16) * kD
-                                  : p.Mk + (sidx * kD + r - 32) * kD;
+    for (int r = lane; r < 64; r += 32) {
         float v[kD];
+        if (r < 48) {
+            const float* src = r < 16 ? p.Mm + (sidx * kD + r) * kD
+                             : r < 32 ? p.Mv + (sidx * kD + r - 16) * kD
+                                      : p.Mk + (sidx * kD + r - 32) * kD;
 #pragma unroll
-        for (int i = 0; i < kD; i += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(src + i);
-            v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+            for (int i = 0; i < kD; i += 4) {
+                const float4 f = *reinterpret_cast<const float4*>(src + i);
+                v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+            }
+        } else {
+            const float* src = r == 48 ? p.Me + sidx * kD : p.Ma + sidx * kD;
+#pragma unroll
+            for (int i = 0; i < kD; ++i) v[i] = r < 50 ? src[i] : 0.f;
         }
-        write_splits16(&cs.mb[0][0][0], r, v);
-    }
-    if (lane < kD) {
-        cs.ea[0][lane] = p.Me[sidx * kD + lane];
-        cs.ea[1][lane] = p.Ma[sidx * kD + lane];
+        put_row_splits(cs, r, v);
     }
     if constexpr (kSpatial) {
         if (lane < kD) {
@@ -296,7 +328,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
                 if (mt >= mtiles) break;  // warp-uniform
-                float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {};
+                float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {}, cea[4] = {};
                 // A fragments: {row qg, row qg+8} x {channels 2qt.., 8+2qt..}
                 uint32_t A_x[4], A_q[4];
                 ldsm_x4(A_x, &cs.xq[0][0][0] + swz(mt * 16 + (lane & 15), lane >> 4));
@@ -314,11 +346,10 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                     mma_16816(cv[1], A_x, bv[2], bv[3]);
                     mma_16816(ck[0], A_x, bk[0], bk[1]);
                     mma_16816(ck[1], A_x, bk[2], bk[3]);
+                    uint32_t bea[2];  // rows 48-55: e, a and zeros -> columns (x.e, x.a)
+                    ldsm_x2(bea, &cs.mb[k][0][0] + swz(48 + (lane & 7), (lane >> 3) & 1));
+                    mma_16816(cea, A_x, bea[0], bea[1]);
                 }
-                const float2 e_lo = *reinterpret_cast<const float2*>(&cs.ea[0][2 * qt]);
-                const float2 e_hi = *reinterpret_cast<const float2*>(&cs.ea[0][8 + 2 * qt]);
-                const float2 a_lo = *reinterpret_cast<const float2*>(&cs.ea[1][2 * qt]);
-                const float2 a_hi = *reinterpret_cast<const float2*>(&cs.ea[1][8 + 2 * qt]);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     // Lane (qg, qt) holds channels {2qt, 2qt+1, 8+2qt, 9+2qt} of token row qg + 8h.
@@ -329,14 +360,10 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                     *reinterpret_cast<float2*>(&cs.kt[row][8 + 2 * qt]) = make_float2(ck[1][2 * h], ck[1][2 * h + 1]);
                     *reinterpret_cast<float2*>(&cs.dt[row][2 * qt]) = make_float2(cv[0][2 * h], cv[0][2 * h + 1]);
                     *reinterpret_cast<float2*>(&cs.dt[row][8 + 2 * qt]) = make_float2(cv[1][2 * h], cv[1][2 * h + 1]);
-                    float qs = q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y;
-                    float ep = x01.x * e_lo.x + x01.y * e_lo.y + x23.x * e_hi.x + x23.y * e_hi.y;
-                    float ap = x01.x * a_lo.x + x01.y * a_lo.y + x23.x * a_hi.x + x23.y * a_hi.y;
-                    qs = quad_sum(qs);
-                    ep = quad_sum(ep);
-                    ap = quad_sum(ap);
-                    if (qt == 0) *reinterpret_cast<float2*>(&cs.gate[row]) = make_float2(ep, ap);
-                    const float qinv = 1.f / fmaxf(sqrtf(qs), 1e-12f);
+                    const float qs = quad_sum(q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y);
+                    if (qt == 0) *reinterpret_cast<float2*>(&cs.gate[row]) = make_float2(cea[2 * h], cea[2 * h + 1]);
+                    // 1 / max(||q||, 1e-12) (inference_recurrence.cuh:45)
+                    const float qinv = rsqrtf(fmaxf(qs, 1e-24f));
                     const float y0 = cy[0][2 * h] * qinv, y1 = cy[0][2 * h + 1] * qinv;
                     const float y2 = cy[1][2 * h] * qinv, y3 = cy[1][2 * h + 1] * qinv;
                     if constexpr (kSpatial) {
@@ -443,18 +470,18 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
             }
 #pragma unroll
             for (int k = 0; k < kSplits; ++k)
-                *reinterpret_cast<uint4*>(&cs.gs[k][0][0] + swz(p2_row, p2_half)) =
+                *reinterpret_cast<uint4*>(gain_parts(cs, k) + swz(p2_row, p2_half)) =
                     make_uint4(gp[k][0][0], gp[k][0][1], gp[k][1][0], gp[k][1][1]);
             __syncwarp();
             uint32_t bg[kSplits][4];
 #pragma unroll
-            for (int k = 0; k < kSplits; ++k) ldsm_x4_trans(bg[k], &cs.gs[k][0][0] + swz(lane & 15, lane >> 4));
+            for (int k = 0; k < kSplits; ++k) ldsm_x4_trans(bg[k], gain_parts(cs, k) + swz(lane & 15, lane >> 4));
             // Products kept: (A part, G part) in {(0,0),(0,1),(1,0),(0,2),(2,0),(1,1)}.
             constexpr int kPa[6] = {0, 0, 1, 0, 2, 1};
             constexpr int kPg[6] = {0, 1, 0, 2, 0, 1};
             float acc[4][2][4] = {};
 #pragma unroll
-            for (int mt = 0; mt < 3; ++mt) {
+            for (int mt = 0; mt < 4; ++mt) {  // rows 0-47 memories, 48-63 e, a and zeros
                 uint32_t am[kSplits][4];
 #pragma unroll
                 for (int k = 0; k < kSplits; ++k)
@@ -465,27 +492,9 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                     mma_16816(acc[mt][1], am[kPa[q]], bg[kPg[q]][2], bg[kPg[q]][3]);
                 }
             }
-            {  // e and a: rows 0 and 1 of a fourth tile, split in registers
-                uint32_t ae[kSplits][4] = {};
-                if (qg < 2) {
-                    uint32_t lo[kSplits], hi[kSplits];
-                    split3(cs.ea[qg][2 * qt], cs.ea[qg][2 * qt + 1], lo);
-                    split3(cs.ea[qg][8 + 2 * qt], cs.ea[qg][9 + 2 * qt], hi);
+            __syncwarp();  // every lane has read the old state parts
 #pragma unroll
-                    for (int k = 0; k < kSplits; ++k) {
-                        ae[k][0] = lo[k];
-                        ae[k][2] = hi[k];
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 6; ++q) {
-                    mma_16816(acc[3][0], ae[kPa[q]], bg[kPg[q]][0], bg[kPg[q]][1]);
-                    mma_16816(acc[3][1], ae[kPa[q]], bg[kPg[q]][2], bg[kPg[q]][3]);
-                }
-            }
-            __syncwarp();  // every lane has read the old memory parts
-#pragma unroll
-            for (int mt = 0; mt < 3; ++mt)
+            for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int r = mt * 16 + qg + 8 * h;
@@ -498,10 +507,6 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                             *reinterpret_cast<uint32_t*>(&cs.mb[k][0][0] + swz(r, nt) + 4 * qt) = parts[k];
                     }
                 }
-            if (qg < 2) {
-                *reinterpret_cast<float2*>(&cs.ea[qg][2 * qt]) = make_float2(acc[3][0][0], acc[3][0][1]);
-                *reinterpret_cast<float2*>(&cs.ea[qg][8 + 2 * qt]) = make_float2(acc[3][1][0], acc[3][1][1]);
-            }
             __syncwarp();
         }
     }
