@@ -229,13 +229,15 @@ int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight, const 
  *   VH_DW_RESID  y = x + (conv(x) + b)
  *   VH_DW_GATE   y = x + sigmoid(gate) * (conv(x) + b)
  *   VH_DW_GELU   h = gelu(x);  y = gelu(h + conv(h) + b)      (gelu: exact erf form)
+ *   VH_DW_RESID_ADD  s = x + r (r in `gate`, gate_dtype);  y = s + (conv(s) + b): the block's
+ *                cpe applied to the previous block's output without materialising it
  * x, gate, y: dense [B, H, W, C] of `dtype` (VH_F32 or VH_BF16), 16-byte aligned, y distinct
  * from the inputs; weight fp32 [C, K, K] (nn.Conv2d's [C, 1, K, K]); bias fp32 [C];
  * C a multiple of 8.  The convolution reads input, weight and bias rounded to bf16 and sums in
  * fp32 (a bf16 convolution under autocast); the residual and gate terms use x and gate as
  * given; y is rounded once.
  * -------------------------------------------------------------------------------------*/
-enum vh_dw_mode { VH_DW_BIAS = 0, VH_DW_RESID = 1, VH_DW_GATE = 2, VH_DW_GELU = 3 };
+enum vh_dw_mode { VH_DW_BIAS = 0, VH_DW_RESID = 1, VH_DW_GATE = 2, VH_DW_GELU = 3, VH_DW_RESID_ADD = 4 };
 
 typedef struct {
     const void* x;
@@ -247,9 +249,33 @@ typedef struct {
     int32_t mode;
     int32_t ksize;
     int32_t batch, height, width, channels;
+    int32_t gate_dtype; /* VH_DW_RESID_ADD: dtype of the addend r (fp32 or bf16) */
 } vh_dwconv_args;
 
 int vh_dwconv_fwd(const vh_dwconv_args* args, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Bias and activation over channels-last rows: y[r, c] = act(x[r, c] + bias[c]), computed in
+ * fp32 and rounded once to y's dtype.  The epilogue of a convolution with its eval-mode
+ * BatchNorm folded in (the stem and downsample layers of models/layers.py:85-107: conv, BN,
+ * GELU).  act: VH_ACT_NONE or VH_ACT_GELU (exact erf form).  x, y: [rows, C], C a multiple of
+ * 8, 16-byte aligned; bias fp32 [C].
+ * -------------------------------------------------------------------------------------*/
+enum vh_act { VH_ACT_NONE = 0, VH_ACT_GELU = 1 };
+
+int vh_bias_act_fwd(const void* x, int32_t x_dtype, const float* bias, void* y, int32_t y_dtype,
+                    int64_t rows, int32_t channels, int32_t act, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Residual add followed by LayerNorm over channels-last rows (models/block.py:105-106, the
+ * block's `x + branch` then `norm2`):  s = x + r is written to sum_out (x's dtype; may be x
+ * itself) and y = LayerNorm(s) to y (y_dtype), with the statistics of the stored s.
+ * x, sum_out: [rows, C] of x_dtype; r: [rows, C] of r_dtype; C a multiple of 8; all
+ * 16-byte aligned.
+ * -------------------------------------------------------------------------------------*/
+int vh_add_layernorm_fwd(const void* x, int32_t x_dtype, const void* r, int32_t r_dtype, void* sum_out,
+                         const float* weight, const float* bias, float eps, void* y, int32_t y_dtype,
+                         int64_t rows, int32_t channels, vh_stream_t stream);
 
 /* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
  * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it

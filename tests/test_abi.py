@@ -64,7 +64,8 @@ def _c_layout(struct, fields):
 @pytest.mark.parametrize("struct,cls", [("vh_srnl_spatial_args", "VhSpatialArgs"),
                                         ("vh_srnl_sequence_args", "VhSequenceArgs"),
                                         ("vh_srnl_consts", "VhConsts"),
-                                        ("vh_srnl_memories", "VhMemories")])
+                                        ("vh_srnl_memories", "VhMemories"),
+                                        ("vh_dwconv_args", "VhDwconvArgs")])
 def test_ctypes_mirrors_match_the_header(struct, cls):
     """Every field of the ctypes mirrors sits at the offset the C compiler gives it."""
     from visionhope_b200 import _lib

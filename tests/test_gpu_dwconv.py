@@ -28,6 +28,11 @@ def _expected(x, conv, mode, gate):
         return conv_out
     if mode == "resid":
         return x.double() + conv_out
+    if mode == "resid_add":
+        s = x.double() + gate.double()
+        s_conv = bf(s.to(x.dtype)) if x.dtype == torch.bfloat16 else bf(s)
+        s_ref = s.to(x.dtype).double()
+        return s_ref + F.conv2d(s_conv, bf(conv.weight), bf(conv.bias), padding=k // 2, groups=x.shape[1])
     if mode == "gate":
         return x.double() + torch.sigmoid(gate.double()) * conv_out
     return F.gelu(xin + conv_out)
@@ -47,6 +52,8 @@ CASES = [
     (1, 16, 16, 32, 5, "resid", torch.bfloat16),  # 16 x 16 tiles
     (2, 64, 28, 42, 7, "bias", torch.bfloat16),   # 14 x 14 tiles, several per image
     (1, 8, 7, 7, 7, "gate", torch.float32),       # kernel wider than half the image
+    (2, 64, 14, 14, 3, "resid_add", torch.float32),   # cpe of x + a pending bf16 residual
+    (1, 32, 9, 13, 3, "resid_add", torch.bfloat16),
 ]
 
 
@@ -61,8 +68,13 @@ def test_dwconv_matches_reference(case, cuda):
         conv.bias.normal_(0, 0.3)
     x = torch.randn(B, C, H, W, device=cuda).to(dt).contiguous(memory_format=torch.channels_last)
     gate = torch.randn_like(x) if mode == "gate" else None
+    if mode == "resid_add":
+        gate = torch.randn(x.shape, device=cuda).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
     with torch.inference_mode():
-        y = depthwise_fused(x, conv, mode, gate=gate)
+        if mode == "resid_add":
+            y = depthwise_fused(x, conv, "resid", addend=gate)
+        else:
+            y = depthwise_fused(x, conv, mode, gate=gate)
     assert y.dtype == dt and y.shape == x.shape and y.is_contiguous(memory_format=torch.channels_last)
     exp = _expected(x, conv, mode, gate)
     tol = 4e-3 if dt == torch.bfloat16 else (1e-3 if mode == "gelu" else 1e-5)

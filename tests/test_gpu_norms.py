@@ -126,3 +126,46 @@ def test_norms_emit_half_outputs(out, oracle, cuda):
     l32 = layernorm_rows(rows, w, bb, 1e-6)
     l16 = layernorm_rows(rows, w, bb, 1e-6, out_dtype=DT[out])
     assert l16.dtype == DT[out] and torch.equal(l16, l32.to(DT[out]))
+
+
+@pytest.mark.parametrize("xdt,rdt,ydt", [("f32", "bf16", "bf16"), ("f32", "f32", "f32"), ("bf16", "bf16", "bf16")])
+def test_add_layernorm(xdt, rdt, ydt, oracle, cuda):
+    """s = x + r stored in x's dtype and LayerNorm of the stored s, against the oracle."""
+    from visionhope_b200.utils.layer_norm_cuda import add_layernorm_rows, layernorm_rows
+
+    gen = np.random.default_rng(13)
+    for rows, C in ((777, 64), (1000, 256), (33, 512)):
+        x = _dev(gen.normal(size=(rows, C)), cuda, DT[xdt])
+        r = _dev(gen.normal(size=(rows, C)), cuda, DT[rdt])
+        w = _dev(gen.normal(1, 0.02, size=C), cuda)
+        b = _dev(gen.normal(0, 0.02, size=C), cuda)
+        s_exp = (x.float() + r.float()).to(DT[xdt])
+        s, y = add_layernorm_rows(x.clone(), r, w, b, 1e-6, out_dtype=DT[ydt])
+        assert torch.equal(s, s_exp)
+        exp = oracle.layernorm_rows(s_exp.float(), w, b)
+        tol = 1e-5 if ydt == "f32" else 4e-3
+        assert rel_err(y.float().cpu().numpy(), exp) < tol
+        # in place into x
+        x2 = x.clone()
+        s2, y2 = add_layernorm_rows(x2, r, w, b, 1e-6, out_dtype=DT[ydt])
+        assert s2.data_ptr() == x2.data_ptr() and torch.equal(x2, s_exp) and torch.equal(y2, y)
+
+
+@pytest.mark.parametrize("act", [None, "gelu"])
+@pytest.mark.parametrize("io", [("bf16", "bf16"), ("bf16", "f32"), ("f32", "f32")])
+def test_bias_act(act, io, cuda):
+    """act(x + b) in fp32, rounded once: against float64 PyTorch (exact erf GELU)."""
+    import torch.nn.functional as F
+
+    from visionhope_b200.utils.bias_act import bias_act
+
+    gen = np.random.default_rng(17)
+    x = _dev(gen.normal(size=(3, 9, 11, 48)) * 2, cuda, DT[io[0]]).permute(0, 3, 1, 2)
+    b = _dev(gen.normal(size=48), cuda)
+    y = bias_act(x, b, act, out_dtype=DT[io[1]])
+    exp = x.double() + b.double().view(1, -1, 1, 1)
+    if act == "gelu":
+        exp = F.gelu(exp)
+    assert y.dtype == DT[io[1]] and y.is_contiguous(memory_format=torch.channels_last)
+    tol = 4e-3 if io[1] == "bf16" else 1e-6
+    assert rel_err(y.double().cpu().numpy(), exp.cpu().numpy()) < tol

@@ -19,10 +19,11 @@ from torch.nn import functional as F
 from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
+from .utils.bias_act import bias_act
 from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_forward
 from .utils.inference import cache_half_weights, linear_cached
-from .utils.layer_norm_cuda import layernorm_rows
+from .utils.layer_norm_cuda import add_layernorm_rows, layernorm_rows
 
 
 def _autocast_dtype():
@@ -82,6 +83,27 @@ class LayerNorm2d(nn.Module):
         y = layernorm_rows(rows.reshape(b * h * w, c), self.weight, self.bias, self.eps, out_dtype=out_dtype)
         return y.view(b, h, w, c).permute(0, 3, 1, 2)
 
+    def forward_add(self, x, r, inplace=False):
+        """(x + r, LayerNorm(x + r)) for a channels-last CUDA x and r of its shape: the residual
+        add and this norm in one pass (the sum goes into x itself when ``inplace``).  Falls
+        back to the two operations when the fused kernel does not apply."""
+        b, c, h, w = x.shape
+        if (x.is_cuda and not torch.is_grad_enabled() and c % 8 == 0 and c <= 2048
+                and x.dtype in (torch.float32, torch.bfloat16) and r.dtype in (torch.float32, torch.bfloat16)
+                and torch.promote_types(x.dtype, r.dtype) == x.dtype and r.shape == x.shape
+                and x.is_contiguous(memory_format=torch.channels_last)
+                and r.is_contiguous(memory_format=torch.channels_last)):
+            out_dtype = torch.float32
+            if self.emit_autocast_dtype and _autocast_dtype() in (torch.bfloat16, torch.float16):
+                out_dtype = _autocast_dtype()
+            s = x if inplace else torch.empty_like(x, memory_format=torch.channels_last)
+            rows = lambda t: t.permute(0, 2, 3, 1).reshape(b * h * w, c)
+            _, y = add_layernorm_rows(rows(x), rows(r), self.weight, self.bias, self.eps, out_dtype=out_dtype,
+                                      sum_out=rows(s))
+            return s, y.view(b, h, w, c).permute(0, 3, 1, 2)
+        x = x + r
+        return x, self(x)
+
 
 def build_norm(dim, norm_layer="group"):
     if norm_layer == "group":
@@ -130,6 +152,13 @@ class FeedForwardNetwork(nn.Module):
         return self.drop(pointwise(self.fc2, self.drop(x)))
 
 
+def _fused_epilogue_ok(x):
+    """bf16 autocast inference on a channels-last CUDA input: the folded stem and downsample
+    layers then run their bias/GELU epilogue as one kernel."""
+    return (x.is_cuda and not torch.is_grad_enabled() and _autocast_dtype() == torch.bfloat16
+            and x.is_contiguous(memory_format=torch.channels_last))
+
+
 def _fold_conv_bn(conv, bn):
     """conv followed by eval-mode bn -> conv with w * g / sqrt(var + eps), (b - mean) * that + beta."""
     scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
@@ -163,6 +192,16 @@ class PatchEmbedding(nn.Module):
         self.norm = nn.Identity()
 
     def forward(self, x):
+        plan = getattr(self, "_folded_plan", None)
+        if plan is not None and _fused_epilogue_ok(x):
+            # Folded convolutions with the bias (and GELU) applied by one pointwise kernel in
+            # fp32: GELU outputs in the autocast dtype (the next convolution's input), the
+            # last layer in fp32, the dtype BatchNorm produced (the residual stream's).
+            for conv, gelu in plan:
+                y = F.conv2d(x, conv.weight, None, conv.stride, conv.padding)
+                x = bias_act(y, conv.bias, "gelu" if gelu else None,
+                             out_dtype=_autocast_dtype() if gelu else torch.float32)
+            return self.norm(x)
         return self.norm(self.proj(x))
 
     @torch.no_grad()
@@ -175,6 +214,13 @@ class PatchEmbedding(nn.Module):
                 layers[i + 1] = nn.Identity()
                 n += 1
         self.proj = nn.Sequential(*layers)
+        plan = []
+        for i, layer in enumerate(layers):
+            if isinstance(layer, nn.Conv2d):
+                nxt = [m for m in layers[i + 1:i + 3] if not isinstance(m, nn.Identity)]
+                plan.append((layer, bool(nxt) and _is_exact_gelu(nxt[0])))
+        if all(conv.bias is not None and conv.out_channels % 8 == 0 for conv, _ in plan):
+            self._folded_plan = plan
         return n
 
 
@@ -185,6 +231,9 @@ class Downsample(nn.Module):
         self.norm = nn.BatchNorm2d(out_dim)
 
     def forward(self, x):
+        if getattr(self, "_folded", False) and self.proj.out_channels % 8 == 0 and _fused_epilogue_ok(x):
+            y = F.conv2d(x, self.proj.weight, None, self.proj.stride, self.proj.padding)
+            return bias_act(y, self.proj.bias, None, out_dtype=torch.float32)  # BatchNorm's dtype
         return self.norm(self.proj(x))
 
     @torch.no_grad()
@@ -194,6 +243,7 @@ class Downsample(nn.Module):
             return 0
         _fold_conv_bn(self.proj, self.norm)
         self.norm = nn.Identity()
+        self._folded = True
         return 1
 
 
@@ -285,12 +335,34 @@ class VisionHOPEBlock(nn.Module):
         return x + branch if gamma is None else x + gamma * branch
 
     def forward(self, x):
+        x, pending = self.forward_deferred(x)
+        return x if pending is None else x + pending
+
+    def forward_deferred(self, x, pending=None):
+        """The block on x + pending, returning (x', r) whose sum is the block's output: the
+        last residual add is left to the next block, whose cpe adds it while reading its
+        input.  pending is None for the first block of a stage."""
         if self.training and self._inference_prepared:
             raise RuntimeError("A block with folded LayerScale weights cannot be trained")
         if self.cpe is not None:
-            x = depthwise_fused(x, self.cpe, "resid") if fusable(x, self.cpe) else x + self.cpe(x)
-        x = self._residual(x, self.spatial_branch(self.norm1(x)), self.gamma1)
-        return self._residual(x, self.ffn(self.norm2(x)), self.gamma2)
+            if fusable(x, self.cpe) and (pending is None or pending.is_contiguous(memory_format=torch.channels_last)):
+                x = depthwise_fused(x, self.cpe, "resid", addend=pending)
+            else:
+                x = x if pending is None else x + pending
+                x = x + self.cpe(x)
+        elif pending is not None:
+            x = x + pending
+        branch = self.spatial_branch(self.norm1(x))
+        if self.gamma1 is None and isinstance(self.norm2, LayerNorm2d):
+            # x + branch and norm2 in one pass; x is this block's own tensor once cpe ran
+            x, n2 = self.norm2.forward_add(x, branch, inplace=self.cpe is not None)
+        else:
+            x = self._residual(x, branch, self.gamma1)
+            n2 = self.norm2(x)
+        ffn = self.ffn(n2)
+        if self.gamma2 is not None:
+            return x + self.gamma2 * ffn, None
+        return x, ffn
 
 
 def initialize_weights(module):
@@ -349,16 +421,29 @@ class HierarchicalVisionHOPE(nn.Module):
         self.head = nn.Linear(self.num_features, num_classes)
         self.apply(initialize_weights)
 
+    @staticmethod
+    def _run_stage(stage, x):
+        """The stage's blocks with each block's last residual add carried into the next block's
+        cpe (one fused pass); the stage's final add is made here."""
+        pending = None
+        for blk in stage:
+            if isinstance(blk, VisionHOPEBlock):
+                x, pending = blk.forward_deferred(x, pending)
+            else:
+                x = blk(x if pending is None else x + pending)
+                pending = None
+        return x if pending is None else x + pending
+
     def forward_intermediates(self, x):
         outs = []
         for down, stage in zip(self.downsample_layers, self.stages):
-            x = stage(down(x))
+            x = self._run_stage(stage, down(x))
             outs.append(x)
         return tuple(outs)
 
     def forward_features(self, x):
         for down, stage in zip(self.downsample_layers, self.stages):
-            x = stage(down(x))
+            x = self._run_stage(stage, down(x))
         x = self.head_act(self.head_norm(self.head_pre_logits(self.norm(x))))
         return x.mean(dim=[2, 3])
 

@@ -3,6 +3,7 @@
 // The block (models/block.py) runs four depthwise convolutions per layer, each followed by
 // elementwise work that PyTorch issues as separate passes over HBM:
 //   cpe             x + (conv3x3(x) + b)                          block.py:100
+//                   (optionally of s = x + r: the previous block's pending FFN residual)
 //   local features  inner + sigmoid(gate) * (conv7x7(inner) + b)  block.py:57-62
 //   output position conv5x5(x_local) + b                          block.py:78
 //   FFN             h = gelu(fc1); gelu(h + conv3x3(h) + b)        layers.py (FeedForward)
@@ -24,6 +25,7 @@
 
 #include "abi_util.h"
 #include "common.cuh"
+#include "activations.cuh"
 #include "f32x2.cuh"
 
 namespace vh {
@@ -33,40 +35,6 @@ constexpr int kDwCG = 32;  // channels per CTA (a staged pixel is 32 floats)
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// gelu(x) = x/2 (1 + erf(x / sqrt 2)) for two lanes.  With a = |z|, t = 1 / (1 + p a),
-// erfc(a) ~= t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2)  (A&S 7.1.26), and
-// 1 + erf(z) = 1 + sign(z) (1 - erfc(a)), so gelu = h + h sign(z) (1 - erfc(a)) with h = x/2.
-// exp and the reciprocal use the hardware approximations directly (relative error near
-// 2^-22, far inside the bf16 rounding every GELU output here receives).
-__device__ __forceinline__ float ex2_approx(float v) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
-}
-__device__ __forceinline__ float rcp_approx(float v) {
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
-}
-__device__ __forceinline__ float2 gelu2(float2 x) {
-    constexpr float kP = 0.3275911f, kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f,
-                    kA4 = -1.453152027f, kA5 = 1.061405429f;
-    constexpr float kLog2e = 1.4426950408889634f;
-    const float2 z = fmul2(x, splat2(0.70710678118654752f));
-    const float2 d = ffma2(make_float2(fabsf(z.x), fabsf(z.y)), splat2(kP), splat2(1.f));
-    const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-    float2 q = ffma2(t, splat2(kA5), splat2(kA4));
-    q = ffma2(q, t, splat2(kA3));
-    q = ffma2(q, t, splat2(kA2));
-    q = ffma2(q, t, splat2(kA1));
-    q = fmul2(q, t);
-    const float2 arg = fmul2(fmul2(z, z), splat2(-kLog2e));
-    const float2 c = fmul2(q, make_float2(ex2_approx(arg.x), ex2_approx(arg.y)));  // erfc(|z|)
-    const float2 om = ffma2(c, splat2(-1.f), splat2(1.f));                           // 1 - erfc(|z|)
-    const float2 sg = make_float2(copysignf(om.x, z.x), copysignf(om.y, z.y));
-    const float2 h = fmul2(x, splat2(0.5f));
-    return ffma2(h, sg, h);
-}
 __device__ __forceinline__ float sigmoid_f(float v) {
     return rcp_approx(1.f + ex2_approx(v * -1.4426950408889634f));
 }
@@ -106,8 +74,8 @@ struct DwGeom {
     static constexpr size_t kSmem = sizeof(float) * ((size_t)XS + K * K * kDwCG + kDwCG);
 };
 
-template <int K, int MODE, typename T, int TC, int RG, int R>
-__global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const T* __restrict__ gate,
+template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
+__global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const GT* __restrict__ gate,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, T* __restrict__ y,
                                                                 int H, int W, int C, int tiles_w) {
@@ -133,6 +101,7 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
 #pragma unroll
     for (int i0 = 0; i0 < IT; i0 += BATCH) {
         Raw8<T> raw[BATCH];
+        Raw8<GT> rawa[MODE == VH_DW_RESID_ADD ? BATCH : 1];
         bool live[BATCH];
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
@@ -140,7 +109,10 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
             const int v = i & 3, pix = i >> 2;
             const int gy = oy0 + pix / IW - P, gx = ox0 + pix % IW - P, c = c0 + 8 * v;
             live[u] = i0 + u < IT && i < NV && gy >= 0 && gy < H && gx >= 0 && gx < W && c < C;
-            if (live[u]) raw[u].load(x + img + ((int64_t)gy * W + gx) * C + c);
+            if (live[u]) {
+                raw[u].load(x + img + ((int64_t)gy * W + gx) * C + c);
+                if (MODE == VH_DW_RESID_ADD) rawa[MODE == VH_DW_RESID_ADD ? u : 0].load(gate + img + ((int64_t)gy * W + gx) * C + c);
+            }
         }
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
@@ -149,6 +121,20 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
             float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             if (live[u]) {
                 raw[u].to_float(f);
+                if (MODE == VH_DW_RESID_ADD) {  // the pending residual: s = x + addend
+                    float a8[8];
+                    rawa[MODE == VH_DW_RESID_ADD ? u : 0].to_float(a8);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] += a8[e];
+                    if (std::is_same<T, __nv_bfloat16>::value) {  // s is stored in x's dtype
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2) {
+                            const float2 r2 = __bfloat1622float2(__floats2bfloat162_rn(f[e], f[e + 1]));
+                            f[e] = r2.x;
+                            f[e + 1] = r2.y;
+                        }
+                    }
+                }
                 if (MODE == VH_DW_GELU) {
 #pragma unroll
                     for (int e = 0; e < 8; e += 2) {
@@ -206,18 +192,22 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
         if (oy >= H) break;
         const int64_t off = img + ((int64_t)oy * W + ox) * C + c;
         float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
-        if (MODE == VH_DW_RESID || MODE == VH_DW_GATE) {
+        if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || MODE == VH_DW_GATE) {
             // The centre value itself: from the staged tile when the input is bf16 (staged
             // exactly), else from global memory (the tile holds it rounded to bf16).
             float2 xc[2];
             if (std::is_same<T, __nv_bfloat16>::value) {
                 lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, xc);
             } else {
-                const float4 t4 = load4(x + off);
+                float4 t4 = load4(x + off);
+                if (MODE == VH_DW_RESID_ADD) {
+                    const float4 a4 = load4(gate + off);
+                    t4 = make_float4(t4.x + a4.x, t4.y + a4.y, t4.z + a4.z, t4.w + a4.w);
+                }
                 xc[0] = make_float2(t4.x, t4.y);
                 xc[1] = make_float2(t4.z, t4.w);
             }
-            if (MODE == VH_DW_RESID) {
+            if (MODE != VH_DW_GATE) {
                 o[0] = fadd2(xc[0], o[0]);
                 o[1] = fadd2(xc[1], o[1]);
             } else {
@@ -235,16 +225,16 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
     }
 }
 
-template <int K, int MODE, typename T, int TC, int RG, int R>
+template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
 int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
     using G = DwGeom<K, TC, RG, R>;
     const int tiles_w = (a.width + TC - 1) / TC, tiles_h = (a.height + G::TH - 1) / G::TH;
     const dim3 grid(tiles_w * tiles_h, (a.channels + kDwCG - 1) / kDwCG, a.batch);
-    const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, TC, RG, R>);
+    const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, TC, RG, R>);
     if (!ensure_smem_attr(fn, G::kSmem))
         return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", G::kSmem);
-    dwconv_kernel<K, MODE, T, TC, RG, R><<<grid, G::NT, G::kSmem, st>>>(
-        static_cast<const T*>(a.x), static_cast<const T*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
+    dwconv_kernel<K, MODE, T, GT, TC, RG, R><<<grid, G::NT, G::kSmem, st>>>(
+        static_cast<const T*>(a.x), static_cast<const GT*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
         a.height, a.width, a.channels, tiles_w);
     return launch_status("depthwise conv");
 }
@@ -252,23 +242,23 @@ int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
 // Tile: the shape among 14 x 14 (224 threads, 7 rows each; divides every VisionHOPE stage
 // size from 14 up), 16 x 16 (256 threads, 8 rows each) and 8 x 8 (256 threads, 2 rows each)
 // that covers the image with the least padding, in that order of preference.
-template <int K, int MODE, typename T>
+template <int K, int MODE, typename T, typename GT>
 int dw_tile(const vh_dwconv_args& a, cudaStream_t st) {
     auto area = [&](int th, int tc) {
         return (int64_t)((a.height + th - 1) / th) * th * (int64_t)((a.width + tc - 1) / tc) * tc;
     };
     const int64_t a14 = area(14, 14), a16 = area(16, 16), a8 = area(8, 8);
-    if (a14 <= a16 && a14 <= a8) return dw_launch<K, MODE, T, 14, 2, 7>(a, st);
-    if (a16 <= a8) return dw_launch<K, MODE, T, 16, 2, 8>(a, st);
-    return dw_launch<K, MODE, T, 8, 4, 2>(a, st);
+    if (a14 <= a16 && a14 <= a8) return dw_launch<K, MODE, T, GT, 14, 2, 7>(a, st);
+    if (a16 <= a8) return dw_launch<K, MODE, T, GT, 16, 2, 8>(a, st);
+    return dw_launch<K, MODE, T, GT, 8, 4, 2>(a, st);
 }
 
-template <int MODE, typename T>
+template <int MODE, typename T, typename GT = T>
 int dw_k(const vh_dwconv_args& a, cudaStream_t st) {
     switch (a.ksize) {
-        case 3: return dw_tile<3, MODE, T>(a, st);
-        case 5: return dw_tile<5, MODE, T>(a, st);
-        default: return dw_tile<7, MODE, T>(a, st);
+        case 3: return dw_tile<3, MODE, T, GT>(a, st);
+        case 5: return dw_tile<5, MODE, T, GT>(a, st);
+        default: return dw_tile<7, MODE, T, GT>(a, st);
     }
 }
 
@@ -278,6 +268,9 @@ int dw_mode(const vh_dwconv_args& a, cudaStream_t st) {
         case VH_DW_BIAS: return dw_k<VH_DW_BIAS, T>(a, st);
         case VH_DW_RESID: return dw_k<VH_DW_RESID, T>(a, st);
         case VH_DW_GATE: return dw_k<VH_DW_GATE, T>(a, st);
+        case VH_DW_RESID_ADD:
+            return a.gate_dtype == VH_F32 ? dw_k<VH_DW_RESID_ADD, T, float>(a, st)
+                                          : dw_k<VH_DW_RESID_ADD, T, __nv_bfloat16>(a, st);
         default: return dw_k<VH_DW_GELU, T>(a, st);
     }
 }
@@ -286,18 +279,18 @@ int dw_mode(const vh_dwconv_args& a, cudaStream_t st) {
 // the largest shared-memory share slows these kernels, whose halo loads hit in L1).
 void dw_attr_one(const void* fn, size_t smem) { ensure_smem_attr(fn, smem); }
 
-template <int K, int MODE, typename T>
+template <int K, int MODE, typename T, typename GT>
 void dw_attr_k() {
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 14, 2, 7>), DwGeom<K, 14, 2, 7>::kSmem);
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 16, 2, 8>), DwGeom<K, 16, 2, 8>::kSmem);
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, 8, 4, 2>), DwGeom<K, 8, 4, 2>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 14, 2, 7>), DwGeom<K, 14, 2, 7>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 16, 2, 8>), DwGeom<K, 16, 2, 8>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 8, 4, 2>), DwGeom<K, 8, 4, 2>::kSmem);
 }
 
-template <int MODE, typename T>
+template <int MODE, typename T, typename GT = T>
 void dw_attr_mode() {
-    dw_attr_k<3, MODE, T>();
-    dw_attr_k<5, MODE, T>();
-    dw_attr_k<7, MODE, T>();
+    dw_attr_k<3, MODE, T, GT>();
+    dw_attr_k<5, MODE, T, GT>();
+    dw_attr_k<7, MODE, T, GT>();
 }
 
 template <typename T>
@@ -306,6 +299,8 @@ void dw_attr_t() {
     dw_attr_mode<VH_DW_RESID, T>();
     dw_attr_mode<VH_DW_GATE, T>();
     dw_attr_mode<VH_DW_GELU, T>();
+    dw_attr_mode<VH_DW_RESID_ADD, T, float>();
+    dw_attr_mode<VH_DW_RESID_ADD, T, __nv_bfloat16>();
 }
 
 }  // namespace
@@ -327,9 +322,14 @@ using namespace vh;
 extern "C" int vh_dwconv_fwd(const vh_dwconv_args* a, vh_stream_t stream) {
     clear_error();
     if (!a) return fail(VH_E_ARG, "vh_dwconv_fwd: null args");
-    if (!a->x || !a->weight || !a->bias || !a->y || (a->mode == VH_DW_GATE && !a->gate))
+    if (!a->x || !a->weight || !a->bias || !a->y ||
+        ((a->mode == VH_DW_GATE || a->mode == VH_DW_RESID_ADD) && !a->gate))
         return fail(VH_E_ARG, "vh_dwconv_fwd: null pointer argument");
-    if (a->mode < VH_DW_BIAS || a->mode > VH_DW_GELU) return fail(VH_E_ARG, "vh_dwconv_fwd: bad mode %d", a->mode);
+    if (a->mode < VH_DW_BIAS || a->mode > VH_DW_RESID_ADD) return fail(VH_E_ARG, "vh_dwconv_fwd: bad mode %d", a->mode);
+    if (a->mode == VH_DW_RESID_ADD && a->gate_dtype != VH_F32 && a->gate_dtype != VH_BF16)
+        return fail(VH_E_DTYPE, "vh_dwconv_fwd: the addend must be fp32 or bf16");
+    if (a->mode == VH_DW_RESID_ADD && a->dtype == VH_BF16 && a->gate_dtype == VH_F32)
+        return fail(VH_E_DTYPE, "vh_dwconv_fwd: an fp32 addend needs fp32 x");
     if (a->ksize != 3 && a->ksize != 5 && a->ksize != 7)
         return fail(VH_E_SHAPE, "vh_dwconv_fwd: kernel size must be 3, 5 or 7 (got %d)", a->ksize);
     if (a->dtype != VH_F32 && a->dtype != VH_BF16)

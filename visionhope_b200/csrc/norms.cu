@@ -4,6 +4,7 @@
 #include <mutex>
 #include <set>
 #include <tuple>
+#include <type_traits>
 
 #include "abi_util.h"
 #include "common.cuh"
@@ -317,11 +318,16 @@ __global__ void __launch_bounds__(kLnThreads) ln_kernel(const T* __restrict__ x,
     }
 }
 
+// Residual operand type of ln8_kernel when there is no residual add.
+struct NoResidual {};
+
 // C a multiple of 8: SW lanes per row, each lane holds NV 8-channel vectors of R rows in
 // registers (all R * NV 16-byte loads are issued before any arithmetic), so enough bytes are
-// in flight per SM to run at HBM speed.  Same two in-register passes as ln_kernel.
-template <typename T, typename YT, int SW, int NV, int R>
-__global__ void __launch_bounds__(kLnThreads) ln8_kernel(const T* __restrict__ x,
+// in flight per SM to run at HBM speed.  Same two in-register passes as ln_kernel.  With a
+// residual operand (RT not NoResidual) each row is first replaced by s = x + r, stored to
+// sum_out in x's dtype (sum_out may be x), and normalized as stored.
+template <typename T, typename YT, int SW, int NV, int R, typename RT = NoResidual>
+__global__ void __launch_bounds__(kLnThreads) ln8_kernel(const T* x, const RT* __restrict__ radd, T* sum_out,
                                                          const float* __restrict__ w,
                                                          const float* __restrict__ bias, float eps,
                                                          YT* __restrict__ y, float* __restrict__ mean_out,
@@ -339,6 +345,16 @@ __global__ void __launch_bounds__(kLnThreads) ln8_kernel(const T* __restrict__ x
             const int g = lane + k * SW;
             if (row < rows && g < G8) {
                 load8(x + row * C + 8 * g, v[r][k]);
+                if constexpr (!std::is_same<RT, NoResidual>::value) {
+                    float rv[8];
+                    load8(radd + row * C + 8 * g, rv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[r][k][e] += rv[e];
+                    store8(sum_out + row * C + 8 * g, v[r][k]);
+                    if constexpr (!std::is_same<T, float>::value) {
+                        load8(sum_out + row * C + 8 * g, v[r][k]);  // normalize s as stored
+                    }
+                }
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) v[r][k][e] = 0.f;
@@ -554,9 +570,45 @@ int ln8_launch(const void* x, const float* w, const float* b, float eps, YT* y, 
                int64_t rows, int C, cudaStream_t st) {
     const int64_t rows_per_cta = (int64_t)(kLnThreads / SW) * R;
     const int64_t blocks = (rows + rows_per_cta - 1) / rows_per_cta;
-    ln8_kernel<T, YT, SW, NV, R><<<(unsigned)blocks, kLnThreads, 0, st>>>(static_cast<const T*>(x), w, b, eps,
-                                                                          y, m, r, rows, C);
+    ln8_kernel<T, YT, SW, NV, R><<<(unsigned)blocks, kLnThreads, 0, st>>>(
+        static_cast<const T*>(x), static_cast<const NoResidual*>(nullptr), static_cast<T*>(nullptr), w, b, eps,
+        y, m, r, rows, C);
     return launch_status("layernorm");
+}
+
+template <typename T, typename RT, typename YT, int SW, int NV, int R>
+int add_ln8_launch(const void* x, const void* radd, void* sum_out, const float* w, const float* b, float eps,
+                   YT* y, int64_t rows, int C, cudaStream_t st) {
+    const int64_t rows_per_cta = (int64_t)(kLnThreads / SW) * R;
+    const int64_t blocks = (rows + rows_per_cta - 1) / rows_per_cta;
+    ln8_kernel<T, YT, SW, NV, R, RT><<<(unsigned)blocks, kLnThreads, 0, st>>>(
+        static_cast<const T*>(x), static_cast<const RT*>(radd), static_cast<T*>(sum_out), w, b, eps, y, nullptr,
+        nullptr, rows, C);
+    return launch_status("add layernorm");
+}
+
+// Residual add + LayerNorm, C a multiple of 8 (checked by the entry point).
+template <typename T, typename RT, typename YT>
+int add_ln_run(const void* x, const void* radd, void* sum_out, const float* w, const float* b, float eps, YT* y,
+               int64_t rows, int C, cudaStream_t st) {
+    const int G8 = C / 8;
+    if (G8 <= 4) return add_ln8_launch<T, RT, YT, 4, 1, 4>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    if (G8 <= 8) return add_ln8_launch<T, RT, YT, 8, 1, 4>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    if (G8 <= 16) return add_ln8_launch<T, RT, YT, 16, 1, 2>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    if (G8 <= 32) return add_ln8_launch<T, RT, YT, 32, 1, 2>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    if (G8 <= 64) return add_ln8_launch<T, RT, YT, 32, 2, 2>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    if (G8 <= 128) return add_ln8_launch<T, RT, YT, 32, 4, 1>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+    return add_ln8_launch<T, RT, YT, 32, 8, 1>(x, radd, sum_out, w, b, eps, y, rows, C, st);
+}
+
+template <typename T, typename RT>
+int add_ln_y(int y_dtype, const void* x, const void* radd, void* sum_out, const float* w, const float* b,
+             float eps, void* y, int64_t rows, int C, cudaStream_t st) {
+    switch (y_dtype) {
+        case VH_F32: return add_ln_run<T, RT, float>(x, radd, sum_out, w, b, eps, static_cast<float*>(y), rows, C, st);
+        case VH_BF16: return add_ln_run<T, RT, __nv_bfloat16>(x, radd, sum_out, w, b, eps, static_cast<__nv_bfloat16*>(y), rows, C, st);
+        default: return add_ln_run<T, RT, __half>(x, radd, sum_out, w, b, eps, static_cast<__half*>(y), rows, C, st);
+    }
 }
 
 template <typename T, typename YT>
@@ -659,6 +711,28 @@ extern "C" int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* wei
         case VH_BF16: return ln_run_y<__nv_bfloat16>(y_dtype, x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
         default: return ln_run_y<__half>(y_dtype, x, weight, bias, eps, y, mean, rstd, rows, channels, vec_ok, st);
     }
+}
+
+extern "C" int vh_add_layernorm_fwd(const void* x, int32_t x_dtype, const void* r, int32_t r_dtype,
+                                    void* sum_out, const float* weight, const float* bias, float eps, void* y,
+                                    int32_t y_dtype, int64_t rows, int32_t channels, vh_stream_t stream) {
+    clear_error();
+    if (!x || !r || !sum_out || !weight || !bias || !y)
+        return fail(VH_E_ARG, "vh_add_layernorm_fwd: null pointer argument");
+    if ((x_dtype != VH_F32 && x_dtype != VH_BF16) || (r_dtype != VH_F32 && r_dtype != VH_BF16) || !dtype_ok(y_dtype))
+        return fail(VH_E_DTYPE, "vh_add_layernorm_fwd: x and r must be fp32 or bf16");
+    if (rows <= 0 || channels <= 0) return fail(VH_E_SHAPE, "vh_add_layernorm_fwd: empty input");
+    if (channels % 8 || channels > 2048) return fail(VH_E_SHAPE, "vh_add_layernorm_fwd: channels must be a multiple of 8, at most 2048");
+    if (rows > ((int64_t)1 << 40)) return fail(VH_E_RANGE, "vh_add_layernorm_fwd: too many rows");
+    if (!aligned(x, 16) || !aligned(r, 16) || !aligned(sum_out, 16) || !aligned(y, 16) || !aligned(weight, 16) ||
+        !aligned(bias, 16))
+        return fail(VH_E_ALIGN, "vh_add_layernorm_fwd: pointers must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (x_dtype == VH_F32)
+        return r_dtype == VH_F32 ? add_ln_y<float, float>(y_dtype, x, r, sum_out, weight, bias, eps, y, rows, channels, st)
+                                 : add_ln_y<float, __nv_bfloat16>(y_dtype, x, r, sum_out, weight, bias, eps, y, rows, channels, st);
+    return r_dtype == VH_F32 ? add_ln_y<__nv_bfloat16, float>(y_dtype, x, r, sum_out, weight, bias, eps, y, rows, channels, st)
+                             : add_ln_y<__nv_bfloat16, __nv_bfloat16>(y_dtype, x, r, sum_out, weight, bias, eps, y, rows, channels, st);
 }
 
 // =========================== GRN without any device allocation ===========================

@@ -9,7 +9,7 @@ import torch
 from .. import _lib
 from .cuda import on_tensor_device
 
-MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3}
+MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3, "resid_add": 4}
 
 
 def fusable(x, conv):
@@ -28,23 +28,30 @@ def fusable(x, conv):
 
 
 @on_tensor_device
-def depthwise_fused(x, conv, mode, gate=None):
+def depthwise_fused(x, conv, mode, gate=None, addend=None):
     """Apply depthwise ``conv`` to channels-last NCHW ``x`` with epilogue ``mode``:
-    "bias": conv(x) + b;  "resid": x + (conv(x) + b);  "gate": x + sigmoid(gate) * (conv(x) + b);
+    "bias": conv(x) + b;  "resid": s + (conv(s) + b) with s = x, or s = x + addend when an
+    addend (fp32/bf16, x's shape) is given;  "gate": x + sigmoid(gate) * (conv(x) + b);
     "gelu": h = gelu(x), gelu(h + conv(h) + b).  Returns a channels-last tensor of x's dtype."""
     _lib.ensure_device(x)
     B, C, H, W = x.shape
     if mode not in MODES:
         raise ValueError(f"unknown depthwise epilogue {mode!r}")
+    gate_dtype = 0
     if mode == "gate":
         if gate is None or gate.shape != x.shape or gate.dtype != x.dtype:
             raise RuntimeError("the gated epilogue needs a gate of x's shape and dtype")
         gate = gate.contiguous(memory_format=torch.channels_last)
+    if addend is not None:
+        if mode != "resid" or addend.shape != x.shape or addend.dtype not in (torch.float32, torch.bfloat16):
+            raise RuntimeError("an addend goes with the residual epilogue, fp32/bf16 of x's shape")
+        mode, gate = "resid_add", addend.contiguous(memory_format=torch.channels_last)
+        gate_dtype = _lib.dtype_code(gate.dtype)
     x = x.contiguous(memory_format=torch.channels_last)
     w = conv.weight.detach().float().contiguous()
     b = conv.bias.detach().float().contiguous()
     y = torch.empty_like(x, memory_format=torch.channels_last)
     args = _lib.VhDwconvArgs(x.data_ptr(), _lib.ptr(gate), w.data_ptr(), b.data_ptr(), y.data_ptr(),
-                             _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C)
+                             _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C, gate_dtype)
     _lib.check(_lib.load().vh_dwconv_fwd(args, _lib.stream_handle(x.device)), "vh_dwconv_fwd")
     return y

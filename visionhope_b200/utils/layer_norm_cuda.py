@@ -31,6 +31,26 @@ def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False, out_dtype=tor
 
 
 @on_tensor_device
+def add_layernorm_rows(x_rows, r_rows, weight, bias, eps, *, out_dtype=torch.float32, sum_out=None):
+    """s = x + r (written to ``sum_out``, default x itself) and LayerNorm(s): the block's
+    residual add followed by its second norm (models/block.py:105-106).  x, r: contiguous
+    [rows, C] fp32/bf16 CUDA tensors, C a multiple of 8.  Returns (s, y)."""
+    _lib.ensure_device(x_rows)
+    rows, C = x_rows.shape
+    if r_rows.shape != x_rows.shape or not x_rows.is_contiguous() or not r_rows.is_contiguous():
+        raise RuntimeError("add_layernorm_rows expects two contiguous [rows, C] tensors of one shape")
+    s = x_rows if sum_out is None else sum_out
+    w = weight.detach().reshape(-1).contiguous().float()
+    b = bias.detach().reshape(-1).contiguous().float()
+    y = torch.empty((rows, C), device=x_rows.device, dtype=out_dtype)
+    _lib.check(_lib.load().vh_add_layernorm_fwd(
+        x_rows.data_ptr(), _lib.dtype_code(x_rows.dtype), r_rows.data_ptr(), _lib.dtype_code(r_rows.dtype),
+        s.data_ptr(), w.data_ptr(), b.data_ptr(), float(eps), y.data_ptr(), _lib.dtype_code(out_dtype), rows, C,
+        _lib.stream_handle(x_rows.device)), "vh_add_layernorm_fwd")
+    return s, y
+
+
+@on_tensor_device
 def _layernorm2d_forward(x, weight, bias, eps):
     batch, channels, height, width = x.shape
     rows = x.permute(0, 2, 3, 1).reshape(batch * height * width, channels)
