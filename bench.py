@@ -8,8 +8,10 @@ scaling).  Inputs and the model's activation footprint are far larger than L2, a
 256 MiB buffer is additionally rewritten between timed steps (outside the timed events).
 Rank 0 prints one JSON line; the time is the max over ranks of the summed per-step CUDA
 event times.  Extra keys:
-  e2e          -- the same metric through the public model call with the batch copied from
-                  pinned host memory and the logits copied back inside every timed step;
+  e2e          -- the same metric through the public model call, timed over the whole run:
+                  every step's batch is copied from pinned host memory (on a copy stream,
+                  overlapping the previous step's forward, then device to device into the
+                  graph's input) and its logits are copied back to pinned host memory;
   roofline     -- the dominant kernel (the fused SRNL operator at the stage-1 shape of this
                   batch) timed alone with CUDA events, against the measured FP32 FMA peak;
   cpu_baseline -- the CPU stand-in for the reference (oracle port of SRNL + PyTorch CPU
@@ -422,32 +424,50 @@ def run_ours(args, world, rank, local):
         ms_max = max_over_ranks(ms, device, world)
         clocks = clk.summary(set(range(torch.cuda.device_count())) if world > 1 else {device.index})
 
-        # ---- end to end: pinned host batch in, logits out, inside every timed step ----
+        # ---- end to end: pinned host batch in, logits out, every step inside the timed run ----
+        # A serving pipeline: batch i+1 crosses PCIe on a copy stream into a staging buffer
+        # while batch i runs; each step then moves its batch from staging into the graph's
+        # input (device to device) and copies its logits back to pinned host memory.  The
+        # timed region spans the whole run, from the first host-to-device copy to the last
+        # logits copy, so all K copies in and out are inside it.
         host_in = torch.randn(args.batch, 3, IMG, IMG, generator=torch.Generator().manual_seed(3 + rank)
                               ).contiguous(memory_format=torch.channels_last).pin_memory()
         host_out = torch.empty(static_out.shape, dtype=static_out.dtype).pin_memory()
+        staging = torch.empty_like(static_in)
+        copy_stream = torch.cuda.Stream(device)
+        main = torch.cuda.current_stream(device)
 
-        def e2e_step():
-            static_in.copy_(host_in, non_blocking=True)
-            graph.replay()
-            if world > 1:
-                dist.all_gather(gathered, static_out)
-            host_out.copy_(static_out, non_blocking=True)
+        def e2e_run(k):
+            copied, freed = torch.cuda.Event(), torch.cuda.Event()
+            copy_stream.wait_stream(main)
+            with torch.cuda.stream(copy_stream):
+                staging.copy_(host_in, non_blocking=True)
+                copied.record()
+            for i in range(k):
+                flush.fill_(1.0)
+                main.wait_event(copied)
+                static_in.copy_(staging, non_blocking=True)
+                freed.record()
+                if i + 1 < k:
+                    copy_stream.wait_event(freed)
+                    with torch.cuda.stream(copy_stream):
+                        staging.copy_(host_in, non_blocking=True)
+                        copied.record()
+                graph.replay()
+                if world > 1:
+                    dist.all_gather(gathered, static_out)
+                host_out.copy_(static_out, non_blocking=True)
 
-        for _ in range(2):
-            e2e_step()
+        e2e_run(2)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        for a, b in evs:
-            flush.fill_(1.0)
-            a.record()
-            e2e_step()
-            b.record()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        e2e_run(args.steps)
+        b.record()
         torch.cuda.synchronize()
-        e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / args.steps, device, world)
+        e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, device, world)
         if not torch.isfinite(host_out).all():
             raise RuntimeError("non-finite logits")
 
@@ -464,7 +484,9 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": world * args.batch * 1000.0 / e2e_ms, "unit": UNIT,
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms,
+                    "pipeline": "host-to-device copy of batch i+1 on a copy stream overlaps the forward of "
+                                "batch i; timed from the first copy in to the last logits copy out"},
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_per_step": launches_per_step,
             "roofline": roof, "clocks": clocks,

@@ -202,6 +202,18 @@ int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* 
  * All calls share the one array: calls that may overlap on the GPU (different streams, or
  * different host threads on one device) race and must be serialized by the caller; the array
  * keeps the last call's contents, which no call relies on. */
+/* GRN from precomputed statistics: the apply pass of vh_grn_fwd when the sums of x^2 per
+ * (image, channel) were produced with x itself (vh_dwconv_fwd's `sumsq`).  sumsq: fp32
+ * [B, nparts, C], sums over disjoint pixel slices of each image, added in slice order;
+ * Gx = sqrt(sum), f = 1 + gamma Gx / (mean_c Gx + eps) is written to `factors` (fp32 [B, C],
+ * 16-byte aligned) and y = x f + beta  (grn_cuda.cu:46-124).  x, y: dense channels-last
+ * [B, H, W, C], 16-byte aligned, y distinct from x; C a multiple of 8 with C / 8 dividing 256
+ * (C in {8, 16, ..., 2048} of that form). */
+int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sumsq, int32_t nparts,
+                     const float* gamma, const float* beta, float eps, float* factors, void* y,
+                     int32_t y_dtype, int32_t batch, int32_t height, int32_t width, int32_t channels,
+                     vh_stream_t stream);
+
 int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma, const float* beta,
                        float eps, float* y, float* gx, float* inv_den, int32_t batch,
                        int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
@@ -250,9 +262,17 @@ typedef struct {
     int32_t ksize;
     int32_t batch, height, width, channels;
     int32_t gate_dtype; /* VH_DW_RESID_ADD: dtype of the addend r (fp32 or bf16) */
+    /* VH_DW_GELU only, may be NULL: fp32 [B, vh_dwconv_tiles(H, W), C] receiving, per image and
+     * pixel tile, the sum over the tile of y^2 per channel, with y as stored (the statistics
+     * pass of a GRN that follows, see vh_grn_apply_fwd).  Written, not accumulated. */
+    float* sumsq;
 } vh_dwconv_args;
 
 int vh_dwconv_fwd(const vh_dwconv_args* args, vh_stream_t stream);
+
+/* Number of pixel tiles per image that vh_dwconv_fwd uses for an H x W image (the middle
+ * extent of its `sumsq` output). */
+int vh_dwconv_tiles(int32_t height, int32_t width);
 
 /* ---------------------------------------------------------------------------------------
  * Bias and activation over channels-last rows: y[r, c] = act(x[r, c] + bias[c]), computed in

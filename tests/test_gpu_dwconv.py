@@ -107,3 +107,38 @@ def test_dwconv_rejects_bad_arguments(cuda):
     x = torch.randn(1, 16, 8, 8, device=cuda).contiguous(memory_format=torch.channels_last)
     with pytest.raises(RuntimeError, match="gate"):
         depthwise_fused(x, conv, "gate")
+
+
+@pytest.mark.parametrize("shape", [(2, 256, 56, 56), (3, 1024, 14, 14), (2, 2048, 7, 7), (1, 96, 23, 5),
+                                   (2, 512, 28, 28)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+def test_dwconv_gelu_tile_sums(shape, dt, cuda):
+    """The GELU epilogue's per-tile sums of y^2 (the statistics of the GRN that follows): y is
+    unchanged by asking for them, the tiles add up to the image's per-channel sums of y as
+    stored, and tile 0 of a 56 x 56 image is its top-left 14 x 14 block."""
+    from visionhope_b200 import _lib
+    from visionhope_b200.utils.dwconv import depthwise_fused
+
+    B, C, H, W = shape
+    torch.manual_seed(zlib.crc32(repr(shape).encode()))
+    conv = torch.nn.Conv2d(C, C, 3, padding=1, groups=C).to(cuda)
+    x = torch.randn(B, C, H, W, device=cuda).to(dt).contiguous(memory_format=torch.channels_last)
+    with torch.inference_mode():
+        y0 = depthwise_fused(x, conv, "gelu")
+        y, ss = depthwise_fused(x, conv, "gelu", with_sumsq=True)
+    assert torch.equal(y, y0)
+    assert ss.shape == (B, _lib.load().vh_dwconv_tiles(H, W), C) and ss.dtype == torch.float32
+    yd = y.double()
+    exp = yd.pow(2).sum(dim=(2, 3))
+    assert rel_err(ss.double().sum(1).cpu().numpy(), exp.cpu().numpy()) < 1e-6
+    if H == W == 56:
+        assert rel_err(ss[:, 0].double().cpu().numpy(), yd[:, :, :14, :14].pow(2).sum(dim=(2, 3)).cpu().numpy()) < 1e-6
+
+
+def test_dwconv_sumsq_needs_gelu(cuda):
+    from visionhope_b200.utils.dwconv import depthwise_fused
+
+    conv = torch.nn.Conv2d(16, 16, 3, padding=1, groups=16).to(cuda)
+    x = torch.randn(1, 16, 8, 8, device=cuda).contiguous(memory_format=torch.channels_last)
+    with torch.inference_mode(), pytest.raises(RuntimeError, match="gelu"):
+        depthwise_fused(x, conv, "bias", with_sumsq=True)

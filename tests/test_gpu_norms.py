@@ -169,3 +169,40 @@ def test_bias_act(act, io, cuda):
     assert y.dtype == DT[io[1]] and y.is_contiguous(memory_format=torch.channels_last)
     tol = 4e-3 if io[1] == "bf16" else 1e-6
     assert rel_err(y.double().cpu().numpy(), exp.cpu().numpy()) < tol
+
+
+GRN_APPLY_CASES = [(2, 56, 56, 256, "bf16", 16), (3, 14, 14, 1024, "bf16", 1), (2, 7, 7, 2048, "f32", 1),
+                   (4, 9, 9, 64, "f16", 3), (1, 5, 5, 8, "f32", 2), (2, 28, 28, 512, "bf16", 4)]
+
+
+@pytest.mark.parametrize("case", GRN_APPLY_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_grn_apply_from_slice_sums(case, oracle, cuda):
+    """GRN fed with per-slice sums of x^2 (as the fused depthwise GELU kernel produces them)
+    against the oracle's GRN of the same x."""
+    from visionhope_b200.utils.grn_cuda import grn_apply
+
+    B, H, W, C, dt, P = case
+    gen = np.random.default_rng(zlib.crc32(repr(case).encode()))
+    x = _dev(gen.normal(size=(B, H, W, C)), cuda, DT[dt]).permute(0, 3, 1, 2)
+    gamma = _dev(gen.normal(0, 0.5, size=C), cuda)
+    beta = _dev(gen.normal(0, 0.5, size=C), cuda)
+    xs = x.permute(0, 2, 3, 1).reshape(B, H * W, C).double().cpu()
+    bounds = np.linspace(0, H * W, P + 1).astype(int)
+    sums = torch.stack([xs[:, a:b].pow(2).sum(1) for a, b in zip(bounds[:-1], bounds[1:])], 1)
+    y = grn_apply(x, sums.float().to(cuda), gamma, beta, 1e-6)
+    exp = oracle.grn_nhwc(x.permute(0, 2, 3, 1), gamma, beta)
+    assert y.dtype == torch.float32 and y.is_contiguous(memory_format=torch.channels_last)
+    assert rel_err(y.permute(0, 2, 3, 1).cpu().numpy(), exp) < 1e-5
+    yb = grn_apply(x, sums.float().to(cuda), gamma, beta, 1e-6, out_dtype=torch.bfloat16)
+    assert rel_err(yb.float().permute(0, 2, 3, 1).cpu().numpy(), exp) < 1e-2
+
+
+def test_grn_apply_rejects_unsupported_channels(cuda):
+    from visionhope_b200.utils.grn_cuda import grn_apply, grn_apply_ok
+
+    for C in (12, 24, 4096):
+        x = torch.zeros(1, C, 2, 2, device=cuda).contiguous(memory_format=torch.channels_last)
+        assert not grn_apply_ok(x)
+        g = torch.zeros(C, device=cuda)
+        with pytest.raises(RuntimeError, match="channels"):
+            grn_apply(x, torch.zeros(1, 1, C, device=cuda), g, g, 1e-6)

@@ -59,7 +59,7 @@ class VhDwconvArgs(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("gate", c_void_p), ("weight", c_void_p), ("bias", c_void_p),
                 ("y", c_void_p), ("dtype", c_int32), ("mode", c_int32), ("ksize", c_int32),
                 ("batch", c_int32), ("height", c_int32), ("width", c_int32), ("channels", c_int32),
-                ("gate_dtype", c_int32)]
+                ("gate_dtype", c_int32), ("sumsq", c_void_p)]
 
 
 _lib = None
@@ -101,6 +101,12 @@ def load() -> ctypes.CDLL:
             lib.vh_init.argtypes = [c_int32]
             lib.vh_dwconv_fwd.restype = c_int32
             lib.vh_dwconv_fwd.argtypes = [ctypes.POINTER(VhDwconvArgs), c_void_p]
+            lib.vh_dwconv_tiles.restype = c_int32
+            lib.vh_dwconv_tiles.argtypes = [c_int32, c_int32]
+            lib.vh_grn_apply_fwd.restype = c_int32
+            lib.vh_grn_apply_fwd.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_float,
+                                             c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                             c_void_p]
             lib.vh_bias_act_fwd.restype = c_int32
             lib.vh_bias_act_fwd.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int64, c_int32,
                                             c_int32, c_void_p]

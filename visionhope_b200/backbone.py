@@ -21,7 +21,7 @@ from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
 from .utils.bias_act import bias_act
 from .utils.dwconv import depthwise_fused, fusable
-from .utils.grn_cuda import grn_forward
+from .utils.grn_cuda import grn_apply, grn_apply_ok, grn_forward
 from .utils.inference import cache_half_weights, linear_cached
 from .utils.layer_norm_cuda import add_layernorm_rows, layernorm_rows
 
@@ -133,10 +133,15 @@ class FeedForwardNetwork(nn.Module):
 
     def forward(self, x):
         x = pointwise(self.fc1, x)
+        sumsq = None
         if (self.use_dwconv and _is_exact_gelu(self.act) and _is_exact_gelu(self.dwconv_act)
                 and fusable(x, self.dwconv)):
-            # gelu(fc1), the depthwise convolution, its residual and the second gelu in one pass
-            x = depthwise_fused(x, self.dwconv, "gelu")
+            # gelu(fc1), the depthwise convolution, its residual and the second gelu in one pass;
+            # with GRN next, the same pass also sums y^2 per channel over each pixel tile
+            stats = isinstance(self.grn, GlobalResponseNorm) and grn_apply_ok(x)
+            x = depthwise_fused(x, self.dwconv, "gelu", with_sumsq=stats)
+            if stats:
+                x, sumsq = x
         else:
             x = self.act(x)
             if self.use_dwconv:
@@ -146,7 +151,10 @@ class FeedForwardNetwork(nn.Module):
             # fc2 runs under autocast and casts GRN's fp32 output to `ac`; emit it directly.
             if not x.is_contiguous(memory_format=torch.channels_last):
                 x = x.contiguous(memory_format=torch.channels_last)
-            x = grn_forward(x, self.grn.gamma, self.grn.beta, self.grn.eps, out_dtype=ac)
+            if sumsq is not None:
+                x = grn_apply(x, sumsq, self.grn.gamma, self.grn.beta, self.grn.eps, out_dtype=ac)
+            else:
+                x = grn_forward(x, self.grn.gamma, self.grn.beta, self.grn.eps, out_dtype=ac)
         else:
             x = self.grn(x)
         return self.drop(pointwise(self.fc2, self.drop(x)))

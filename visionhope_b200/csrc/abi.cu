@@ -61,6 +61,18 @@ bool ensure_smem_attr(const void* func, size_t bytes) {
     return true;
 }
 
+int sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
 // Defined in the kernel translation units: set every kernel's attributes for `device`.
 int init_scan_kernels();
 int init_norm_kernels();

@@ -25,4 +25,7 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 // Sets the dynamic shared-memory limit of a kernel once per device; returns false on failure.
 bool ensure_smem_attr(const void* func, size_t bytes);
 
+// Number of SMs of the current device (looked up once per device; 148 if the query fails).
+int sm_count();
+
 }  // namespace vh

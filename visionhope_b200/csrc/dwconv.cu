@@ -78,6 +78,7 @@ template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
 __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const GT* __restrict__ gate,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, T* __restrict__ y,
+                                                                float* __restrict__ sumsq,
                                                                 int H, int W, int C, int tiles_w) {
     using G = DwGeom<K, TC, RG, R>;
     constexpr int TH = G::TH, P = G::P, IW = G::IW, NT = G::NT;
@@ -183,13 +184,14 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
         }
     }
 
-    if (!out_ok) return;
+    // GELU mode with `sumsq`: this thread's sums of y^2 (as stored) over its rows, 4 channels.
+    float2 ss[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     float2 bv[2];
     lds4(bs + 4 * q, bv);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int oy = oy0 + r0 + r;
-        if (oy >= H) break;
+        if (!out_ok || oy >= H) break;
         const int64_t off = img + ((int64_t)oy * W + ox) * C + c;
         float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
         if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || MODE == VH_DW_GATE) {
@@ -220,8 +222,35 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
             lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, h);
             o[0] = gelu2(fadd2(h[0], o[0]));
             o[1] = gelu2(fadd2(h[1], o[1]));
+            if (sumsq && std::is_same<T, __nv_bfloat16>::value) {
+                o[0] = __bfloat1622float2(__floats2bfloat162_rn(o[0].x, o[0].y));
+                o[1] = __bfloat1622float2(__floats2bfloat162_rn(o[1].x, o[1].y));
+            }
+            ss[0] = ffma2(o[0], o[0], ss[0]);
+            ss[1] = ffma2(o[1], o[1], ss[1]);
         }
         store4(y + off, make_float4(o[0].x, o[0].y, o[1].x, o[1].y));
+    }
+    if (MODE == VH_DW_GELU && sumsq) {
+        // Per-tile channel sums in a fixed order: the four lanes of a warp that share channels
+        // (lane bits 3-4), then the warps in index order; the staged tile is free by now.
+#pragma unroll
+        for (int m = 8; m <= 16; m <<= 1) {
+            ss[0].x += __shfl_xor_sync(0xffffffffu, ss[0].x, m);
+            ss[0].y += __shfl_xor_sync(0xffffffffu, ss[0].y, m);
+            ss[1].x += __shfl_xor_sync(0xffffffffu, ss[1].x, m);
+            ss[1].y += __shfl_xor_sync(0xffffffffu, ss[1].y, m);
+        }
+        __syncthreads();
+        const int lane = tid & 31, warp = tid >> 5;
+        if (lane < 8) *reinterpret_cast<float4*>(xs + warp * kDwCG + 4 * lane) = make_float4(ss[0].x, ss[0].y, ss[1].x, ss[1].y);
+        __syncthreads();
+        if (tid < kDwCG && c0 + tid < C) {
+            float t = 0.f;
+#pragma unroll
+            for (int w8 = 0; w8 < NT / 32; ++w8) t += xs[w8 * kDwCG + tid];
+            sumsq[((int64_t)b * gridDim.x + blockIdx.x) * C + c0 + tid] = t;
+        }
     }
 }
 
@@ -235,22 +264,27 @@ int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
         return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", G::kSmem);
     dwconv_kernel<K, MODE, T, GT, TC, RG, R><<<grid, G::NT, G::kSmem, st>>>(
         static_cast<const T*>(a.x), static_cast<const GT*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
-        a.height, a.width, a.channels, tiles_w);
+        MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w);
     return launch_status("depthwise conv");
 }
 
 // Tile: the shape among 14 x 14 (224 threads, 7 rows each; divides every VisionHOPE stage
 // size from 14 up), 16 x 16 (256 threads, 8 rows each) and 8 x 8 (256 threads, 2 rows each)
 // that covers the image with the least padding, in that order of preference.
+inline int dw_tile_side(int H, int W) {
+    auto area = [&](int t) { return (int64_t)((H + t - 1) / t) * t * (int64_t)((W + t - 1) / t) * t; };
+    const int64_t a14 = area(14), a16 = area(16), a8 = area(8);
+    if (a14 <= a16 && a14 <= a8) return 14;
+    return a16 <= a8 ? 16 : 8;
+}
+
 template <int K, int MODE, typename T, typename GT>
 int dw_tile(const vh_dwconv_args& a, cudaStream_t st) {
-    auto area = [&](int th, int tc) {
-        return (int64_t)((a.height + th - 1) / th) * th * (int64_t)((a.width + tc - 1) / tc) * tc;
-    };
-    const int64_t a14 = area(14, 14), a16 = area(16, 16), a8 = area(8, 8);
-    if (a14 <= a16 && a14 <= a8) return dw_launch<K, MODE, T, GT, 14, 2, 7>(a, st);
-    if (a16 <= a8) return dw_launch<K, MODE, T, GT, 16, 2, 8>(a, st);
-    return dw_launch<K, MODE, T, GT, 8, 4, 2>(a, st);
+    switch (dw_tile_side(a.height, a.width)) {
+        case 14: return dw_launch<K, MODE, T, GT, 14, 2, 7>(a, st);
+        case 16: return dw_launch<K, MODE, T, GT, 16, 2, 8>(a, st);
+        default: return dw_launch<K, MODE, T, GT, 8, 4, 2>(a, st);
+    }
 }
 
 template <int MODE, typename T, typename GT = T>
@@ -319,6 +353,12 @@ int init_dw_kernels() {
 
 using namespace vh;
 
+extern "C" int vh_dwconv_tiles(int32_t height, int32_t width) {
+    if (height <= 0 || width <= 0) return 0;
+    const int t = dw_tile_side(height, width);
+    return ((height + t - 1) / t) * ((width + t - 1) / t);
+}
+
 extern "C" int vh_dwconv_fwd(const vh_dwconv_args* a, vh_stream_t stream) {
     clear_error();
     if (!a) return fail(VH_E_ARG, "vh_dwconv_fwd: null args");
@@ -341,6 +381,9 @@ extern "C" int vh_dwconv_fwd(const vh_dwconv_args* a, vh_stream_t stream) {
         return fail(VH_E_RANGE, "vh_dwconv_fwd: sizes exceed the supported range");
     if (!aligned(a->x, 16) || !aligned(a->y, 16) || (a->gate && !aligned(a->gate, 16)))
         return fail(VH_E_ALIGN, "vh_dwconv_fwd: x, gate and y must be 16-byte aligned");
+    if (a->sumsq && a->mode != VH_DW_GELU)
+        return fail(VH_E_ARG, "vh_dwconv_fwd: sumsq goes with the GELU epilogue");
+    if (a->sumsq && !aligned(a->sumsq, 4)) return fail(VH_E_ALIGN, "vh_dwconv_fwd: misaligned sumsq");
     if (a->x == a->y || (a->gate && a->gate == a->y))
         return fail(VH_E_ARG, "vh_dwconv_fwd: y must not alias the inputs");
     cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -116,6 +116,84 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
     }
 }
 
+// ====== GRN from precomputed sums of squares (the statistics pass fused into the producer) =====
+// part [B, nparts, C]: sums of x^2 per channel over disjoint pixel slices of each image (the
+// FFN's depthwise GELU kernel writes them per pixel tile as it stores x).
+// grn_factor_kernel: one CTA per image sums the slices in index order and writes the factors
+//   f[b, c] = 1 + gamma[c] Gx[c] / (mean_c Gx + eps), Gx = sqrt(sum)  (as grn_apply_kernel).
+// grn_scale8_kernel: y = x f[b, c] + beta[c] over all 16-byte vectors of the batch, a grid of
+//   a few CTAs per SM striding over them; the stride is a multiple of C / 8, so each thread
+//   keeps one channel group (its betas in registers) and four vector loads are in flight
+//   before any is used.  Needs C % 8 == 0 and C / 8 dividing 256.
+constexpr int kGrnScaleUnroll = 4;
+constexpr int kGrnScaleCtasPerSm = 4;
+
+__global__ void __launch_bounds__(kGrnThreads) grn_factor_kernel(const float* __restrict__ part, int nparts,
+                                                                 const float* __restrict__ gamma, float eps,
+                                                                 float* __restrict__ fac_out, int C) {
+    __shared__ float scratch[32];
+    const int b = blockIdx.x;
+    const float* pb = part + (int64_t)b * nparts * C;
+    float local = 0.f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < nparts; ++k) s += pb[(int64_t)k * C + c];
+        local += sqrtf(s);
+    }
+    local = warp_sum(local);
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? scratch[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) scratch[0] = 1.f / (v / (float)C + eps);
+    }
+    __syncthreads();
+    const float inv_den = scratch[0];
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < nparts; ++k) s += pb[(int64_t)k * C + c];
+        fac_out[(int64_t)b * C + c] = 1.f + gamma[c] * (sqrtf(s) * inv_den);
+    }
+}
+
+template <typename T, typename YT>
+__global__ void __launch_bounds__(kGrnThreads, kGrnScaleCtasPerSm) grn_scale8_kernel(
+    const T* __restrict__ x, const float* __restrict__ fac, const float* __restrict__ beta,
+    YT* __restrict__ y, int C, uint32_t per_image, uint32_t nvec) {
+    const uint32_t G8 = (uint32_t)C >> 3, stride = gridDim.x * blockDim.x;
+    const uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = 8 * (int)(v0 % G8);
+    float bt[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bt[e] = beta[c + e];
+    for (uint32_t v = v0; v < nvec; v += stride * kGrnScaleUnroll) {
+        uint4 raw[kGrnScaleUnroll][sizeof(T) == 4 ? 2 : 1];
+#pragma unroll
+        for (int u = 0; u < kGrnScaleUnroll; ++u) {
+            const uint32_t vu = v + u * stride;
+            if (vu < nvec) {
+                const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)vu * 8);
+#pragma unroll
+                for (int h = 0; h < (sizeof(T) == 4 ? 2 : 1); ++h) raw[u][h] = __ldcs(src + h);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kGrnScaleUnroll; ++u) {
+            const uint32_t vu = v + u * stride;
+            if (vu >= nvec) break;
+            const float* f = fac + (size_t)(vu / per_image) * C + c;
+            const float4 f0 = *reinterpret_cast<const float4*>(f), f1 = *reinterpret_cast<const float4*>(f + 4);
+            float xv[8];
+            load8(reinterpret_cast<const T*>(&raw[u][0]), xv);
+            const float fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[e] = fmaf(xv[e], fv[e], bt[e]);
+            store8(y + (size_t)vu * 8, xv);
+        }
+    }
+}
+
 // ============ GRN in one read: a thread-block cluster per image (grn_cuda.cu:46-124) ============
 // The K CTAs of image b each copy a contiguous slice of its pixels (all channels) into shared
 // memory with asynchronous 16-byte copies, sum x^2 per channel over the slice, and read the K
@@ -693,6 +771,53 @@ extern "C" int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, co
         case VH_F32: return grn_run_y<float>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
         case VH_BF16: return grn_run_y<__nv_bfloat16>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
         default: return grn_run_y<__half>(y_dtype, x, gamma, beta, eps, y, gx, inv_den, part, batch, S, channels, st);
+    }
+}
+
+extern "C" int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sumsq, int32_t nparts,
+                                const float* gamma, const float* beta, float eps, float* factors, void* y,
+                                int32_t y_dtype, int32_t batch, int32_t height, int32_t width,
+                                int32_t channels, vh_stream_t stream) {
+    clear_error();
+    if (!x || !sumsq || !gamma || !beta || !factors || !y)
+        return fail(VH_E_ARG, "vh_grn_apply_fwd: null pointer argument");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(VH_E_DTYPE, "vh_grn_apply_fwd: bad dtype");
+    if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || nparts <= 0)
+        return fail(VH_E_SHAPE, "GRN expects nonempty input");
+    if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_apply_fwd: batch must be <= 65535");
+    if (channels % 8 || channels > 2048 || kGrnThreads % (channels / 8))
+        return fail(VH_E_SHAPE, "vh_grn_apply_fwd: channels must be a multiple of 8 with channels/8 dividing 256");
+    const int64_t per_image = (int64_t)height * width * (channels / 8);
+    if (per_image * batch >= ((int64_t)1 << 32) - (int64_t)kGrnThreads * 1024 * kGrnScaleUnroll * 2)
+        return fail(VH_E_RANGE, "vh_grn_apply_fwd: tensor too large");
+    if (!aligned(x, 16) || !aligned(y, 16) || !aligned(factors, 16))
+        return fail(VH_E_ALIGN, "vh_grn_apply_fwd: misaligned pointers");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    grn_factor_kernel<<<batch, kGrnThreads, 0, st>>>(sumsq, nparts, gamma, eps, factors, channels);
+    int rc = launch_status("grn factors");
+    if (rc) return rc;
+    const uint32_t nvec = (uint32_t)(per_image * batch);
+    const int64_t want = (nvec + kGrnThreads - 1) / kGrnThreads;
+    const dim3 grid((unsigned)std::min<int64_t>(want, (int64_t)sm_count() * kGrnScaleCtasPerSm));
+    auto run = [&](auto xt, auto yt) -> int {
+        using T = decltype(xt);
+        using YT = decltype(yt);
+        grn_scale8_kernel<T, YT><<<grid, kGrnThreads, 0, st>>>(static_cast<const T*>(x), factors, beta,
+                                                               static_cast<YT*>(y), channels,
+                                                               (uint32_t)per_image, nvec);
+        return launch_status("grn scale");
+    };
+    auto run_x = [&](auto yt) -> int {
+        switch (x_dtype) {
+            case VH_F32: return run(float{}, yt);
+            case VH_BF16: return run(__nv_bfloat16{}, yt);
+            default: return run(__half{}, yt);
+        }
+    };
+    switch (y_dtype) {
+        case VH_F32: return run_x(float{});
+        case VH_BF16: return run_x(__nv_bfloat16{});
+        default: return run_x(__half{});
     }
 }
 

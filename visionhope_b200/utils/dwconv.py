@@ -28,11 +28,13 @@ def fusable(x, conv):
 
 
 @on_tensor_device
-def depthwise_fused(x, conv, mode, gate=None, addend=None):
+def depthwise_fused(x, conv, mode, gate=None, addend=None, with_sumsq=False):
     """Apply depthwise ``conv`` to channels-last NCHW ``x`` with epilogue ``mode``:
     "bias": conv(x) + b;  "resid": s + (conv(s) + b) with s = x, or s = x + addend when an
     addend (fp32/bf16, x's shape) is given;  "gate": x + sigmoid(gate) * (conv(x) + b);
-    "gelu": h = gelu(x), gelu(h + conv(h) + b).  Returns a channels-last tensor of x's dtype."""
+    "gelu": h = gelu(x), gelu(h + conv(h) + b).  Returns a channels-last tensor of x's dtype,
+    and with ``with_sumsq`` ("gelu" only) also the fp32 [B, tiles, C] sums of y^2 per pixel
+    tile that a following GRN needs (``grn_cuda.grn_apply``)."""
     _lib.ensure_device(x)
     B, C, H, W = x.shape
     if mode not in MODES:
@@ -51,7 +53,13 @@ def depthwise_fused(x, conv, mode, gate=None, addend=None):
     w = conv.weight.detach().float().contiguous()
     b = conv.bias.detach().float().contiguous()
     y = torch.empty_like(x, memory_format=torch.channels_last)
+    sumsq = None
+    if with_sumsq:
+        if mode != "gelu":
+            raise RuntimeError("tile statistics go with the gelu epilogue")
+        sumsq = torch.empty((B, int(_lib.load().vh_dwconv_tiles(H, W)), C), device=x.device, dtype=torch.float32)
     args = _lib.VhDwconvArgs(x.data_ptr(), _lib.ptr(gate), w.data_ptr(), b.data_ptr(), y.data_ptr(),
-                             _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C, gate_dtype)
+                             _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C, gate_dtype,
+                             _lib.ptr(sumsq))
     _lib.check(_lib.load().vh_dwconv_fwd(args, _lib.stream_handle(x.device)), "vh_dwconv_fwd")
-    return y
+    return (y, sumsq) if with_sumsq else y

@@ -36,6 +36,35 @@ def grn_forward(x, gamma, beta, eps, *, want_stats=False, out_dtype=torch.float3
     return (y, gx, inv) if want_stats else y
 
 
+def grn_apply(x, sumsq, gamma, beta, eps, *, out_dtype=torch.float32):
+    """GRN of channels-last ``x`` from its precomputed statistics: ``sumsq`` fp32 [B, P, C]
+    holds sums of x^2 per channel over P disjoint pixel slices of each image (as the fused
+    depthwise GELU kernel returns them), so x is read once here (``vh_grn_apply_fwd``).
+    Same result as :func:`grn_forward` up to the order of the fp32 sums."""
+    _lib.ensure_device(x)
+    if x.dim() != 4 or not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError("GRN CUDA expects channels-last NCHW input")
+    B, C, H, W = x.shape
+    if sumsq.dtype != torch.float32 or sumsq.dim() != 3 or sumsq.shape[0] != B or sumsq.shape[2] != C:
+        raise RuntimeError("grn_apply: sumsq must be fp32 [B, slices, C]")
+    sumsq = sumsq.contiguous()
+    g = gamma.detach().reshape(-1).contiguous().float()
+    b = beta.detach().reshape(-1).contiguous().float()
+    y = torch.empty_like(x, dtype=out_dtype, memory_format=torch.channels_last)
+    factors = torch.empty((B, C), device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().vh_grn_apply_fwd(
+        x.data_ptr(), _lib.dtype_code(x.dtype), sumsq.data_ptr(), sumsq.shape[1], g.data_ptr(), b.data_ptr(),
+        float(eps), factors.data_ptr(), y.data_ptr(), _lib.dtype_code(out_dtype), B, H, W, C,
+        _lib.stream_handle(x.device)), "vh_grn_apply_fwd")
+    return y
+
+
+def grn_apply_ok(x):
+    """Shapes the statistics-fed GRN takes: channels a multiple of 8 with C/8 dividing 256."""
+    C = x.shape[1]
+    return C % 8 == 0 and C <= 2048 and 256 % (C // 8) == 0
+
+
 class _GRNForwardOnly(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, gamma, beta, eps):
