@@ -331,9 +331,12 @@ def roofline_norms(device, iters=10):
     """GRN and LayerNorm alone at the GRN/LN configuration's shapes (channels-last
     [128, 56, 56, 96] and [128, 7, 7, 768], fp32 and bf16 in, fp32 out): achieved HBM GB/s of
     the algorithmic bytes (one read of x, one write of y) against the measured copy bandwidth.
-    A 256 MiB buffer is rewritten before every timed launch (outside the events)."""
+    "grn" is the standalone op (statistics and apply from x); "grn_apply" is the apply pass
+    fed with per-slice sums of x^2, as the model runs it after the FFN depthwise kernel (the
+    sums come from an untimed pre-pass here).  A 256 MiB buffer is rewritten before every timed
+    launch (outside the events)."""
     from visionhope_b200 import _lib
-    from visionhope_b200.utils.grn_cuda import grn_forward
+    from visionhope_b200.utils.grn_cuda import grn_apply, grn_forward
     from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
 
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -348,7 +351,9 @@ def roofline_norms(device, iters=10):
             bet = torch.randn(C, device=device, generator=g) * 0.02
             w = 1 + torch.randn(C, device=device, generator=g) * 0.02
             xr = x.permute(0, 2, 3, 1).reshape(-1, C)
+            sums = x.float().pow(2).sum(dim=(2, 3)).reshape(B, 1, C)
             for name, fn in (("grn", lambda: grn_forward(x, gam, bet, 1e-6)),
+                             ("grn_apply", lambda: grn_apply(x, sums, gam, bet, 1e-6)),
                              ("layernorm", lambda: layernorm_rows(xr, w, bet, 1e-6))):
                 for _ in range(3):
                     fn()

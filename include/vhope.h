@@ -207,8 +207,7 @@ int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* 
  * [B, nparts, C], sums over disjoint pixel slices of each image, added in slice order;
  * Gx = sqrt(sum), f = 1 + gamma Gx / (mean_c Gx + eps) is written to `factors` (fp32 [B, C],
  * 16-byte aligned) and y = x f + beta  (grn_cuda.cu:46-124).  x, y: dense channels-last
- * [B, H, W, C], 16-byte aligned, y distinct from x; C a multiple of 8 with C / 8 dividing 256
- * (C in {8, 16, ..., 2048} of that form). */
+ * [B, H, W, C], 16-byte aligned, y distinct from x; C a multiple of 8, at most 2048. */
 int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sumsq, int32_t nparts,
                      const float* gamma, const float* beta, float eps, float* factors, void* y,
                      int32_t y_dtype, int32_t batch, int32_t height, int32_t width, int32_t channels,
@@ -285,6 +284,15 @@ enum vh_act { VH_ACT_NONE = 0, VH_ACT_GELU = 1 };
 
 int vh_bias_act_fwd(const void* x, int32_t x_dtype, const float* bias, void* y, int32_t y_dtype,
                     int64_t rows, int32_t channels, int32_t act, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Residual add with a cast: y = (y_dtype)(x + r), summed in fp32 and rounded once
+ * (models/block.py:106, the last block's `x + branch` of a stage, fused with the autocast cast
+ * of the downsample convolution that reads it).  x, r, y: n elements each (n a multiple of 8),
+ * fp32 or bf16, 16-byte aligned; y distinct from x and r.
+ * -------------------------------------------------------------------------------------*/
+int vh_add_cast_fwd(const void* x, int32_t x_dtype, const void* r, int32_t r_dtype, void* y, int32_t y_dtype,
+                    int64_t n, vh_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
  * Residual add followed by LayerNorm over channels-last rows (models/block.py:105-106, the

@@ -172,7 +172,8 @@ def test_bias_act(act, io, cuda):
 
 
 GRN_APPLY_CASES = [(2, 56, 56, 256, "bf16", 16), (3, 14, 14, 1024, "bf16", 1), (2, 7, 7, 2048, "f32", 1),
-                   (4, 9, 9, 64, "f16", 3), (1, 5, 5, 8, "f32", 2), (2, 28, 28, 512, "bf16", 4)]
+                   (4, 9, 9, 64, "f16", 3), (1, 5, 5, 8, "f32", 2), (2, 28, 28, 512, "bf16", 4),
+                   (3, 56, 56, 96, "f32", 1), (2, 7, 7, 768, "bf16", 2), (1, 3, 5, 24, "f32", 1)]
 
 
 @pytest.mark.parametrize("case", GRN_APPLY_CASES, ids=lambda c: "x".join(map(str, c)))
@@ -200,9 +201,27 @@ def test_grn_apply_from_slice_sums(case, oracle, cuda):
 def test_grn_apply_rejects_unsupported_channels(cuda):
     from visionhope_b200.utils.grn_cuda import grn_apply, grn_apply_ok
 
-    for C in (12, 24, 4096):
+    for C in (12, 20, 4096):
         x = torch.zeros(1, C, 2, 2, device=cuda).contiguous(memory_format=torch.channels_last)
         assert not grn_apply_ok(x)
         g = torch.zeros(C, device=cuda)
         with pytest.raises(RuntimeError, match="channels"):
             grn_apply(x, torch.zeros(1, 1, C, device=cuda), g, g, 1e-6)
+
+
+@pytest.mark.parametrize("xdt,rdt,ydt", [(torch.float32, torch.bfloat16, torch.bfloat16),
+                                         (torch.float32, torch.float32, torch.float32),
+                                         (torch.bfloat16, torch.bfloat16, torch.float32)])
+def test_add_cast(xdt, rdt, ydt, cuda):
+    """(y dtype)(x + r) summed in fp32 and rounded once: bit-exact against torch's fp32 add
+    followed by the cast."""
+    from visionhope_b200.utils.bias_act import add_cast
+
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(3, 64, 9, 7, device=cuda, generator=g).to(xdt).contiguous(memory_format=torch.channels_last)
+    r = torch.randn(3, 64, 9, 7, device=cuda, generator=g).to(rdt).contiguous(memory_format=torch.channels_last)
+    y = add_cast(x, r, ydt)
+    assert y.dtype == ydt and y.is_contiguous(memory_format=torch.channels_last)
+    assert torch.equal(y, (x.float() + r.float()).to(ydt))
+    with pytest.raises(RuntimeError):
+        add_cast(x, r.contiguous(), ydt)

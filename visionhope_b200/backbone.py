@@ -19,7 +19,7 @@ from torch.nn import functional as F
 from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
-from .utils.bias_act import bias_act
+from .utils.bias_act import add_cast, add_cast_ok, bias_act
 from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_apply, grn_apply_ok, grn_forward
 from .utils.inference import cache_half_weights, linear_cached
@@ -238,10 +238,16 @@ class Downsample(nn.Module):
         self.proj = nn.Conv2d(in_dim, out_dim, 3, stride=2, padding=1, bias=False)
         self.norm = nn.BatchNorm2d(out_dim)
 
-    def forward(self, x):
+    def forward(self, x, pending=None):
+        """Downsample x (+ pending: the previous stage's last residual branch, added first)."""
         if getattr(self, "_folded", False) and self.proj.out_channels % 8 == 0 and _fused_epilogue_ok(x):
+            if pending is not None:
+                # the stage's last residual add and autocast's bf16 cast of the sum in one pass
+                x = add_cast(x, pending, torch.bfloat16) if add_cast_ok(x, pending) else x + pending
             y = F.conv2d(x, self.proj.weight, None, self.proj.stride, self.proj.padding)
             return bias_act(y, self.proj.bias, None, out_dtype=torch.float32)  # BatchNorm's dtype
+        if pending is not None:
+            x = x + pending
         return self.norm(self.proj(x))
 
     @torch.no_grad()
@@ -432,7 +438,8 @@ class HierarchicalVisionHOPE(nn.Module):
     @staticmethod
     def _run_stage(stage, x):
         """The stage's blocks with each block's last residual add carried into the next block's
-        cpe (one fused pass); the stage's final add is made here."""
+        cpe (one fused pass).  Returns (x, pending): the stage's output is x + pending (pending
+        None when nothing is left to add), so its consumer can fuse the final add."""
         pending = None
         for blk in stage:
             if isinstance(blk, VisionHOPEBlock):
@@ -440,19 +447,29 @@ class HierarchicalVisionHOPE(nn.Module):
             else:
                 x = blk(x if pending is None else x + pending)
                 pending = None
-        return x if pending is None else x + pending
+        return x, pending
 
     def forward_intermediates(self, x):
         outs = []
         for down, stage in zip(self.downsample_layers, self.stages):
-            x = self._run_stage(stage, down(x))
+            x, pending = self._run_stage(stage, down(x))
+            x = x if pending is None else x + pending
             outs.append(x)
         return tuple(outs)
 
     def forward_features(self, x):
-        for down, stage in zip(self.downsample_layers, self.stages):
-            x = self._run_stage(stage, down(x))
-        x = self.head_act(self.head_norm(self.head_pre_logits(self.norm(x))))
+        pending = None
+        for i, (down, stage) in enumerate(zip(self.downsample_layers, self.stages)):
+            if i == 0 or isinstance(down, Downsample):
+                x = down(x) if pending is None else down(x, pending)
+            else:
+                x = down(x if pending is None else x + pending)
+            x, pending = self._run_stage(stage, x)
+        if pending is not None and isinstance(self.norm, LayerNorm2d):
+            _, n = self.norm.forward_add(x, pending)  # the last residual add and the final norm
+        else:
+            n = self.norm(x if pending is None else x + pending)
+        x = self.head_act(self.head_norm(self.head_pre_logits(n)))
         return x.mean(dim=[2, 3])
 
     def forward(self, x):
@@ -477,6 +494,11 @@ def prepare_for_inference(model):
         if isinstance(m, SRNL):
             m.fast_inference = True
             counts["srnl"] += 1
+            # A model converted to channels_last stores the 4-D memory matrices permuted; the
+            # scan reads them dense, so store them dense once instead of copying every call.
+            for mem in m.initial_memories:
+                if not mem.is_contiguous():
+                    mem.data = mem.data.contiguous()
         elif isinstance(m, VisionHOPEOperator):
             counts["operator"] += 1
         elif isinstance(m, LayerNorm2d):

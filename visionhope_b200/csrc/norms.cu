@@ -122,9 +122,10 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
 // grn_factor_kernel: one CTA per image sums the slices in index order and writes the factors
 //   f[b, c] = 1 + gamma[c] Gx[c] / (mean_c Gx + eps), Gx = sqrt(sum)  (as grn_apply_kernel).
 // grn_scale8_kernel: y = x f[b, c] + beta[c] over all 16-byte vectors of the batch, a grid of
-//   a few CTAs per SM striding over them; the stride is a multiple of C / 8, so each thread
-//   keeps one channel group (its betas in registers) and four vector loads are in flight
-//   before any is used.  Needs C % 8 == 0 and C / 8 dividing 256.
+//   a few CTAs per SM striding over them; a CTA has C / 8 x floor(256 / (C / 8)) threads, so
+//   the stride is a multiple of C / 8 and each thread keeps one channel group (its betas in
+//   registers); four vector loads are in flight before any is used.  Needs C % 8 == 0 and
+//   C <= 2048.
 constexpr int kGrnScaleUnroll = 4;
 constexpr int kGrnScaleCtasPerSm = 4;
 
@@ -785,8 +786,8 @@ extern "C" int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sum
     if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || nparts <= 0)
         return fail(VH_E_SHAPE, "GRN expects nonempty input");
     if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_apply_fwd: batch must be <= 65535");
-    if (channels % 8 || channels > 2048 || kGrnThreads % (channels / 8))
-        return fail(VH_E_SHAPE, "vh_grn_apply_fwd: channels must be a multiple of 8 with channels/8 dividing 256");
+    if (channels % 8 || channels > 2048)
+        return fail(VH_E_SHAPE, "vh_grn_apply_fwd: channels must be a multiple of 8, at most 2048");
     const int64_t per_image = (int64_t)height * width * (channels / 8);
     if (per_image * batch >= ((int64_t)1 << 32) - (int64_t)kGrnThreads * 1024 * kGrnScaleUnroll * 2)
         return fail(VH_E_RANGE, "vh_grn_apply_fwd: tensor too large");
@@ -797,12 +798,13 @@ extern "C" int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sum
     int rc = launch_status("grn factors");
     if (rc) return rc;
     const uint32_t nvec = (uint32_t)(per_image * batch);
-    const int64_t want = (nvec + kGrnThreads - 1) / kGrnThreads;
+    const int threads = (channels / 8) * (kGrnThreads / (channels / 8));
+    const int64_t want = (nvec + threads - 1) / threads;
     const dim3 grid((unsigned)std::min<int64_t>(want, (int64_t)sm_count() * kGrnScaleCtasPerSm));
     auto run = [&](auto xt, auto yt) -> int {
         using T = decltype(xt);
         using YT = decltype(yt);
-        grn_scale8_kernel<T, YT><<<grid, kGrnThreads, 0, st>>>(static_cast<const T*>(x), factors, beta,
+        grn_scale8_kernel<T, YT><<<grid, threads, 0, st>>>(static_cast<const T*>(x), factors, beta,
                                                                static_cast<YT*>(y), channels,
                                                                (uint32_t)per_image, nvec);
         return launch_status("grn scale");

@@ -73,20 +73,33 @@ int launch_scan(ScanParams p, const ScanPlan& pl, dim3 grid, cudaStream_t st) {
 
 // Warp-per-chain scan (D = 16, bf16), four warps per CTA: the four scans of one (b, head)
 // (kKindBoth, needs the three aux planes) or four sequence chains (kKindSeq).
-template <int KIND>
-int launch_warp(ScanParams p, int pairs_or_chains, cudaStream_t st) {
+template <int KIND, int TILE>
+int launch_warp_tile(ScanParams p, int pairs_or_chains, cudaStream_t st) {
     p.kind = KIND;
     p.nch = wpc::kWarps;
-    p.tile = wpc::kTile;
-    p.log2tile = 5;
-    const size_t smem = sizeof(wpc::ChainSmem) * wpc::kWarps;
+    p.tile = TILE;
+    p.log2tile = TILE == 16 ? 4 : 5;
+    const size_t smem = sizeof(wpc::ChainSmemT<TILE>) * wpc::kWarps;
     const int per_cta = KIND == kKindBoth ? 1 : wpc::kWarps;
     const dim3 grid((pairs_or_chains + per_cta - 1) / per_cta, KIND == kKindSeq ? p.R : 1);
-    const void* fn = reinterpret_cast<const void*>(&wpc::srnl_warp_kernel<KIND>);
+    const void* fn = reinterpret_cast<const void*>(&wpc::srnl_warp_kernel<KIND, TILE>);
     if (!ensure_smem_attr(fn, smem))
         return fail(VH_E_DEVICE, "srnl warp scan: cannot reserve %zu bytes of shared memory", smem);
-    wpc::srnl_warp_kernel<KIND><<<grid, wpc::kThreads, smem, st>>>(p);
+    wpc::srnl_warp_kernel<KIND, TILE><<<grid, wpc::kThreads, smem, st>>>(p);
     return launch_status("srnl warp scan");
+}
+
+// Steps of 16 tokens when no chunk is longer (VisionHOPE stages 3 and 4), else of 32.
+template <int KIND>
+int launch_warp(const ScanParams& p, int pairs_or_chains, cudaStream_t st) {
+    int maxc = 0;
+    if (KIND == kKindSeq) {
+        for (int r = 0; r < p.R; ++r) maxc = std::max(maxc, p.chunk[r]);
+    } else {
+        maxc = std::max(p.H, p.W);
+    }
+    return maxc <= 16 ? launch_warp_tile<KIND, 16>(p, pairs_or_chains, st)
+                      : launch_warp_tile<KIND, 32>(p, pairs_or_chains, st);
 }
 
 // Sequences: the warp-per-chain scan when it applies (D = 16, bf16, chunks of 9+ tokens).

@@ -43,6 +43,9 @@ namespace wpc {
 #ifndef VH_WPC_MIN_BLOCKS
 #define VH_WPC_MIN_BLOCKS 4
 #endif
+#ifndef VH_WPC_MIN_BLOCKS_16
+#define VH_WPC_MIN_BLOCKS_16 5
+#endif
 
 constexpr int kD = 16;
 constexpr int kWarps = 4;
@@ -51,22 +54,28 @@ constexpr int kTile = 32;  // tokens per step (two 16-row MMA tiles)
 constexpr int kKP = 20;    // padded row stride (floats) of the per-token key rows: 80-byte rows
                            // keep the one-token-per-lane float4 accesses free of bank conflicts
 
-// Per-warp (per-chain) shared memory.
-struct alignas(16) ChainSmem {
+// Per-warp (per-chain) shared memory for steps of TILE tokens (32, or 16 when every chunk
+// has at most 16 tokens: less shared memory per chain, so five CTAs fit an SM).
+template <int TILE>
+struct alignas(16) ChainSmemT {
+    static constexpr int kTileT = TILE;
     // The stacked state as three exact bf16 parts: rows 0-15 M_m, 16-31 M_v, 32-47 M_k,
     // 48 e (learning-rate memory), 49 a (retention memory), 50-63 zero.
     unsigned char mb[kSplits][64][32];
-    float kt[kTile][kKP];               // raw k~, then the normalized key k
-    float dt[kTile][kKP];               // raw v, then d = k - v
-    float4 gate[kTile];                 // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
+    float kt[TILE][kKP];                // raw k~, then the normalized key k
+    float dt[TILE][kKP];                // raw v, then d = k - v
+    float4 gate[TILE];                  // (x.e, x.a) then (eta_eff, alpha, k_t . k_{t+1}, -)
     float fw[2][kD];                    // spatial: this scan's fusion weight and skip per channel
-    unsigned char xq[2][kTile][32];     // the step's x and raw q token rows (bf16, swizzled)
+    unsigned char xq[2][TILE][32];      // the step's x and raw q token rows (bf16, swizzled)
+    static_assert(kSplits * 16 * 32 <= 2 * (int)sizeof(float) * TILE * kKP,
+                  "gain parts must fit the key and value rows");
 };
-static_assert(kSplits * 16 * 32 <= (int)sizeof(float) * kTile * kKP, "gain parts must fit the key rows");
+using ChainSmem = ChainSmemT<kTile>;
 
-// The three bf16 parts of G (row-major, k x n) live in the key rows during the boundary
-// refresh, when no token data is held there.
-__device__ __forceinline__ unsigned char* gain_parts(ChainSmem& cs, int k) {
+// The three bf16 parts of G (row-major, k x n) live in the key (and value) rows during the
+// boundary refresh, when no token data is held there.
+template <class CS>
+__device__ __forceinline__ unsigned char* gain_parts(CS& cs, int k) {
     return reinterpret_cast<unsigned char*>(&cs.kt[0][0]) + k * 16 * 32;
 }
 
@@ -102,7 +111,8 @@ __device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSp
 }
 
 // Stores one 16-value row of the stacked state as its three bf16 parts.
-__device__ __forceinline__ void put_row_splits(ChainSmem& cs, int r, const float* v) {
+template <class CS>
+__device__ __forceinline__ void put_row_splits(CS& cs, int r, const float* v) {
     uint32_t w[kSplits][8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -144,7 +154,8 @@ __device__ __forceinline__ Role warp_role(const ScanParams& p, int warp) {
 // The gain recurrence over the `count` tokens of one step (N > 0: exactly N, unrolled).
 // Lane (row, half) holds G[row][8 half .. 8 half + 7] in g as four column pairs; the dot
 // products and the update run as packed two-lane FMAs (lane pair (2i, 2i+1) of g[i]).
-__device__ __forceinline__ void load_key_half(const ChainSmem& cs, int t, int half, float2 (&k)[4]) {
+template <class CS>
+__device__ __forceinline__ void load_key_half(const CS& cs, int t, int half, float2 (&k)[4]) {
     const float4 lo = *reinterpret_cast<const float4*>(&cs.kt[t][8 * half]);
     const float4 hi = *reinterpret_cast<const float4*>(&cs.kt[t][8 * half + 4]);
     k[0] = make_float2(lo.x, lo.y);
@@ -164,8 +175,8 @@ __device__ __forceinline__ float row_dot(const float2 (&g)[4], const float2 (&k)
     return part;
 }
 
-template <int N>
-__device__ __forceinline__ void gain_pass(const ChainSmem& cs, int count, int row, int half, float2 (&g)[4]) {
+template <int N, class CS>
+__device__ __forceinline__ void gain_pass(const CS& cs, int count, int row, int half, float2 (&g)[4]) {
     if (N > 0) count = N;
     float2 kc[4];
     load_key_half(cs, 0, half, kc);
@@ -196,19 +207,25 @@ __device__ __forceinline__ void gain_pass(const ChainSmem& cs, int count, int ro
 
 // Dispatches the gain recurrence to a fully unrolled body for the step lengths the
 // VisionHOPE stages produce (chunks of 56, 28, 14 and 7 tokens in steps of at most 32).
-__device__ __forceinline__ void gain_step(const ChainSmem& cs, int count, int row, int half, float2 (&g)[4]) {
+template <class CS>
+__device__ __forceinline__ void gain_step(const CS& cs, int count, int row, int half, float2 (&g)[4]) {
+    if constexpr (CS::kTileT == 32) {
+        switch (count) {
+            case 32: gain_pass<32>(cs, count, row, half, g); return;
+            case 28: gain_pass<28>(cs, count, row, half, g); return;
+            case 24: gain_pass<24>(cs, count, row, half, g); return;
+            default: break;
+        }
+    }
     switch (count) {
-        case 32: gain_pass<32>(cs, count, row, half, g); break;
-        case 28: gain_pass<28>(cs, count, row, half, g); break;
-        case 24: gain_pass<24>(cs, count, row, half, g); break;
         case 14: gain_pass<14>(cs, count, row, half, g); break;
         case 7: gain_pass<7>(cs, count, row, half, g); break;
         default: gain_pass<0>(cs, count, row, half, g);
     }
 }
 
-template <bool kSpatial>
-__device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, const Role& ro) {
+template <bool kSpatial, int TILE>
+__device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmemT<TILE>& cs, const Role& ro) {
     using bf16 = __nv_bfloat16;
     const int lane = threadIdx.x & 31;
     const int qg = lane >> 2, qt = lane & 3;  // MMA fragment coordinates
@@ -252,8 +269,8 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
         Lc = p.chunk[dir];
         nchunks = (p.L + Lc - 1) / Lc;
     }
-    const int tpc = (Lc + kTile - 1) / kTile;  // steps per chunk
-    const int last_count = Lc - (tpc - 1) * kTile;
+    const int tpc = (Lc + TILE - 1) / TILE;  // steps per chunk
+    const int last_count = Lc - (tpc - 1) * TILE;
     const int mtiles_last = (last_count + 15) >> 4;
 
     // ---- input addressing ------------------------------------------------------------
@@ -298,10 +315,10 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
     auto prefetch = [&](int c, int j) {
         const int cb = sb + c * sc_step;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int id = u * 32 + lane;  // 128 chunks: tensor, token, half
-            const int tensor = id >> 6, tok = (id >> 1) & 31, half = id & 1;
-            const int tin = j * kTile + tok;
+        for (int u = 0; u < TILE / 8; ++u) {
+            const int id = u * 32 + lane;  // 4 TILE chunks: tensor, token, half
+            const int tensor = id / (2 * TILE), tok = (id >> 1) & (TILE - 1), half = id & 1;
+            const int tin = j * TILE + tok;
             const bool ok = tin < Lc && (kSpatial || (int64_t)c * Lc + tin < p.L);
             const int64_t s = cb + tin * st_step;
             const bf16* src = tensor ? qbase + s * qts : xbase + s * xts;
@@ -319,14 +336,14 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
         for (int i = 0; i < 4; ++i)
             g8[i] = make_float2(p2_half * 8 + 2 * i == p2_row ? 1.f : 0.f, p2_half * 8 + 2 * i + 1 == p2_row ? 1.f : 0.f);
         for (int j = 0; j < tpc; ++j) {
-            const int count = j + 1 < tpc ? kTile : last_count;
-            const int mtiles = j + 1 < tpc ? 2 : mtiles_last;
+            const int count = j + 1 < tpc ? TILE : last_count;
+            const int mtiles = j + 1 < tpc ? TILE / 16 : mtiles_last;
             cp_async_wait<0>();
             __syncwarp();
 
             // ---------------------------- P1: projections -------------------------------
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
+            for (int mt = 0; mt < TILE / 16; ++mt) {
                 if (mt >= mtiles) break;  // warp-uniform
                 float ck[2][4] = {}, cv[2][4] = {}, cy[2][4] = {}, cea[4] = {};
                 // A fragments: {row qg, row qg+8} x {channels 2qt.., 8+2qt..}
@@ -372,14 +389,14 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmem& cs, c
                         const float2 sl = *reinterpret_cast<const float2*>(&cs.fw[1][2 * qt]);
                         const float2 sh = *reinterpret_cast<const float2*>(&cs.fw[1][8 + 2 * qt]);
                         if (row < count) {  // this scan's plane: w_d (y + s_d x) for the pixel
-                            float* op = obase + (int64_t)(pb + c * pc_step + (j * kTile + row) * pt_step) * p.C;
+                            float* op = obase + (int64_t)(pb + c * pc_step + (j * TILE + row) * pt_step) * p.C;
                             *reinterpret_cast<float2*>(op) =
                                 make_float2(wl.x * (y0 + sl.x * x01.x), wl.y * (y1 + sl.y * x01.y));
                             *reinterpret_cast<float2*>(op + 8) =
                                 make_float2(wh.x * (y2 + sh.x * x23.x), wh.y * (y3 + sh.y * x23.y));
                         }
                     } else {
-                        const int64_t t = (int64_t)c * Lc + j * kTile + row;
+                        const int64_t t = (int64_t)c * Lc + j * TILE + row;
                         if (row < count && t < p.L) {
                             bf16* yo = ybase + t * kD;
                             *reinterpret_cast<uint32_t*>(yo) = pack_bf2(y0, y1);
@@ -564,13 +581,14 @@ __device__ __forceinline__ void fold_planes(const ScanParams& p, int b, int head
     }
 }
 
-template <int KIND>
-__global__ void __launch_bounds__(kThreads, VH_WPC_MIN_BLOCKS) srnl_warp_kernel(const ScanParams p) {
+template <int KIND, int TILE>
+__global__ void __launch_bounds__(kThreads, TILE == 16 ? VH_WPC_MIN_BLOCKS_16 : VH_WPC_MIN_BLOCKS)
+    srnl_warp_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5;
-    ChainSmem& cs = reinterpret_cast<ChainSmem*>(smem_raw)[warp];
+    ChainSmemT<TILE>& cs = reinterpret_cast<ChainSmemT<TILE>*>(smem_raw)[warp];
     const Role ro = warp_role<KIND>(p, warp);
-    if (ro.valid) scan_chain<KIND != kKindSeq>(p, cs, ro);
+    if (ro.valid) scan_chain<KIND != kKindSeq, TILE>(p, cs, ro);
     if constexpr (KIND == kKindBoth) {
         __syncthreads();  // the four planes of this (b, head) are complete
         fold_planes(p, ro.b, ro.head);

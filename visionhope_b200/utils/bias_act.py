@@ -1,5 +1,6 @@
 """Bias and activation epilogue of a convolution whose BatchNorm was folded into it
-(``vh_bias_act_fwd``): y = act(x + b) in fp32, rounded once to the requested dtype."""
+(``vh_bias_act_fwd``): y = act(x + b) in fp32, rounded once to the requested dtype; and the
+residual add with a cast (``vh_add_cast_fwd``): y = (dtype)(x + r)."""
 import torch
 
 from .. import _lib
@@ -21,4 +22,28 @@ def bias_act(x, bias, act=None, out_dtype=None):
     _lib.check(_lib.load().vh_bias_act_fwd(
         x.data_ptr(), _lib.dtype_code(x.dtype), b.data_ptr(), y.data_ptr(), _lib.dtype_code(out_dtype),
         B * H * W, C, ACTS[act], _lib.stream_handle(x.device)), "vh_bias_act_fwd")
+    return y
+
+
+def add_cast_ok(x, r):
+    """Whether ``add_cast`` applies: CUDA x and r of one shape, fp32/bf16, both channels-last
+    contiguous (or both contiguous), with a multiple of 8 elements."""
+    def dense(t):
+        return t.is_contiguous(memory_format=torch.channels_last) if t.dim() == 4 else t.is_contiguous()
+    return (x.is_cuda and r.device == x.device and x.shape == r.shape and x.numel() % 8 == 0
+            and x.dtype in (torch.float32, torch.bfloat16) and r.dtype in (torch.float32, torch.bfloat16)
+            and dense(x) and dense(r) and (x.dim() != 4 or x.stride() == r.stride()))
+
+
+@on_tensor_device
+def add_cast(x, r, out_dtype):
+    """(out_dtype)(x + r), summed in fp32 and rounded once, laid out as x."""
+    _lib.ensure_device(x)
+    if not add_cast_ok(x, r):
+        raise RuntimeError("add_cast expects dense fp32/bf16 CUDA tensors of one shape and layout")
+    fmt = torch.channels_last if x.dim() == 4 else torch.contiguous_format
+    y = torch.empty_like(x, dtype=out_dtype, memory_format=fmt)
+    _lib.check(_lib.load().vh_add_cast_fwd(
+        x.data_ptr(), _lib.dtype_code(x.dtype), r.data_ptr(), _lib.dtype_code(r.dtype), y.data_ptr(),
+        _lib.dtype_code(out_dtype), x.numel(), _lib.stream_handle(x.device)), "vh_add_cast_fwd")
     return y
