@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-scan", action="store_true",
                     help="time only the fused SRNL operator at the stage-1 shape (profiling aid)")
+    ap.add_argument("--only-depthwise", action="store_true",
+                    help="time the block's depthwise kernels and GRN apply at the model's shapes and exit")
     ap.add_argument("--only-norms", action="store_true",
                     help="time only GRN and LayerNorm at the GRN/LN configuration's shapes")
     return ap.parse_args()
@@ -355,26 +357,81 @@ def roofline_norms(device, iters=10):
             for name, fn in (("grn", lambda: grn_forward(x, gam, bet, 1e-6)),
                              ("grn_apply", lambda: grn_apply(x, sums, gam, bet, 1e-6)),
                              ("layernorm", lambda: layernorm_rows(xr, w, bet, 1e-6))):
-                for _ in range(3):
-                    fn()
-                times = []
-                n0 = _lib.launch_count
-                for _ in range(iters):
-                    flush.fill_(1.0)
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record()
-                    fn()
-                    b.record()
-                    b.synchronize()
-                    times.append(a.elapsed_time(b))
-                ms = statistics.median(times)
+                ms, launches = _time_calls(fn, iters, flush)
                 nbytes = x.numel() * (x.element_size() + 4)
                 gbs = nbytes / (ms * 1e-3) / 1e9
                 rows.append({"kernel": name, "shape": [B, H, W, C], "dtype_in": str(dt).split(".")[-1],
                              "dtype_out": "float32", "ms": ms, "alg_bytes": nbytes, "achieved_gbs": gbs,
-                             "launches": (_lib.launch_count - n0) // iters,
-                             "frac_of_measured_hbm": gbs / hbm if hbm else None})
+                             "launches": launches, "frac_of_measured_hbm": gbs / hbm if hbm else None})
     return {"norms_roofline": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+
+
+def _time_calls(fn, iters, flush):
+    """Median CUDA-event time (ms) of fn over `iters` calls after 3 warm-up calls, with `flush`
+    rewritten before each (outside the events), and libvhope launches per call."""
+    from visionhope_b200 import _lib
+
+    for _ in range(3):
+        fn()
+    times = []
+    n0 = _lib.launch_count
+    for _ in range(iters):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.median(times), (_lib.launch_count - n0) // iters
+
+
+def roofline_depthwise(device, iters=10):
+    """The block's depthwise kernels and the statistics-fed GRN at VisionHOPE-T's shapes, batch
+    256 (the bench workload), each timed alone: achieved HBM GB/s of the algorithmic bytes
+    against the measured copy bandwidth.  Per element: gelu (FFN, 3x3, with the GRN sums)
+    reads bf16 x and writes bf16 y (4 B); gate (7x7) also reads the bf16 gate (6 B); bias (5x5)
+    4 B; resid_add (cpe, 3x3) reads fp32 x and the bf16 pending branch and writes fp32 (10 B);
+    grn_apply (bf16 in and out, sums from the gelu call) 4 B; grn is the standalone cluster
+    kernel on the same tensor (4 B)."""
+    from visionhope_b200.utils.dwconv import depthwise_fused
+    from visionhope_b200.utils.grn_cuda import grn_apply, grn_forward
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs")
+    flush = torch.empty(64 * 1024 * 1024, device=device)
+    g = torch.Generator(device=device).manual_seed(5)
+    B, bf = 256, torch.bfloat16
+    rows = []
+    with torch.inference_mode():
+        for H, emb, mix in ((56, 64, 32), (28, 128, 64), (14, 256, 128), (7, 512, 256)):
+            def img(C, dt):
+                return torch.randn(B, C, H, H, device=device, generator=g).to(dt).contiguous(
+                    memory_format=torch.channels_last)
+
+            def conv(C, k):
+                return torch.nn.Conv2d(C, C, k, padding=k // 2, groups=C).to(device)
+
+            h, cg = img(4 * emb, bf), conv(4 * emb, 3)
+            y, sums = depthwise_fused(h, cg, "gelu", with_sumsq=True)
+            gam = torch.randn(4 * emb, device=device, generator=g) * 0.02
+            bet = torch.randn(4 * emb, device=device, generator=g) * 0.02
+            xl, gate, cl, cp = img(mix, bf), img(mix, bf), conv(mix, 7), conv(mix, 5)
+            xr, pend, cc = img(emb, torch.float32), img(emb, bf), conv(emb, 3)
+            cases = (("dwconv gelu + GRN sums (3x3)", h, 4, lambda: depthwise_fused(h, cg, "gelu", with_sumsq=True)),
+                     ("grn_apply", y, 4, lambda: grn_apply(y, sums, gam, bet, 1e-6, out_dtype=bf)),
+                     ("grn (cluster)", y, 4, lambda: grn_forward(y, gam, bet, 1e-6, out_dtype=bf)),
+                     ("dwconv gate (7x7)", xl, 6, lambda: depthwise_fused(xl, cl, "gate", gate=gate)),
+                     ("dwconv bias (5x5)", xl, 4, lambda: depthwise_fused(xl, cp, "bias")),
+                     ("dwconv resid_add (3x3, fp32)", xr, 10, lambda: depthwise_fused(xr, cc, "resid", addend=pend)))
+            for name, t, bpe, fn in cases:
+                ms, launches = _time_calls(fn, iters, flush)
+                nbytes = t.numel() * bpe
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                rows.append({"kernel": name, "shape": [B, H, H, t.shape[1]], "ms": ms, "alg_bytes": nbytes,
+                             "achieved_gbs": gbs, "launches": launches,
+                             "frac_of_measured_hbm": gbs / hbm if hbm else None})
+    return {"depthwise_roofline": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
 
 
 def run_ours(args, world, rank, local):
@@ -525,11 +582,16 @@ def main():
                     "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
             return
-        if args.only_scan or args.only_norms:
+        if args.only_scan or args.only_norms or args.only_depthwise:
             if rank == 0:
                 torch.cuda.set_device(local)
                 dev = torch.device("cuda", local)
-                res = roofline_scan(args, dev, args.steps) if args.only_scan else roofline_norms(dev, args.steps)
+                if args.only_scan:
+                    res = roofline_scan(args, dev, args.steps)
+                elif args.only_norms:
+                    res = roofline_norms(dev, args.steps)
+                else:
+                    res = roofline_depthwise(dev, args.steps)
                 print(json.dumps(res), flush=True)
             return
         result = run_ours(args, world, rank, local)

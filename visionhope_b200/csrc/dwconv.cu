@@ -52,12 +52,17 @@ struct Raw8<float> {
     __device__ __forceinline__ void to_float(float (&f)[8]) const {
         f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
     }
+    __device__ __forceinline__ void store_raw(float* p) const {
+        reinterpret_cast<float4*>(p)[0] = a;
+        reinterpret_cast<float4*>(p)[1] = b;
+    }
 };
 template <>
 struct Raw8<__nv_bfloat16> {
     uint4 u;
     __device__ __forceinline__ void load(const __nv_bfloat16* p) { u = __ldg(reinterpret_cast<const uint4*>(p)); }
     __device__ __forceinline__ void to_float(float (&f)[8]) const { load8(reinterpret_cast<const __nv_bfloat16*>(&u), f); }
+    __device__ __forceinline__ void store_raw(__nv_bfloat16* p) const { *reinterpret_cast<uint4*>(p) = u; }
 };
 
 // Four channels as two lane pairs.
@@ -74,8 +79,24 @@ struct DwGeom {
     static constexpr size_t kSmem = sizeof(float) * ((size_t)XS + K * K * kDwCG + kDwCG);
 };
 
+// Epilogue operands of the gated mode staged beside the tile during the load phase, so its
+// epilogue reads only shared memory: the exact fp32 input of every output pixel when x is fp32
+// (the staged tile holds it rounded to bf16), then the gate of every output pixel.  (The
+// residual modes read an fp32 centre from global memory: staging it too costs them more
+// occupancy than the loads cost.)
+template <int K, int MODE, typename T, int TC, int RG, int R>
+struct DwCenter {
+    using G = DwGeom<K, TC, RG, R>;
+    static constexpr bool kGate = MODE == VH_DW_GATE;
+    static constexpr bool kExact = std::is_same<T, float>::value && MODE == VH_DW_GATE;
+    static constexpr size_t kPix = (size_t)G::TH * TC * kDwCG;  // elements per region
+    static constexpr size_t kGateOffset = kExact ? kPix * 4 : 0;  // bytes
+    static constexpr size_t kBytes = kGateOffset + (kGate ? kPix * sizeof(T) : 0);
+    static constexpr size_t kSmem = G::kSmem + kBytes;
+};
+
 template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
-__global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const GT* __restrict__ gate,
+__global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const GT* __restrict__ gate,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, T* __restrict__ y,
                                                                 float* __restrict__ sumsq,
@@ -86,6 +107,8 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
     float* xs = dw_smem;                  // [IH][IW][32]
     float* ws = dw_smem + G::XS;          // [K*K][32]
     float* bs = ws + K * K * kDwCG;       // [32]
+    using CT = DwCenter<K, MODE, T, TC, RG, R>;
+    unsigned char* cbuf = reinterpret_cast<unsigned char*>(bs + kDwCG);  // [TH][TC][32] epilogue operands
     const int tid = threadIdx.x;
     const int b = blockIdx.z, c0 = blockIdx.y * kDwCG;
     const int oy0 = (blockIdx.x / tiles_w) * TH, ox0 = (blockIdx.x % tiles_w) * TC;
@@ -103,17 +126,21 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
     for (int i0 = 0; i0 < IT; i0 += BATCH) {
         Raw8<T> raw[BATCH];
         Raw8<GT> rawa[MODE == VH_DW_RESID_ADD ? BATCH : 1];
-        bool live[BATCH];
+        Raw8<T> rawg[CT::kGate ? BATCH : 1];
+        bool live[BATCH], centre[BATCH];
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
             const int i = (i0 + u) * NT + tid;
             const int v = i & 3, pix = i >> 2;
-            const int gy = oy0 + pix / IW - P, gx = ox0 + pix % IW - P, c = c0 + 8 * v;
+            const int py = pix / IW, px = pix % IW;
+            const int gy = oy0 + py - P, gx = ox0 + px - P, c = c0 + 8 * v;
             live[u] = i0 + u < IT && i < NV && gy >= 0 && gy < H && gx >= 0 && gx < W && c < C;
+            centre[u] = live[u] && py >= P && py < P + TH && px >= P && px < P + TC;
             if (live[u]) {
                 raw[u].load(x + img + ((int64_t)gy * W + gx) * C + c);
                 if (MODE == VH_DW_RESID_ADD) rawa[MODE == VH_DW_RESID_ADD ? u : 0].load(gate + img + ((int64_t)gy * W + gx) * C + c);
             }
+            if (CT::kGate && centre[u]) rawg[CT::kGate ? u : 0].load(reinterpret_cast<const T*>(gate) + img + ((int64_t)gy * W + gx) * C + c);
         }
 #pragma unroll
         for (int u = 0; u < BATCH; ++u) {
@@ -144,6 +171,15 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
                         f[e + 1] = g.y;
                     }
                 }
+                const int pix = i >> 2;
+                const int cidx = ((pix / IW - P) * TC + (pix % IW - P)) * kDwCG + 8 * (i & 3);
+                if (CT::kExact && centre[u]) {  // the exact input of this output pixel
+                    float* d = reinterpret_cast<float*>(cbuf) + cidx;
+                    reinterpret_cast<float4*>(d)[0] = make_float4(f[0], f[1], f[2], f[3]);
+                    reinterpret_cast<float4*>(d)[1] = make_float4(f[4], f[5], f[6], f[7]);
+                }
+                if (CT::kGate && centre[u])
+                    rawg[CT::kGate ? u : 0].store_raw(reinterpret_cast<T*>(cbuf + CT::kGateOffset) + cidx);
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {  // packed round to bf16 and back
                     const float2 r = __bfloat1622float2(__floats2bfloat162_rn(f[e], f[e + 1]));
@@ -197,9 +233,15 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
         if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || MODE == VH_DW_GATE) {
             // The centre value itself: from the staged tile when the input is bf16 (staged
             // exactly), else from global memory (the tile holds it rounded to bf16).
+            // The centre value itself: from the staged tile when the input is bf16 (staged
+            // exactly), else from the exact copy staged for the gated epilogue, or from global
+            // memory.
             float2 xc[2];
+            const int cidx = ((r0 + r) * TC + col) * kDwCG + 4 * q;
             if (std::is_same<T, __nv_bfloat16>::value) {
                 lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, xc);
+            } else if (CT::kExact) {
+                lds4(reinterpret_cast<const float*>(cbuf) + cidx, xc);
             } else {
                 float4 t4 = load4(x + off);
                 if (MODE == VH_DW_RESID_ADD) {
@@ -213,7 +255,7 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 || MODE == VH_DW_GELU) ? 
                 o[0] = fadd2(xc[0], o[0]);
                 o[1] = fadd2(xc[1], o[1]);
             } else {
-                const float4 g = load4(gate + off);
+                const float4 g = load4(reinterpret_cast<const T*>(cbuf + CT::kGateOffset) + cidx);
                 o[0] = ffma2(make_float2(sigmoid_f(g.x), sigmoid_f(g.y)), o[0], xc[0]);
                 o[1] = ffma2(make_float2(sigmoid_f(g.z), sigmoid_f(g.w)), o[1], xc[1]);
             }
@@ -260,9 +302,10 @@ int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
     const int tiles_w = (a.width + TC - 1) / TC, tiles_h = (a.height + G::TH - 1) / G::TH;
     const dim3 grid(tiles_w * tiles_h, (a.channels + kDwCG - 1) / kDwCG, a.batch);
     const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, TC, RG, R>);
-    if (!ensure_smem_attr(fn, G::kSmem))
-        return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", G::kSmem);
-    dwconv_kernel<K, MODE, T, GT, TC, RG, R><<<grid, G::NT, G::kSmem, st>>>(
+    constexpr size_t smem = DwCenter<K, MODE, T, TC, RG, R>::kSmem;
+    if (!ensure_smem_attr(fn, smem))
+        return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", smem);
+    dwconv_kernel<K, MODE, T, GT, TC, RG, R><<<grid, G::NT, smem, st>>>(
         static_cast<const T*>(a.x), static_cast<const GT*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
         MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w);
     return launch_status("depthwise conv");
@@ -315,9 +358,9 @@ void dw_attr_one(const void* fn, size_t smem) { ensure_smem_attr(fn, smem); }
 
 template <int K, int MODE, typename T, typename GT>
 void dw_attr_k() {
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 14, 2, 7>), DwGeom<K, 14, 2, 7>::kSmem);
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 16, 2, 8>), DwGeom<K, 16, 2, 8>::kSmem);
-    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 8, 4, 2>), DwGeom<K, 8, 4, 2>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 14, 2, 7>), DwCenter<K, MODE, T, 14, 2, 7>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 16, 2, 8>), DwCenter<K, MODE, T, 16, 2, 8>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 8, 4, 2>), DwCenter<K, MODE, T, 8, 4, 2>::kSmem);
 }
 
 template <int MODE, typename T, typename GT = T>
