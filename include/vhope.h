@@ -286,6 +286,19 @@ int vh_bias_act_fwd(const void* x, int32_t x_dtype, const float* bias, void* y, 
                     int64_t rows, int32_t channels, int32_t act, vh_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
+ * First stem layer with its BatchNorm folded in (models/layers.py:85-107): a 3x3 convolution,
+ * stride 2, padding 1, of a 3-channel image, then bias and activation:
+ *   y = act(bf16(conv(bf16(x), bf16(w))) + bias), rounded once to y_dtype
+ * (the arithmetic of the convolution under bf16 autocast followed by vh_bias_act_fwd).
+ * x: fp32 [B, H, W, 3] (channels-last image); weight fp32 [C_out, 3, 3, 3] (nn.Conv2d's);
+ * bias fp32 [C_out]; y: [B, (H+1)/2, (W+1)/2, C_out] of y_dtype (VH_F32 or VH_BF16);
+ * C_out in {16, 24, 32, 48, 64}; act VH_ACT_NONE or VH_ACT_GELU.
+ * -------------------------------------------------------------------------------------*/
+int vh_stem_conv_fwd(const float* x, const float* weight, const float* bias, void* y, int32_t y_dtype,
+                     int32_t batch, int32_t height, int32_t width, int32_t out_channels, int32_t act,
+                     vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
  * Residual add with a cast: y = (y_dtype)(x + r), summed in fp32 and rounded once
  * (models/block.py:106, the last block's `x + branch` of a stage, fused with the autocast cast
  * of the downsample convolution that reads it).  x, r, y: n elements each (n a multiple of 8),

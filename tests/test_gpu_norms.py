@@ -225,3 +225,28 @@ def test_add_cast(xdt, rdt, ydt, cuda):
     assert torch.equal(y, (x.float() + r.float()).to(ydt))
     with pytest.raises(RuntimeError):
         add_cast(x, r.contiguous(), ydt)
+
+
+@pytest.mark.parametrize("cout,H,W,act,ydt", [(32, 224, 224, "gelu", torch.bfloat16), (48, 37, 50, "gelu", torch.bfloat16),
+                                              (16, 9, 7, None, torch.float32), (64, 64, 66, "gelu", torch.float32)])
+def test_stem_conv(cout, H, W, act, ydt, cuda):
+    """First stem layer (3x3/2 conv of a 3-channel image, bias, GELU) against the autocast
+    arithmetic written in PyTorch: bf16 inputs and weights, fp32 sums, bf16 convolution output,
+    fp32 bias and exact GELU, one rounding."""
+    import torch.nn.functional as F
+
+    from visionhope_b200.utils.bias_act import stem_conv
+
+    g = torch.Generator(device=cuda).manual_seed(cout + H)
+    x = torch.randn(3, 3, H, W, device=cuda, generator=g).contiguous(memory_format=torch.channels_last)
+    conv = torch.nn.Conv2d(3, cout, 3, stride=2, padding=1).to(cuda)
+    y = stem_conv(x, conv, act, out_dtype=ydt)
+    assert y.dtype == ydt and y.is_contiguous(memory_format=torch.channels_last)
+    with torch.no_grad():
+        c = F.conv2d(x.to(torch.bfloat16).double(), conv.weight.to(torch.bfloat16).double(), None, 2, 1)
+        c = c.to(torch.bfloat16).double() + conv.bias.double().view(1, -1, 1, 1)
+        if act == "gelu":
+            c = F.gelu(c)
+    assert y.shape == c.shape
+    tol = 1e-2 if ydt == torch.bfloat16 else 4e-3
+    assert rel_err(y.double().cpu().numpy(), c.cpu().numpy()) < tol

@@ -19,7 +19,7 @@ from torch.nn import functional as F
 from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
-from .utils.bias_act import add_cast, add_cast_ok, bias_act
+from .utils.bias_act import add_cast, add_cast_ok, bias_act, stem_conv, stem_conv_ok
 from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_apply, grn_apply_ok, grn_forward
 from .utils.inference import cache_half_weights, linear_cached
@@ -205,10 +205,14 @@ class PatchEmbedding(nn.Module):
             # Folded convolutions with the bias (and GELU) applied by one pointwise kernel in
             # fp32: GELU outputs in the autocast dtype (the next convolution's input), the
             # last layer in fp32, the dtype BatchNorm produced (the residual stream's).
-            for conv, gelu in plan:
+            for i, (conv, gelu) in enumerate(plan):
+                out_dtype = _autocast_dtype() if gelu else torch.float32
+                if i == 0 and out_dtype in (torch.bfloat16, torch.float32) and stem_conv_ok(x, conv):
+                    # the 3-channel first layer: convolution, bias and GELU in one kernel
+                    x = stem_conv(x, conv, "gelu" if gelu else None, out_dtype=out_dtype)
+                    continue
                 y = F.conv2d(x, conv.weight, None, conv.stride, conv.padding)
-                x = bias_act(y, conv.bias, "gelu" if gelu else None,
-                             out_dtype=_autocast_dtype() if gelu else torch.float32)
+                x = bias_act(y, conv.bias, "gelu" if gelu else None, out_dtype=out_dtype)
             return self.norm(x)
         return self.norm(self.proj(x))
 

@@ -114,7 +114,7 @@ class VisionHOPEOperator(nn.Module):
     def _inference_path(self, x):
         if self.training:
             return "ordinary", "The operator is in training mode"
-        query_dtype = torch.get_autocast_gpu_dtype() if torch.is_autocast_enabled() else x.dtype
+        query_dtype = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
         path, reason = self.srnl._inference_path(x, query_dtype)
         if path == "ordinary":
             return path, reason

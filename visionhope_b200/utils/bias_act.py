@@ -47,3 +47,33 @@ def add_cast(x, r, out_dtype):
         x.data_ptr(), _lib.dtype_code(x.dtype), r.data_ptr(), _lib.dtype_code(r.dtype), y.data_ptr(),
         _lib.dtype_code(out_dtype), x.numel(), _lib.stream_handle(x.device)), "vh_add_cast_fwd")
     return y
+
+
+def stem_conv_ok(x, conv):
+    """Whether the first stem layer can run as ``stem_conv``: a 3-channel fp32 channels-last
+    CUDA image and a 3x3 stride-2 padding-1 convolution with bias to 16/24/32/48/64 channels."""
+    return (x.is_cuda and x.dim() == 4 and x.shape[1] == 3 and x.dtype == torch.float32
+            and x.is_contiguous(memory_format=torch.channels_last)
+            and conv.in_channels == 3 and conv.out_channels in (16, 24, 32, 48, 64) and conv.groups == 1
+            and conv.kernel_size == (3, 3) and conv.stride == (2, 2) and conv.padding == (1, 1)
+            and conv.dilation == (1, 1) and conv.bias is not None)
+
+
+@on_tensor_device
+def stem_conv(x, conv, act=None, out_dtype=torch.bfloat16):
+    """act(bf16(conv(x)) + b) of a 3-channel channels-last fp32 image (``vh_stem_conv_fwd``):
+    the first stem convolution with its folded BatchNorm and GELU.  Returns a channels-last
+    tensor of ``out_dtype``."""
+    _lib.ensure_device(x)
+    if not stem_conv_ok(x, conv):
+        raise RuntimeError("stem_conv expects a 3-channel fp32 channels-last image and a 3x3/2 convolution")
+    B, _, H, W = x.shape
+    cout = conv.out_channels
+    w = conv.weight.detach().float().contiguous()
+    b = conv.bias.detach().float().contiguous()
+    y = torch.empty((B, cout, (H + 1) // 2, (W + 1) // 2), device=x.device, dtype=out_dtype,
+                    memory_format=torch.channels_last)
+    _lib.check(_lib.load().vh_stem_conv_fwd(
+        x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), _lib.dtype_code(out_dtype), B, H, W, cout,
+        ACTS[act], _lib.stream_handle(x.device)), "vh_stem_conv_fwd")
+    return y
