@@ -264,9 +264,18 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
             lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, h);
             o[0] = gelu2(fadd2(h[0], o[0]));
             o[1] = gelu2(fadd2(h[1], o[1]));
-            if (sumsq && std::is_same<T, __nv_bfloat16>::value) {
-                o[0] = __bfloat1622float2(__floats2bfloat162_rn(o[0].x, o[0].y));
-                o[1] = __bfloat1622float2(__floats2bfloat162_rn(o[1].x, o[1].y));
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+                // Round once: the stored pair is also what the GRN sums see.
+                const __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0].x, o[0].y);
+                const __nv_bfloat162 p1 = __floats2bfloat162_rn(o[1].x, o[1].y);
+                *reinterpret_cast<uint2*>(y + off) = make_uint2(*reinterpret_cast<const uint32_t*>(&p0),
+                                                                *reinterpret_cast<const uint32_t*>(&p1));
+                if (sumsq) {
+                    const float2 s0 = __bfloat1622float2(p0), s1 = __bfloat1622float2(p1);
+                    ss[0] = ffma2(s0, s0, ss[0]);
+                    ss[1] = ffma2(s1, s1, ss[1]);
+                }
+                continue;
             }
             ss[0] = ffma2(o[0], o[0], ss[0]);
             ss[1] = ffma2(o[1], o[1], ss[1]);

@@ -24,9 +24,10 @@
 namespace vh {
 namespace {
 
-constexpr int kStemWarps = 4;            // one output row of the tile per warp
+constexpr int kStemWarps = 4;
+constexpr int kStemRowsPerWarp = 4;      // output rows of the tile per warp
 constexpr int kStemTW = 32;              // output columns per tile (two 16-pixel MMA tiles)
-constexpr int kStemTH = kStemWarps;      // output rows per tile
+constexpr int kStemTH = kStemWarps * kStemRowsPerWarp;  // output rows per tile
 constexpr int kStemIH = 2 * kStemTH + 1; // staged input rows
 constexpr int kStemIW = 2 * kStemTW + 1; // staged input columns
 constexpr int kStemCin = 3;
@@ -49,14 +50,23 @@ __global__ void __launch_bounds__(32 * kStemWarps) stem_conv_kernel(const float*
     const int oy0 = (blockIdx.x / tiles_w) * kStemTH, ox0 = (blockIdx.x % tiles_w) * kStemTW;
     const int iy0 = 2 * oy0 - 1, ix0 = 2 * ox0 - 1;
 
-    // Input window, rounded to bf16, zeros outside the image (the convolution's padding).
+    // Input window, rounded to bf16, zeros outside the image (the convolution's padding);
+    // the loads of a batch are issued before any is converted.
     const float* xb = x + (int64_t)b * H * W * kStemCin;
-    for (int i = tid; i < kStemIH * kStemIW * kStemCin; i += 32 * kStemWarps) {
-        const int c = i % kStemCin, pix = i / kStemCin;
-        const int gy = iy0 + pix / kStemIW, gx = ix0 + pix % kStemIW;
-        float v = 0.f;
-        if (gy >= 0 && gy < H && gx >= 0 && gx < W) v = __ldg(xb + ((int64_t)gy * W + gx) * kStemCin + c);
-        xs[i] = __float2bfloat16_rn(v);
+    constexpr int kN = kStemIH * kStemIW * kStemCin, kT = 32 * kStemWarps, kBatch = 8;
+    for (int i0 = tid; i0 < kN; i0 += kT * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + u * kT;
+            const int c = i % kStemCin, pix = i / kStemCin;
+            const int gy = iy0 + pix / kStemIW, gx = ix0 + pix % kStemIW;
+            v[u] = 0.f;
+            if (i < kN && gy >= 0 && gy < H && gx >= 0 && gx < W) v[u] = __ldg(xb + ((int64_t)gy * W + gx) * kStemCin + c);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (i0 + u * kT < kN) xs[i0 + u * kT] = __float2bfloat16_rn(v[u]);
     }
 
     // B fragments: B[k][n] = w[n][c][ky][kx] with k = (ky * 3 + kx) * 3 + c (k >= 27: zero).
@@ -96,45 +106,47 @@ __global__ void __launch_bounds__(32 * kStemWarps) stem_conv_kernel(const float*
     }
     __syncthreads();
 
-    const int oy = oy0 + warp;
-    if (oy >= Ho) return;
+    for (int rr = 0; rr < kStemRowsPerWarp; ++rr) {
+        const int ry = warp * kStemRowsPerWarp + rr, oy = oy0 + ry;
+        if (oy >= Ho) break;
 #pragma unroll
-    for (int m = 0; m < kStemTW / 16; ++m) {
-        // Rows qg and qg + 8 of this MMA tile: output columns ox0 + 16 m + {qg, qg + 8}.
-        const int base0 = ((2 * warp) * kStemIW + 2 * (16 * m + qg)) * kStemCin;
-        const int base1 = base0 + 2 * 8 * kStemCin;
-        float acc[NT][4];
+        for (int m = 0; m < kStemTW / 16; ++m) {
+            // Rows qg and qg + 8 of this MMA tile: output columns ox0 + 16 m + {qg, qg + 8}.
+            const int base0 = ((2 * ry) * kStemIW + 2 * (16 * m + qg)) * kStemCin;
+            const int base1 = base0 + 2 * 8 * kStemCin;
+            float acc[NT][4];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+            for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            __nv_bfloat16 e0[4], e1[4];
+            for (int s = 0; s < 2; ++s) {
+                __nv_bfloat16 e0[4], e1[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const __nv_bfloat16 z = __float2bfloat16_rn(0.f);
-                e0[j] = koff[s][j] >= 0 ? xs[base0 + koff[s][j]] : z;
-                e1[j] = koff[s][j] >= 0 ? xs[base1 + koff[s][j]] : z;
+                for (int j = 0; j < 4; ++j) {
+                    const __nv_bfloat16 z = __float2bfloat16_rn(0.f);
+                    e0[j] = koff[s][j] >= 0 ? xs[base0 + koff[s][j]] : z;
+                    e1[j] = koff[s][j] >= 0 ? xs[base1 + koff[s][j]] : z;
+                }
+                const uint32_t a[4] = {pack_bf16x2(e0[0], e0[1]), pack_bf16x2(e1[0], e1[1]),
+                                       pack_bf16x2(e0[2], e0[3]), pack_bf16x2(e1[2], e1[3])};
+#pragma unroll
+                for (int t = 0; t < NT; ++t) mma_16816(acc[t], a, bf[t][s][0], bf[t][s][1]);
             }
-            const uint32_t a[4] = {pack_bf16x2(e0[0], e0[1]), pack_bf16x2(e1[0], e1[1]),
-                                   pack_bf16x2(e0[2], e0[3]), pack_bf16x2(e1[2], e1[3])};
+            // Epilogue: round the convolution to bf16, add the bias, GELU, round once more.
 #pragma unroll
-            for (int t = 0; t < NT; ++t) mma_16816(acc[t], a, bf[t][s][0], bf[t][s][1]);
-        }
-        // Epilogue: round the convolution to bf16, add the bias, GELU, round once more.
+            for (int h = 0; h < 2; ++h) {
+                const int ox = ox0 + 16 * m + qg + 8 * h;
+                if (ox >= Wo) continue;
+                YT* yp = y + (((int64_t)b * Ho + oy) * Wo + ox) * COUT + 2 * qt;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int ox = ox0 + 16 * m + qg + 8 * h;
-            if (ox >= Wo) continue;
-            YT* yp = y + (((int64_t)b * Ho + oy) * Wo + ox) * COUT + 2 * qt;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const float2 r = __bfloat1622float2(__floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]));
-                float2 v = make_float2(r.x + bv[t][0], r.y + bv[t][1]);
-                if (GELU) v = gelu2(v);
-                if constexpr (std::is_same<YT, float>::value) {
-                    *reinterpret_cast<float2*>(yp + 8 * t) = v;
-                } else {
-                    *reinterpret_cast<__nv_bfloat162*>(yp + 8 * t) = __floats2bfloat162_rn(v.x, v.y);
+                for (int t = 0; t < NT; ++t) {
+                    const float2 r = __bfloat1622float2(__floats2bfloat162_rn(acc[t][2 * h], acc[t][2 * h + 1]));
+                    float2 v = make_float2(r.x + bv[t][0], r.y + bv[t][1]);
+                    if (GELU) v = gelu2(v);
+                    if constexpr (std::is_same<YT, float>::value) {
+                        *reinterpret_cast<float2*>(yp + 8 * t) = v;
+                    } else {
+                        *reinterpret_cast<__nv_bfloat162*>(yp + 8 * t) = __floats2bfloat162_rn(v.x, v.y);
+                    }
                 }
             }
         }
