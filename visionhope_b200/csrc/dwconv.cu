@@ -121,7 +121,10 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     if (tid < kDwCG) bs[tid] = c0 + tid < C ? round_bf16(bias[c0 + tid]) : 0.f;
     // Input tile with halo, in 8-channel vectors; zero outside the image (the convolution's
     // zero padding).  The loads of a batch are all issued before any of them is converted.
-    constexpr int NV = G::IH * IW * 4, IT = (NV + NT - 1) / NT, BATCH = 4;
+    // Loads per batch: the whole tile at once for the GELU and bias modes (one round trip to
+    // HBM); four for the others, whose extra operands would otherwise spill or cost occupancy.
+    constexpr int NV = G::IH * IW * 4, IT = (NV + NT - 1) / NT;
+    constexpr int BATCH = (MODE == VH_DW_GELU || MODE == VH_DW_BIAS) ? (IT < 8 ? IT : 8) : 4;
 #pragma unroll
     for (int i0 = 0; i0 < IT; i0 += BATCH) {
         Raw8<T> raw[BATCH];
