@@ -203,15 +203,18 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     float2 acc[R][2];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
+    // Per-thread bases; every shared-memory address below is one of these plus a constant.
+    const float* xt = xs + (r0 * IW + col) * kDwCG + 4 * q;
+    const float* wt = ws + 4 * q;
 #pragma unroll
     for (int kx = 0; kx < K; ++kx) {
         float2 wk[K][2];
 #pragma unroll
-        for (int ky = 0; ky < K; ++ky) lds4(ws + (ky * K + kx) * kDwCG + 4 * q, wk[ky]);
+        for (int ky = 0; ky < K; ++ky) lds4(wt + (ky * K + kx) * kDwCG, wk[ky]);
 #pragma unroll
         for (int iy = 0; iy < R + K - 1; ++iy) {
             float2 in[2];
-            lds4(xs + ((r0 + iy) * IW + col + kx) * kDwCG + 4 * q, in);
+            lds4(xt + (iy * IW + kx) * kDwCG, in);
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int ky = iy - r;
@@ -227,22 +230,21 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     float2 ss[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     float2 bv[2];
     lds4(bs + 4 * q, bv);
+    const int64_t off0 = img + ((int64_t)(oy0 + r0) * W + ox) * C + c, row = (int64_t)W * C;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int oy = oy0 + r0 + r;
         if (!out_ok || oy >= H) break;
-        const int64_t off = img + ((int64_t)oy * W + ox) * C + c;
+        const int64_t off = off0 + r * row;
         float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
         if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || MODE == VH_DW_GATE) {
-            // The centre value itself: from the staged tile when the input is bf16 (staged
-            // exactly), else from global memory (the tile holds it rounded to bf16).
             // The centre value itself: from the staged tile when the input is bf16 (staged
             // exactly), else from the exact copy staged for the gated epilogue, or from global
             // memory.
             float2 xc[2];
             const int cidx = ((r0 + r) * TC + col) * kDwCG + 4 * q;
             if (std::is_same<T, __nv_bfloat16>::value) {
-                lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, xc);
+                lds4(xt + ((r + P) * IW + P) * kDwCG, xc);
             } else if (CT::kExact) {
                 lds4(reinterpret_cast<const float*>(cbuf) + cidx, xc);
             } else {
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
             }
         } else if (MODE == VH_DW_GELU) {
             float2 h[2];  // gelu(x) at the centre, as staged
-            lds4(xs + ((r0 + r + P) * IW + col + P) * kDwCG + 4 * q, h);
+            lds4(xt + ((r + P) * IW + P) * kDwCG, h);
             o[0] = gelu2(fadd2(h[0], o[0]));
             o[1] = gelu2(fadd2(h[1], o[1]));
             if constexpr (std::is_same<T, __nv_bfloat16>::value) {
