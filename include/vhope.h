@@ -286,6 +286,16 @@ int vh_bias_act_fwd(const void* x, int32_t x_dtype, const float* bias, void* y, 
                     int64_t rows, int32_t channels, int32_t act, vh_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Row GEMM of the block's 1x1 projections: y[M, N] = x[M, K] W[N, K]^T + bias, bf16 x, W and
+ * y, fp32 bias (may be NULL), fp32 accumulation and one rounding (F.linear under bf16
+ * autocast; models/block.py proj_in / local_gate / proj_out, models/operator.py W_q, the
+ * FFN's fc1 / fc2 as 1x1 convolutions of channels-last tensors).  K and N in
+ * {32, 64, 128, 256} with K * N <= 32768; x, W, y 16-byte aligned, dense rows.
+ * -------------------------------------------------------------------------------------*/
+int vh_rows_gemm_fwd(const void* x, const void* weight, const float* bias, void* y, int64_t rows,
+                     int32_t in_features, int32_t out_features, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
  * First stem layer with its BatchNorm folded in (models/layers.py:85-107): a 3x3 convolution,
  * stride 2, padding 1, of a 3-channel image, then bias and activation:
  *   y = act(bf16(conv(bf16(x), bf16(w))) + bias), rounded once to y_dtype

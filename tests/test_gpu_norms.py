@@ -250,3 +250,32 @@ def test_stem_conv(cout, H, W, act, ydt, cuda):
     assert y.shape == c.shape
     tol = 1e-2 if ydt == torch.bfloat16 else 4e-3
     assert rel_err(y.double().cpu().numpy(), c.cpu().numpy()) < tol
+
+
+@pytest.mark.parametrize("M,K,N", [(802816, 64, 32), (1000, 32, 32), (37, 64, 64), (517, 128, 256), (4099, 256, 128),
+                                   (16, 32, 256)])
+def test_rows_gemm(M, K, N, cuda):
+    """Row GEMM of the 1x1 projections against F.linear with the same bf16 operands: fp32 sums
+    in another order, so within a bf16 rounding; ragged row counts included."""
+    import torch.nn.functional as F
+
+    from visionhope_b200.utils.inference import rows_gemm
+
+    g = torch.Generator(device=cuda).manual_seed(M + K + N)
+    x = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    y = rows_gemm(x, w, b.float())
+    exp = F.linear(x.double(), w.double(), b.double())
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    assert rel_err(y.double().cpu().numpy(), exp.cpu().numpy()) < 4e-3
+    y0 = rows_gemm(x, w, None)
+    assert rel_err(y0.double().cpu().numpy(), (exp - b.double()).cpu().numpy()) < 4e-3
+
+
+def test_rows_gemm_rejects_shapes(cuda):
+    from visionhope_b200.utils.inference import rows_gemm
+
+    x = torch.zeros(8, 48, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        rows_gemm(x, torch.zeros(32, 48, device=cuda, dtype=torch.bfloat16))

@@ -1,0 +1,170 @@
+// Skinny row GEMM for the block's 1x1 projections: y[M, N] = x[M, K] W[N, K]^T + b, bf16 in and
+// out, fp32 accumulation (the arithmetic of F.linear under bf16 autocast: fp32 sums, the bf16
+// bias added in fp32, one rounding).
+//
+// The VisionHOPE block's projections have K, N <= 256 and millions of rows, so they are
+// bounded by HBM, not by the tensor cores: the kernel is shaped to stream x once at full
+// bandwidth.  The weights (at most 64 KB) sit in shared memory for the whole CTA; each warp
+// walks 16-row tiles of x and feeds `mma.sync.m16n8k16` straight from 16-byte global loads:
+//
+//   Within each 32-channel slice, lane (g, q) of the MMA fragment holds rows g and g + 8 of the
+//   tile and the logical K indices {2q, 2q+1, 2q+8, 2q+9} of two 16-wide K steps.  The kernel
+//   assigns those eight logical indices to the eight consecutive physical channels 8q .. 8q+7,
+//   for x and for W alike.  The dot product is a sum over all channels, so any bijection used
+//   for both operands gives the same result, and then each lane's A fragment for a slice is
+//   one 16-byte load per row, and its B fragment one 16-byte shared-memory read of a W row.
+#include <algorithm>
+
+#include "abi_util.h"
+#include "common.cuh"
+#include "srnl_scan.cuh"
+
+namespace vh {
+namespace {
+
+constexpr int kRgWarps = 8;
+constexpr int kRgThreads = 32 * kRgWarps;
+constexpr int kRgNGroup = 64;  // output columns per accumulation pass (8 n-tiles)
+
+template <int K, int N>
+struct RgGeom {
+    // Padded W row (bf16): a row stride of 64 bytes modulo 128 puts the 16-byte reads of the
+    // 8 lanes of one shared-memory phase (2 rows x 4 slices) in distinct banks.
+    static constexpr int KP = K % 64 == 0 ? K + 32 : K;
+    static constexpr size_t kSmem = (size_t)N * KP * 2 + (size_t)N * 4;
+};
+
+template <int K, int N>
+__global__ void __launch_bounds__(kRgThreads, 2) rows_gemm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                  const __nv_bfloat16* __restrict__ w,
+                                                                  const float* __restrict__ bias,
+                                                                  __nv_bfloat16* __restrict__ y, int64_t M) {
+    using G = RgGeom<K, N>;
+    constexpr int KC = K / 32;                       // 32-channel slices
+    constexpr int NG = N < kRgNGroup ? N : kRgNGroup;
+    constexpr int NT = NG / 8;                       // n-tiles per pass
+    extern __shared__ __align__(16) unsigned char rg_smem[];
+    __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(rg_smem);          // [N][KP]
+    float* bs = reinterpret_cast<float*>(rg_smem + (size_t)N * G::KP * 2);  // [N]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, q = lane & 3;
+
+    for (int i = tid; i < N * K / 8; i += kRgThreads) {
+        const int n = i / (K / 8), k8 = i % (K / 8);
+        *reinterpret_cast<uint4*>(ws + n * G::KP + 8 * k8) = *reinterpret_cast<const uint4*>(w + (int64_t)n * K + 8 * k8);
+    }
+    for (int n = tid; n < N; n += kRgThreads) bs[n] = bias ? bias[n] : 0.f;
+    __syncthreads();
+
+    // A warp takes MT 16-row tiles at a time (every B fragment read from shared memory then
+    // feeds 2 MT MMAs).  One tile measured fastest at the shapes this kernel serves: more tiles
+    // per warp cost registers and CTAs that the loads in flight do not recover.
+    constexpr int MT = 1;
+    const int64_t groups = (M + 16 * MT - 1) / (16 * MT);
+    for (int64_t grp = (int64_t)blockIdx.x * kRgWarps + warp; grp < groups; grp += (int64_t)gridDim.x * kRgWarps) {
+        uint4 a0[MT][KC], a1[MT][KC];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const int64_t r0 = (grp * MT + m) * 16 + g, r1 = r0 + 8;
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+                a0[m][c] = r0 < M ? __ldcs(reinterpret_cast<const uint4*>(x + r0 * K + 32 * c + 8 * q)) : make_uint4(0, 0, 0, 0);
+                a1[m][c] = r1 < M ? __ldcs(reinterpret_cast<const uint4*>(x + r1 * K + 32 * c + 8 * q)) : make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int n0 = 0; n0 < N; n0 += NG) {
+            float acc[MT][NT][4];
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) acc[m][t][0] = acc[m][t][1] = acc[m][t][2] = acc[m][t][3] = 0.f;
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const uint4 b = *reinterpret_cast<const uint4*>(ws + (n0 + 8 * t + g) * G::KP + 32 * c + 8 * q);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        const uint32_t A0[4] = {a0[m][c].x, a1[m][c].x, a0[m][c].y, a1[m][c].y};
+                        const uint32_t A1[4] = {a0[m][c].z, a1[m][c].z, a0[m][c].w, a1[m][c].w};
+                        mma_16816(acc[m][t], A0, b.x, b.y);
+                        mma_16816(acc[m][t], A1, b.z, b.w);
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int64_t r0 = (grp * MT + m) * 16 + g, r1 = r0 + 8;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const int col = n0 + 8 * t + 2 * q;
+                    const float b0 = bs[col], b1 = bs[col + 1];
+                    if (r0 < M)
+                        *reinterpret_cast<__nv_bfloat162*>(y + r0 * N + col) =
+                            __floats2bfloat162_rn(acc[m][t][0] + b0, acc[m][t][1] + b1);
+                    if (r1 < M)
+                        *reinterpret_cast<__nv_bfloat162*>(y + r1 * N + col) =
+                            __floats2bfloat162_rn(acc[m][t][2] + b0, acc[m][t][3] + b1);
+                }
+            }
+        }
+    }
+}
+
+template <int K, int N>
+int rows_gemm_run(const void* x, const void* w, const float* bias, void* y, int64_t M, cudaStream_t st) {
+    using G = RgGeom<K, N>;
+    const void* fn = reinterpret_cast<const void*>(&rows_gemm_kernel<K, N>);
+    if (!ensure_smem_attr(fn, G::kSmem))
+        return fail(VH_E_DEVICE, "row gemm: cannot reserve %zu bytes of shared memory", G::kSmem);
+    static int per_sm = 0;  // resident CTAs per SM of this instantiation
+    if (per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kRgThreads, G::kSmem) != cudaSuccess || n <= 0) n = 1;
+        per_sm = n;
+    }
+    const int64_t tiles = (M + 15) / 16;
+    const int64_t want = (tiles + kRgWarps - 1) / kRgWarps;
+    const int grid = (int)std::min<int64_t>(want, (int64_t)per_sm * sm_count());
+    rows_gemm_kernel<K, N><<<grid, kRgThreads, G::kSmem, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                               static_cast<const __nv_bfloat16*>(w), bias,
+                                                               static_cast<__nv_bfloat16*>(y), M);
+    return launch_status("row gemm");
+}
+
+template <int K>
+int rows_gemm_n(int N, const void* x, const void* w, const float* bias, void* y, int64_t M, cudaStream_t st) {
+    switch (N) {
+        case 32: return rows_gemm_run<K, 32>(x, w, bias, y, M, st);
+        case 64: return rows_gemm_run<K, 64>(x, w, bias, y, M, st);
+        case 128: return rows_gemm_run<K, 128>(x, w, bias, y, M, st);
+        default: return rows_gemm_run<K, 256>(x, w, bias, y, M, st);
+    }
+}
+
+}  // namespace
+}  // namespace vh
+
+using namespace vh;
+
+extern "C" int vh_rows_gemm_fwd(const void* x, const void* weight, const float* bias, void* y, int64_t rows,
+                                int32_t in_features, int32_t out_features, vh_stream_t stream) {
+    clear_error();
+    if (!x || !weight || !y) return fail(VH_E_ARG, "vh_rows_gemm_fwd: null pointer argument");
+    const int K = in_features, N = out_features;
+    auto pow2_ok = [](int v) { return v == 32 || v == 64 || v == 128 || v == 256; };
+    if (!pow2_ok(K) || !pow2_ok(N) || K * N > 32768)
+        return fail(VH_E_SHAPE, "vh_rows_gemm_fwd: in/out features must be 32, 64, 128 or 256 with in*out <= 32768 "
+                    "(got %d x %d)", K, N);
+    if (rows <= 0) return fail(VH_E_SHAPE, "vh_rows_gemm_fwd: empty input");
+    if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(y, 16) || (bias && !aligned(bias, 4)))
+        return fail(VH_E_ALIGN, "vh_rows_gemm_fwd: misaligned pointers");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (K) {
+        case 32: return rows_gemm_n<32>(N, x, weight, bias, y, rows, st);
+        case 64: return rows_gemm_n<64>(N, x, weight, bias, y, rows, st);
+        case 128: return rows_gemm_n<128>(N, x, weight, bias, y, rows, st);
+        default: return rows_gemm_n<256>(N, x, weight, bias, y, rows, st);
+    }
+}
