@@ -5,7 +5,7 @@ normalization (``models/srnl.py:113-114`` rejects CPU tensors), and ships no gol
 vectors.  The strongest parity pin available is therefore the reference's own CUDA
 extensions, run on a B200.  This recipe:
 
-1. imports the reference package read-only from ``/root/reference`` (with a
+1. imports the reference package read-only from its checkout (``VHOPE_REFERENCE``; with a
    four-alias ``timm`` shim, because timm is not installed) so that the reference
    renders its own templated sources exactly as it does at run time
    (``models/srnl_core/fused.py:51-64``, ``chunk.py:89-105``, ``lines.py:59-70``,

@@ -7,7 +7,7 @@ LayerNorm2d).  This script imports the reference read-only (with a four-alias ``
 timm is not installed), runs those paths on seeded inputs and stores inputs and outputs in
 ``tests/golden/cpu_*.npz``.
 
-Usage:  python tests/golden/make_golden_cpu.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden_cpu.py [--reference <reference checkout>]
 """
 from __future__ import annotations
 

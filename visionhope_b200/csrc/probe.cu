@@ -1,5 +1,5 @@
 // Measurement helper: an FFMA throughput probe used by bench.py to measure the FP32
-// (non-tensor) peak of the device the SRNL scan is judged against.
+// (non-tensor) peak of the device, the denominator of the SRNL scan's roofline.
 #include "abi_util.h"
 #include "common.cuh"
 
