@@ -158,3 +158,41 @@ def test_grn_workspace_query():
     lib = _lib.load()
     assert lib.vh_grn_workspace_bytes(128, 56, 56, 96) > 0
     assert lib.vh_grn_workspace_bytes(0, 56, 56, 96) == 0
+
+
+def test_harness_entry_points_validate_without_a_gpu():
+    """The harness kernels' entry points reject bad shapes, dtypes and pointers with a status
+    and a message before any CUDA call."""
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    # row GEMM: unsupported feature counts, empty input, misaligned x
+    assert lib.vh_rows_gemm_fwd(p, p, p, p, 16, 48, 32, None) == -2
+    assert "in/out features" in _err(lib)
+    assert lib.vh_rows_gemm_fwd(p, p, p, p, 0, 64, 32, None) == -2
+    assert lib.vh_rows_gemm_fwd(p + 4, p, p, p, 16, 64, 32, None) == -5
+    assert lib.vh_rows_gemm_fwd(None, p, p, p, 16, 64, 32, None) == -1
+    # stem convolution: output channels, activation, dtype
+    assert lib.vh_stem_conv_fwd(p, p, p, p, 1, 2, 32, 32, 40, 1, None) == -2
+    assert "out_channels" in _err(lib)
+    assert lib.vh_stem_conv_fwd(p, p, p, p, 1, 2, 32, 32, 32, 7, None) == -1
+    assert lib.vh_stem_conv_fwd(p, p, p, p, 2, 2, 32, 32, 32, 1, None) == -3
+    # add + cast: element count and dtype
+    assert lib.vh_add_cast_fwd(p, 0, p, 1, p, 1, 12, None) == -2
+    assert lib.vh_add_cast_fwd(p, 2, p, 1, p, 1, 16, None) == -3
+    # statistics-fed GRN: channel count
+    assert lib.vh_grn_apply_fwd(p, 1, p, 1, p, p, 1e-6, p, p, 1, 2, 4, 4, 12, None) == -2
+    assert "channels" in _err(lib)
+    assert lib.vh_grn_apply_fwd(p, 1, p, 1, p, p, 1e-6, p, p, 1, 2, 4, 4, 4096, None) == -2
+
+
+def test_dwconv_tile_count_query():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.vh_dwconv_tiles(56, 56) == 16   # 14 x 14 tiles
+    assert lib.vh_dwconv_tiles(14, 14) == 1
+    assert lib.vh_dwconv_tiles(7, 7) == 1      # one 8 x 8 tile
+    assert lib.vh_dwconv_tiles(32, 32) == 4    # 16 x 16 tiles
+    assert lib.vh_dwconv_tiles(0, 5) == 0
