@@ -98,6 +98,28 @@ def _grn_target():
     return "vhref_grn", [str(src / "grn.cpp"), str(src / "grn_cuda.cu")]
 
 
+def _names():
+    return [t[0] for t in _targets()] + [_grn_target()[0]]
+
+
+def build_parallel(workers=None):
+    """Build every reference extension, several at a time in spawned processes (each one is a
+    separate nvcc job of a few minutes; built ones are up to date and return at once)."""
+    import concurrent.futures as cf
+    import multiprocessing as mp
+
+    if not REF_ROOT.is_dir():
+        raise FileNotFoundError(f"reference tree not found at {REF_ROOT}")
+    _install_reference()
+    names = _names()
+    workers = workers or max(1, min(len(names), (os.cpu_count() or 2) // 2))
+    built = []
+    with cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")) as ex:
+        for res in ex.map(build, [[n] for n in names]):
+            built += res
+    return built
+
+
 def build(only=None):
     if not REF_ROOT.is_dir():
         raise FileNotFoundError(f"reference tree not found at {REF_ROOT}")
@@ -107,18 +129,25 @@ def build(only=None):
     OUT_DIR.mkdir(parents=True, exist_ok=True)
     flags = ["-O3", "--use_fast_math", *GENCODE]
     built = []
+    def fresh_dir(name):
+        # A build killed half-way leaves torch's `lock` file behind, and the next build of the
+        # same extension would wait on it for ever; this script builds each extension in one
+        # process only, so a lock found here is always such a leftover.
+        d = OUT_DIR / name
+        d.mkdir(parents=True, exist_ok=True)
+        (d / "lock").unlink(missing_ok=True)
+        return d
+
     for name, cpp, cuda, fns in _targets():
         if only and name not in only:
             continue
-        build_dir = OUT_DIR / name
-        build_dir.mkdir(parents=True, exist_ok=True)
+        build_dir = fresh_dir(name)
         load_inline(name=name, cpp_sources=cpp, cuda_sources=cuda, functions=fns,
                     extra_cuda_cflags=flags, build_directory=str(build_dir), verbose=False)
         built.append(name)
     name, sources = _grn_target()
     if not only or name in only:
-        build_dir = OUT_DIR / name
-        build_dir.mkdir(parents=True, exist_ok=True)
+        build_dir = fresh_dir(name)
         load(name=name, sources=sources, extra_cuda_cflags=["-O3", *GENCODE], extra_cflags=["-O3"],
              build_directory=str(build_dir), verbose=False)
         built.append(name)
@@ -141,4 +170,4 @@ def load_built(name):
 
 
 if __name__ == "__main__":
-    print("built:", build(sys.argv[1:] or None))
+    print("built:", build(sys.argv[1:]) if sys.argv[1:] else build_parallel())
