@@ -186,7 +186,8 @@ def run_cpu(args, steps, warmup):
 
 # ----------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region (every 200 ms)."""
+    """nvidia-smi clock/throttle samples during the timed region (every 50 ms; entering waits,
+    up to 5 s, for the first sample, so that the sampler runs before the timed region starts)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -195,6 +196,7 @@ class ClockSampler:
     def __init__(self):
         self.proc = None
         self.path = None
+        self.skip = 0
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -202,9 +204,15 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            if Path(self.path).stat().st_size > 0:
+                break
+            time.sleep(0.02)
+        self.skip = len(Path(self.path).read_text().splitlines()) if self.path else 0
         return self
 
     def __exit__(self, *exc):
@@ -220,7 +228,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         mhz, mx, reasons, power = [], [], set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in Path(self.path).read_text().splitlines():
+        for line in Path(self.path).read_text().splitlines()[self.skip:]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
