@@ -296,6 +296,20 @@ int vh_rows_gemm_fwd(const void* x, const void* weight, const float* bias, void*
                      int32_t in_features, int32_t out_features, vh_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
+ * The block's first LayerNorm and input projection in one pass (models/block.py:104, norm1
+ * then proj_in; norm: models/layers.py:9-35, projection: the 1x1 convolution proj_in):
+ *   y[M, N] = bf16(LayerNorm(x)[M, K]) W[N, K]^T + bias,
+ * LayerNorm over each row's K channels (biased variance, eps inside the square root, fp32
+ * ln_weight / ln_bias), its result rounded to bf16 as the projection under bf16 autocast reads
+ * it, then the row GEMM's arithmetic (fp32 accumulation, fp32 bias may be NULL, one rounding).
+ * x: fp32 [M, K] (the residual stream); W, y bf16.  K in {32, 64, 128}, N in {32, 64}; x, W,
+ * y, ln_weight and ln_bias 16-byte aligned, dense rows.  The normalized rows are not written.
+ * -------------------------------------------------------------------------------------*/
+int vh_ln_rows_gemm_fwd(const float* x, const float* ln_weight, const float* ln_bias, float eps,
+                        const void* weight, const float* bias, void* y, int64_t rows,
+                        int32_t in_features, int32_t out_features, vh_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
  * First stem layer with its BatchNorm folded in (models/layers.py:85-107): a 3x3 convolution,
  * stride 2, padding 1, of a 3-channel image, then bias and activation:
  *   y = act(bf16(conv(bf16(x), bf16(w))) + bias), rounded once to y_dtype

@@ -173,6 +173,14 @@ def test_harness_entry_points_validate_without_a_gpu():
     assert lib.vh_rows_gemm_fwd(p, p, p, p, 0, 64, 32, None) == -2
     assert lib.vh_rows_gemm_fwd(p + 4, p, p, p, 16, 64, 32, None) == -5
     assert lib.vh_rows_gemm_fwd(None, p, p, p, 16, 64, 32, None) == -1
+    # LayerNorm + row GEMM: feature counts, empty input, eps, misaligned x, null pointers
+    assert lib.vh_ln_rows_gemm_fwd(p, p, p, 1e-6, p, p, p, 16, 256, 32, None) == -2
+    assert "in_features" in _err(lib)
+    assert lib.vh_ln_rows_gemm_fwd(p, p, p, 1e-6, p, p, p, 16, 64, 128, None) == -2
+    assert lib.vh_ln_rows_gemm_fwd(p, p, p, 1e-6, p, p, p, 0, 64, 32, None) == -2
+    assert lib.vh_ln_rows_gemm_fwd(p, p, p, -1.0, p, p, p, 16, 64, 32, None) == -1
+    assert lib.vh_ln_rows_gemm_fwd(p + 4, p, p, 1e-6, p, p, p, 16, 64, 32, None) == -5
+    assert lib.vh_ln_rows_gemm_fwd(p, None, p, 1e-6, p, p, p, 16, 64, 32, None) == -1
     # stem convolution: output channels, activation, dtype
     assert lib.vh_stem_conv_fwd(p, p, p, p, 1, 2, 32, 32, 40, 1, None) == -2
     assert "out_channels" in _err(lib)

@@ -273,6 +273,48 @@ def test_rows_gemm(M, K, N, cuda):
     assert rel_err(y0.double().cpu().numpy(), (exp - b.double()).cpu().numpy()) < 4e-3
 
 
+@pytest.mark.parametrize("M,K,N", [(802816, 64, 32), (200704, 128, 64), (1000, 32, 32), (37, 64, 64),
+                                   (4099, 128, 32), (16, 32, 64)])
+def test_ln_rows_gemm(M, K, N, cuda):
+    """norm1 -> proj_in in one kernel against (a) the two kernels it replaces (LayerNorm
+    writing bf16, then the row GEMM) and (b) an fp64 restatement of LayerNorm, bf16 rounding
+    and F.linear.  The row statistics are summed in another order than the LayerNorm kernel's,
+    so a normalized value can differ by one bf16 rounding: both within 4e-3 normwise."""
+    import torch.nn.functional as F
+
+    from visionhope_b200.utils.inference import ln_rows_gemm, rows_gemm
+    from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
+
+    g = torch.Generator(device=cuda).manual_seed(3 * M + K + N)
+    x = torch.randn(M, K, device=cuda, generator=g) * 2.0 + 0.5
+    lw = 1.0 + 0.02 * torch.randn(K, device=cuda, generator=g)
+    lb = 0.02 * torch.randn(K, device=cuda, generator=g)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    eps = 1e-6
+    y = ln_rows_gemm(x, lw, lb, eps, w, b.float())
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    two = rows_gemm(layernorm_rows(x, lw, lb, eps, out_dtype=torch.bfloat16), w, b.float())
+    assert rel_err(y.double().cpu().numpy(), two.double().cpu().numpy()) < 4e-3
+    n = F.layer_norm(x.double(), (K,), lw.double(), lb.double(), eps).to(torch.bfloat16).double()
+    exp = F.linear(n, w.double(), b.double())
+    assert rel_err(y.double().cpu().numpy(), exp.cpu().numpy()) < 4e-3
+    y0 = ln_rows_gemm(x, lw, lb, eps, w, None)
+    assert rel_err(y0.double().cpu().numpy(), (exp - b.double()).cpu().numpy()) < 4e-3
+
+
+def test_ln_rows_gemm_rejects_shapes(cuda):
+    from visionhope_b200.utils.inference import ln_rows_gemm
+
+    x = torch.zeros(8, 256, device=cuda)
+    ones, zeros = torch.ones(256, device=cuda), torch.zeros(256, device=cuda)
+    with pytest.raises(RuntimeError):
+        ln_rows_gemm(x, ones, zeros, 1e-6, torch.zeros(32, 256, device=cuda, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError):  # bf16 x: the kernel reads the fp32 residual stream
+        ln_rows_gemm(x[:, :64].to(torch.bfloat16), ones[:64], zeros[:64], 1e-6,
+                     torch.zeros(32, 64, device=cuda, dtype=torch.bfloat16))
+
+
 def test_rows_gemm_rejects_shapes(cuda):
     from visionhope_b200.utils.inference import rows_gemm
 

@@ -110,6 +110,9 @@ def load() -> ctypes.CDLL:
             lib.vh_rows_gemm_fwd.restype = c_int32
             lib.vh_rows_gemm_fwd.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
                                              c_void_p]
+            lib.vh_ln_rows_gemm_fwd.restype = c_int32
+            lib.vh_ln_rows_gemm_fwd.argtypes = [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                                c_int64, c_int32, c_int32, c_void_p]
             lib.vh_stem_conv_fwd.restype = c_int32
             lib.vh_stem_conv_fwd.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                              c_int32, c_int32, c_int32, c_void_p]

@@ -22,8 +22,13 @@ from .utils.grn import GlobalResponseNorm
 from .utils.bias_act import add_cast, add_cast_ok, bias_act, stem_conv, stem_conv_ok
 from .utils.dwconv import depthwise_fused, fusable
 from .utils.grn_cuda import grn_apply, grn_apply_ok, grn_forward
-from .utils.inference import cache_half_weights, linear_cached
+from .utils.inference import cache_half_weights, linear_cached, norm_linear_cached
 from .utils.layer_norm_cuda import add_layernorm_rows, layernorm_rows
+
+
+# (in, out) channels of proj_in where norm1 runs as the projection's prologue: the stage-1 and
+# stage-2 shapes of VisionHOPE-T, narrow enough for the row GEMM.
+_NORM1_PROJ_IN_FUSED = {(64, 32), (128, 64)}
 
 
 def _autocast_dtype():
@@ -308,8 +313,20 @@ class VisionHOPEBlock(nn.Module):
             self.gamma1 = None
             self.gamma2 = None
 
-    def _local_features(self, x):
-        inner = pointwise(self.proj_in, x)
+    def _norm1_proj_in(self, x):
+        """proj_in(norm1(x)) as one kernel (the LayerNorm as the row GEMM's prologue) for the
+        prepared block under bf16 autocast, at the projection shapes where that measured faster
+        than the two passes; None elsewhere."""
+        if not (self._inference_prepared and isinstance(self.norm1, LayerNorm2d) and x.is_cuda
+                and x.is_contiguous(memory_format=torch.channels_last)
+                and (self.proj_in.in_channels, self.proj_in.out_channels) in _NORM1_PROJ_IN_FUSED):
+            return None
+        inner = norm_linear_cached(self.norm1, self.proj_in, x.permute(0, 2, 3, 1))
+        return None if inner is None else inner.permute(0, 3, 1, 2)
+
+    def _local_features(self, x, inner=None):
+        if inner is None:
+            inner = pointwise(self.proj_in, x)
         if self.local_mode == "gated_dwconv7":
             gate = pointwise(self.local_gate, inner)
             if fusable(inner, self.local_conv) and gate.dtype == inner.dtype:
@@ -318,9 +335,11 @@ class VisionHOPEBlock(nn.Module):
         conv = self.local_act(self.local_conv(inner))
         return conv if self.local_mode == "silu_dwconv" else inner + conv
 
-    def spatial_branch(self, x):
+    def spatial_branch(self, x, *, inner=None):
+        """The mixer branch on x = norm1(block input); ``inner`` = proj_in(x) when the caller
+        already computed it (then x only supplies the memory format)."""
         channels_last = x.is_contiguous(memory_format=torch.channels_last)
-        x_local = self._local_features(x)
+        x_local = self._local_features(x, inner)
         if self._inference_prepared:
             path, _ = self.operator._inference_path(x_local)
             if path != "ordinary":
@@ -370,7 +389,8 @@ class VisionHOPEBlock(nn.Module):
                 x = x + self.cpe(x)
         elif pending is not None:
             x = x + pending
-        branch = self.spatial_branch(self.norm1(x))
+        inner = self._norm1_proj_in(x)
+        branch = self.spatial_branch(self.norm1(x)) if inner is None else self.spatial_branch(x, inner=inner)
         if self.gamma1 is None and isinstance(self.norm2, LayerNorm2d):
             # x + branch and norm2 in one pass; x is this block's own tensor once cpe ran
             x, n2 = self.norm2.forward_add(x, branch, inplace=self.cpe is not None)

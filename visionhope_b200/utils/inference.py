@@ -56,6 +56,49 @@ def rows_gemm(x, w, bias32=None):
     return y
 
 
+def ln_rows_gemm_ok(k, n):
+    """Shapes the LayerNorm + row GEMM kernel takes (``vh_ln_rows_gemm_fwd``)."""
+    return k in (32, 64, 128) and n in (32, 64)
+
+
+def ln_rows_gemm(x, ln_weight, ln_bias, eps, w, bias32=None):
+    """bf16(LayerNorm(x)) W^T + b over the rows of fp32 ``x`` [..., K] in one pass: the
+    block's norm1 followed by proj_in under bf16 autocast, without writing the normalized rows
+    (``vh_ln_rows_gemm_fwd``).  ``w``: bf16 [N, K]; ``bias32``: the fp32 (widened bf16) bias."""
+    from .. import _lib
+
+    _lib.ensure_device(x)
+    n, k = w.shape
+    if (x.dtype != torch.float32 or w.dtype != torch.bfloat16 or x.shape[-1] != k or not ln_rows_gemm_ok(k, n)
+            or ln_weight.numel() != k or ln_bias.numel() != k):
+        raise RuntimeError("ln_rows_gemm expects fp32 x [..., K], bf16 W [N, K], K in {32, 64, 128}, N in {32, 64}")
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    lw = ln_weight.detach().reshape(-1).float().contiguous()
+    lb = ln_bias.detach().reshape(-1).float().contiguous()
+    y = torch.empty(x.shape[:-1] + (n,), device=x.device, dtype=torch.bfloat16)
+    _lib.check(_lib.load().vh_ln_rows_gemm_fwd(x2.data_ptr(), lw.data_ptr(), lb.data_ptr(), float(eps), w.data_ptr(),
+                                               _lib.ptr(bias32), y.data_ptr(), x2.shape[0], k, n,
+                                               _lib.stream_handle(x.device)), "vh_ln_rows_gemm_fwd")
+    return y
+
+
+def norm_linear_cached(norm, module, x):
+    """``linear_cached(module, norm(x))`` in one kernel when ``norm`` is a LayerNorm over the
+    last dim of fp32 rows ``x`` and the projection's cached bf16 weight has a shape the fused
+    kernel takes (under bf16 autocast, autograd off); None otherwise, for the caller to run the
+    two operations."""
+    cached = getattr(module, "_vh_half", None)
+    if (cached is None or x.dtype != torch.float32 or not x.is_cuda or torch.is_grad_enabled()
+            or not _autocast_bf16() or cached[0].device != x.device or not x.is_contiguous()):
+        return None
+    n, k = cached[0].shape
+    if not ln_rows_gemm_ok(k, n) or x.shape[-1] != k or norm.weight is None or norm.bias is None:
+        return None
+    return ln_rows_gemm(x, norm.weight, norm.bias, norm.eps, cached[0], getattr(module, "_vh_bias32", None))
+
+
 def linear_cached(module, x):
     """``F.linear(x, W, b)`` for a Linear or a 1x1 Conv2d applied to channels-last rows ``x``
     (last dim = in_features), using the cached bf16 weights when x is bf16 under bf16 autocast
