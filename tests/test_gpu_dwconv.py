@@ -54,6 +54,15 @@ CASES = [
     (1, 8, 7, 7, 7, "gate", torch.float32),       # kernel wider than half the image
     (2, 64, 14, 14, 3, "resid_add", torch.float32),   # cpe of x + a pending bf16 residual
     (1, 32, 9, 13, 3, "resid_add", torch.bfloat16),
+    # 7 x 7 images run four whole images per CTA: batches that do not fill the last CTA,
+    # channel counts that do not fill the last 32-channel group
+    (5, 256, 7, 7, 3, "gelu", torch.bfloat16),
+    (6, 40, 7, 7, 7, "gate", torch.bfloat16),
+    (9, 32, 7, 7, 7, "gate", torch.float32),
+    (5, 64, 7, 7, 5, "bias", torch.bfloat16),
+    (2, 48, 7, 7, 3, "resid", torch.float32),
+    (3, 96, 7, 7, 3, "resid_add", torch.float32),
+    (7, 24, 7, 7, 3, "resid_add", torch.bfloat16),
 ]
 
 
@@ -109,8 +118,9 @@ def test_dwconv_rejects_bad_arguments(cuda):
         depthwise_fused(x, conv, "gate")
 
 
-@pytest.mark.parametrize("shape", [(2, 256, 56, 56), (3, 1024, 14, 14), (2, 2048, 7, 7), (1, 96, 23, 5),
-                                   (2, 512, 28, 28)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("shape", [(2, 256, 56, 56), (3, 1024, 14, 14), (2, 2048, 7, 7), (5, 2048, 7, 7),
+                                   (6, 40, 7, 7), (1, 96, 23, 5), (2, 512, 28, 28)],
+                         ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
 def test_dwconv_gelu_tile_sums(shape, dt, cuda):
     """The GELU epilogue's per-tile sums of y^2 (the statistics of the GRN that follows): y is

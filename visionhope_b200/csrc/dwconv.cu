@@ -72,9 +72,14 @@ __device__ __forceinline__ void lds4(const float* p, float2 (&v)[2]) {
     v[1] = make_float2(a.z, a.w);
 }
 
-template <int K, int TC, int RG, int R>
+// MI (several images per CTA): the image is R x TC pixels, and row group g of the CTA owns the
+// whole of image RG * blockIdx.z + g, staged as its own (R + K - 1) x (TC + K - 1) halo region.
+// Small images then fill a CTA: at 7 x 7 a one-image tile spends most of its time on the
+// per-CTA fixed costs (weights, barriers, launch).
+template <int K, int TC, int RG, int R, bool MI = false>
 struct DwGeom {
-    static constexpr int TH = RG * R, P = K / 2, IH = TH + K - 1, IW = TC + K - 1, NT = 8 * TC * RG;
+    static constexpr int TH = RG * R, P = K / 2, SR = R + K - 1;
+    static constexpr int IH = MI ? RG * SR : TH + K - 1, IW = TC + K - 1, NT = 8 * TC * RG;
     static constexpr int XS = IH * IW * kDwCG;  // floats of the staged tile
     static constexpr size_t kSmem = sizeof(float) * ((size_t)XS + K * K * kDwCG + kDwCG);
 };
@@ -84,9 +89,9 @@ struct DwGeom {
 // (the staged tile holds it rounded to bf16), then the gate of every output pixel.  (The
 // residual modes read an fp32 centre from global memory: staging it too costs them more
 // occupancy than the loads cost.)
-template <int K, int MODE, typename T, int TC, int RG, int R>
+template <int K, int MODE, typename T, int TC, int RG, int R, bool MI = false>
 struct DwCenter {
-    using G = DwGeom<K, TC, RG, R>;
+    using G = DwGeom<K, TC, RG, R, MI>;
     static constexpr bool kGate = MODE == VH_DW_GATE;
     static constexpr bool kExact = std::is_same<T, float>::value && MODE == VH_DW_GATE;
     static constexpr size_t kPix = (size_t)G::TH * TC * kDwCG;  // elements per region
@@ -95,24 +100,25 @@ struct DwCenter {
     static constexpr size_t kSmem = G::kSmem + kBytes;
 };
 
-template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
+template <int K, int MODE, typename T, typename GT, int TC, int RG, int R, bool MI = false>
 __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 || MODE == VH_DW_GELU) ? 3 : 4) dwconv_kernel(const T* __restrict__ x, const GT* __restrict__ gate,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, T* __restrict__ y,
                                                                 float* __restrict__ sumsq,
-                                                                int H, int W, int C, int tiles_w) {
-    using G = DwGeom<K, TC, RG, R>;
-    constexpr int TH = G::TH, P = G::P, IW = G::IW, NT = G::NT;
+                                                                int H, int W, int C, int tiles_w, int B) {
+    using G = DwGeom<K, TC, RG, R, MI>;
+    constexpr int TH = G::TH, P = G::P, IW = G::IW, NT = G::NT, SR = G::SR;
     extern __shared__ __align__(16) float dw_smem[];
     float* xs = dw_smem;                  // [IH][IW][32]
     float* ws = dw_smem + G::XS;          // [K*K][32]
     float* bs = ws + K * K * kDwCG;       // [32]
-    using CT = DwCenter<K, MODE, T, TC, RG, R>;
+    using CT = DwCenter<K, MODE, T, TC, RG, R, MI>;
     unsigned char* cbuf = reinterpret_cast<unsigned char*>(bs + kDwCG);  // [TH][TC][32] epilogue operands
     const int tid = threadIdx.x;
-    const int b = blockIdx.z, c0 = blockIdx.y * kDwCG;
-    const int oy0 = (blockIdx.x / tiles_w) * TH, ox0 = (blockIdx.x % tiles_w) * TC;
-    const int64_t img = (int64_t)b * H * W * C;
+    // MI: images b0 .. b0 + RG - 1, one per row group; otherwise one tile of image b0.
+    const int b0 = MI ? blockIdx.z * RG : blockIdx.z, c0 = blockIdx.y * kDwCG;
+    const int oy0 = MI ? 0 : (blockIdx.x / tiles_w) * TH, ox0 = MI ? 0 : (blockIdx.x % tiles_w) * TC;
+    const int64_t plane = (int64_t)H * W * C;
 
     for (int i = tid; i < K * K * kDwCG; i += NT) {
         const int tap = i / kDwCG, cc = i % kDwCG, c = c0 + cc;
@@ -136,9 +142,12 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
             const int i = (i0 + u) * NT + tid;
             const int v = i & 3, pix = i >> 2;
             const int py = pix / IW, px = pix % IW;
-            const int gy = oy0 + py - P, gx = ox0 + px - P, c = c0 + 8 * v;
-            live[u] = i0 + u < IT && i < NV && gy >= 0 && gy < H && gx >= 0 && gx < W && c < C;
-            centre[u] = live[u] && py >= P && py < P + TH && px >= P && px < P + TC;
+            // MI: staged row py is row ly of the halo region of image b0 + py / SR.
+            const int ly = MI ? py % SR : py, bi = MI ? b0 + py / SR : b0;
+            const int gy = oy0 + ly - P, gx = ox0 + px - P, c = c0 + 8 * v;
+            live[u] = i0 + u < IT && i < NV && gy >= 0 && gy < H && gx >= 0 && gx < W && c < C && bi < B;
+            centre[u] = live[u] && ly >= P && ly < P + (MI ? R : TH) && px >= P && px < P + TC;
+            const int64_t img = (int64_t)bi * plane;
             if (live[u]) {
                 raw[u].load(x + img + ((int64_t)gy * W + gx) * C + c);
                 if (MODE == VH_DW_RESID_ADD) rawa[MODE == VH_DW_RESID_ADD ? u : 0].load(gate + img + ((int64_t)gy * W + gx) * C + c);
@@ -174,8 +183,10 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
                         f[e + 1] = g.y;
                     }
                 }
-                const int pix = i >> 2;
-                const int cidx = ((pix / IW - P) * TC + (pix % IW - P)) * kDwCG + 8 * (i & 3);
+                const int pix = i >> 2, py = pix / IW;
+                // output pixel row within the CTA's [TH][TC] operands (MI: image row group first)
+                const int orow = MI ? (py / SR) * R + py % SR - P : py - P;
+                const int cidx = (orow * TC + (pix % IW - P)) * kDwCG + 8 * (i & 3);
                 if (CT::kExact && centre[u]) {  // the exact input of this output pixel
                     float* d = reinterpret_cast<float*>(cbuf) + cidx;
                     reinterpret_cast<float4*>(d)[0] = make_float4(f[0], f[1], f[2], f[3]);
@@ -197,14 +208,16 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     }
     __syncthreads();
 
-    const int q = tid & 7, col = (tid >> 3) % TC, r0 = ((tid >> 3) / TC) * R;
+    const int q = tid & 7, col = (tid >> 3) % TC, rg = (tid >> 3) / TC, r0 = rg * R;
     const int c = c0 + 4 * q, ox = ox0 + col;
-    const bool out_ok = c < C && ox < W;
+    const int b = MI ? b0 + rg : b0;
+    const int64_t img = (int64_t)b * plane;
+    const bool out_ok = c < C && ox < W && b < B;
     float2 acc[R][2];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
     // Per-thread bases; every shared-memory address below is one of these plus a constant.
-    const float* xt = xs + (r0 * IW + col) * kDwCG + 4 * q;
+    const float* xt = xs + ((MI ? rg * SR : r0) * IW + col) * kDwCG + 4 * q;
     const float* wt = ws + 4 * q;
 #pragma unroll
     for (int kx = 0; kx < K; ++kx) {
@@ -230,10 +243,10 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     float2 ss[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     float2 bv[2];
     lds4(bs + 4 * q, bv);
-    const int64_t off0 = img + ((int64_t)(oy0 + r0) * W + ox) * C + c, row = (int64_t)W * C;
+    const int64_t off0 = img + ((int64_t)(oy0 + (MI ? 0 : r0)) * W + ox) * C + c, row = (int64_t)W * C;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const int oy = oy0 + r0 + r;
+        const int oy = oy0 + (MI ? 0 : r0) + r;
         if (!out_ok || oy >= H) break;
         const int64_t off = off0 + r * row;
         float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
@@ -287,7 +300,20 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
         }
         store4(y + off, make_float4(o[0].x, o[0].y, o[1].x, o[1].y));
     }
-    if (MODE == VH_DW_GELU && sumsq) {
+    if (MI && MODE == VH_DW_GELU && sumsq) {
+        // Per-image channel sums in a fixed order (the columns of the image's row group; a row
+        // group need not start on a warp boundary, so the sums go through shared memory).
+        __syncthreads();
+        *reinterpret_cast<float4*>(xs + 4 * tid) = make_float4(ss[0].x, ss[0].y, ss[1].x, ss[1].y);
+        __syncthreads();
+        if (tid < RG * kDwCG) {
+            const int g = tid / kDwCG, ch = tid % kDwCG, bi = b0 + g;
+            float t = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < TC; ++cc) t += xs[4 * ((g * TC + cc) * 8 + ch / 4) + ch % 4];
+            if (bi < B && c0 + ch < C) sumsq[(int64_t)bi * C + c0 + ch] = t;
+        }
+    } else if (MODE == VH_DW_GELU && sumsq) {
         // Per-tile channel sums in a fixed order: the four lanes of a warp that share channels
         // (lane bits 3-4), then the warps in index order; the staged tile is free by now.
 #pragma unroll
@@ -310,18 +336,18 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
     }
 }
 
-template <int K, int MODE, typename T, typename GT, int TC, int RG, int R>
+template <int K, int MODE, typename T, typename GT, int TC, int RG, int R, bool MI = false>
 int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
-    using G = DwGeom<K, TC, RG, R>;
-    const int tiles_w = (a.width + TC - 1) / TC, tiles_h = (a.height + G::TH - 1) / G::TH;
-    const dim3 grid(tiles_w * tiles_h, (a.channels + kDwCG - 1) / kDwCG, a.batch);
-    const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, TC, RG, R>);
-    constexpr size_t smem = DwCenter<K, MODE, T, TC, RG, R>::kSmem;
+    using G = DwGeom<K, TC, RG, R, MI>;
+    const int tiles_w = MI ? 1 : (a.width + TC - 1) / TC, tiles_h = MI ? 1 : (a.height + G::TH - 1) / G::TH;
+    const dim3 grid(tiles_w * tiles_h, (a.channels + kDwCG - 1) / kDwCG, MI ? (a.batch + RG - 1) / RG : a.batch);
+    const void* fn = reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, TC, RG, R, MI>);
+    constexpr size_t smem = DwCenter<K, MODE, T, TC, RG, R, MI>::kSmem;
     if (!ensure_smem_attr(fn, smem))
         return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", smem);
-    dwconv_kernel<K, MODE, T, GT, TC, RG, R><<<grid, G::NT, smem, st>>>(
+    dwconv_kernel<K, MODE, T, GT, TC, RG, R, MI><<<grid, G::NT, smem, st>>>(
         static_cast<const T*>(a.x), static_cast<const GT*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
-        MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w);
+        MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w, a.batch);
     return launch_status("depthwise conv");
 }
 
@@ -335,8 +361,12 @@ inline int dw_tile_side(int H, int W) {
     return a16 <= a8 ? 16 : 8;
 }
 
+// Images of 7 x 7 pixels (the last stage at 224 x 224): four whole images per CTA.
+constexpr int kDwMiImages = 4;
+
 template <int K, int MODE, typename T, typename GT>
 int dw_tile(const vh_dwconv_args& a, cudaStream_t st) {
+    if (a.height == 7 && a.width == 7) return dw_launch<K, MODE, T, GT, 7, kDwMiImages, 7, true>(a, st);
     switch (dw_tile_side(a.height, a.width)) {
         case 14: return dw_launch<K, MODE, T, GT, 14, 2, 7>(a, st);
         case 16: return dw_launch<K, MODE, T, GT, 16, 2, 8>(a, st);
@@ -375,6 +405,8 @@ void dw_attr_k() {
     dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 14, 2, 7>), DwCenter<K, MODE, T, 14, 2, 7>::kSmem);
     dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 16, 2, 8>), DwCenter<K, MODE, T, 16, 2, 8>::kSmem);
     dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 8, 4, 2>), DwCenter<K, MODE, T, 8, 4, 2>::kSmem);
+    dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<K, MODE, T, GT, 7, kDwMiImages, 7, true>),
+                DwCenter<K, MODE, T, 7, kDwMiImages, 7, true>::kSmem);
 }
 
 template <int MODE, typename T, typename GT = T>
@@ -412,6 +444,7 @@ using namespace vh;
 
 extern "C" int vh_dwconv_tiles(int32_t height, int32_t width) {
     if (height <= 0 || width <= 0) return 0;
+    if (height == 7 && width == 7) return 1;  // whole images per CTA
     const int t = dw_tile_side(height, width);
     return ((height + t - 1) / t) * ((width + t - 1) / t);
 }

@@ -67,10 +67,13 @@ __global__ void __launch_bounds__(kRgThreads, 2) rows_gemm_kernel(const void* __
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, q = lane & 3;
 
+    // W goes to shared memory as asynchronous 16-byte copies, all in flight at once; the CTA
+    // waits for them only after its warps have issued the loads of their first x tile.
     for (int i = tid; i < N * K / 8; i += kRgThreads) {
         const int n = i / (K / 8), k8 = i % (K / 8);
-        *reinterpret_cast<uint4*>(ws + n * G::KP + 8 * k8) = *reinterpret_cast<const uint4*>(w + (int64_t)n * K + 8 * k8);
+        cp_async<16>(ws + n * G::KP + 8 * k8, w + (int64_t)n * K + 8 * k8);
     }
+    cp_async_commit();
     for (int n = tid; n < N; n += kRgThreads) bs[n] = bias ? bias[n] : 0.f;
     if constexpr (LN) {
         for (int k = tid; k < K; k += kRgThreads) {
@@ -78,14 +81,24 @@ __global__ void __launch_bounds__(kRgThreads, 2) rows_gemm_kernel(const void* __
             lbs[k] = lnb[k];
         }
     }
-    __syncthreads();
+    // Every warp runs the tile loop at least once (an iteration past the last tile loads and
+    // stores nothing), so every thread reaches this barrier exactly once.
+    bool first = true;
+    auto weights_ready = [&]() {
+        if (first) {
+            cp_async_wait<0>();
+            __syncthreads();
+            first = false;
+        }
+    };
 
     // A warp takes MT 16-row tiles at a time (every B fragment read from shared memory then
     // feeds 2 MT MMAs).  One tile measured fastest at the shapes this kernel serves: more tiles
     // per warp cost registers and CTAs that the loads in flight do not recover.
     constexpr int MT = 1;
     const int64_t groups = (M + 16 * MT - 1) / (16 * MT);
-    for (int64_t grp = (int64_t)blockIdx.x * kRgWarps + warp; grp < groups; grp += (int64_t)gridDim.x * kRgWarps) {
+    for (int64_t grp = (int64_t)blockIdx.x * kRgWarps + warp; first || grp < groups;
+         grp += (int64_t)gridDim.x * kRgWarps) {
         uint4 a0[MT][KC], a1[MT][KC];
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
@@ -97,6 +110,7 @@ __global__ void __launch_bounds__(kRgThreads, 2) rows_gemm_kernel(const void* __
                     a0[m][c] = r0 < M ? __ldcs(reinterpret_cast<const uint4*>(x + r0 * K + 32 * c + 8 * q)) : make_uint4(0, 0, 0, 0);
                     a1[m][c] = r1 < M ? __ldcs(reinterpret_cast<const uint4*>(x + r1 * K + 32 * c + 8 * q)) : make_uint4(0, 0, 0, 0);
                 }
+                weights_ready();
             } else {
                 // This lane's 8 channels of each slice for rows r0 and r1, then each row's
                 // statistics over its four lanes: mean, then the centred sum of squares, and
@@ -118,6 +132,7 @@ __global__ void __launch_bounds__(kRgThreads, 2) rows_gemm_kernel(const void* __
                         v[h][c][4] = hi.x; v[h][c][5] = hi.y; v[h][c][6] = hi.z; v[h][c][7] = hi.w;
                     }
                 }
+                weights_ready();  // also orders the LayerNorm parameters written above
                 float mean[2], rstd[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
