@@ -127,7 +127,17 @@ __global__ void __launch_bounds__(kGrnThreads) grn_apply_kernel(
 //   registers); four vector loads are in flight before any is used.  Needs C % 8 == 0 and
 //   C <= 2048.
 constexpr int kGrnScaleUnroll = 4;
-constexpr int kGrnScaleCtasPerSm = 4;
+// CTAs per SM: 16-bit x loads its factors together with x (3 CTAs, registers for both); fp32 x
+// (twice the registers per vector) reads them after its x loads, at 4 CTAs.
+template <typename T>
+constexpr int grn_scale_ctas_per_sm() { return sizeof(T) == 4 ? 4 : 3; }
+
+// A thread owns the channels tid, tid + 256, ... (at most kGrnFactorCh of them: C <= 2048) and
+// keeps their sums in registers from the one pass over the slices: the loads of kGrnFactorK
+// slices for all its channels are issued before any is added, and each channel still sums its
+// slices in index order.
+constexpr int kGrnFactorCh = 8;
+constexpr int kGrnFactorK = 4;
 
 __global__ void __launch_bounds__(kGrnThreads) grn_factor_kernel(const float* __restrict__ part, int nparts,
                                                                  const float* __restrict__ gamma, float eps,
@@ -135,11 +145,29 @@ __global__ void __launch_bounds__(kGrnThreads) grn_factor_kernel(const float* __
     __shared__ float scratch[32];
     const int b = blockIdx.x;
     const float* pb = part + (int64_t)b * nparts * C;
+    float s[kGrnFactorCh];
+#pragma unroll
+    for (int j = 0; j < kGrnFactorCh; ++j) s[j] = 0.f;
+    for (int k0 = 0; k0 < nparts; k0 += kGrnFactorK) {
+        float v[kGrnFactorK][kGrnFactorCh];
+#pragma unroll
+        for (int k = 0; k < kGrnFactorK; ++k)
+#pragma unroll
+            for (int j = 0; j < kGrnFactorCh; ++j) {
+                const int c = threadIdx.x + j * kGrnThreads;
+                v[k][j] = (k0 + k < nparts && c < C) ? pb[(int64_t)(k0 + k) * C + c] : 0.f;
+            }
+#pragma unroll
+        for (int k = 0; k < kGrnFactorK; ++k)
+#pragma unroll
+            for (int j = 0; j < kGrnFactorCh; ++j)
+                if (k0 + k < nparts) s[j] += v[k][j];
+    }
     float local = 0.f;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float s = 0.f;
-        for (int k = 0; k < nparts; ++k) s += pb[(int64_t)k * C + c];
-        local += sqrtf(s);
+#pragma unroll
+    for (int j = 0; j < kGrnFactorCh; ++j) {
+        s[j] = sqrtf(s[j]);  // Gx of this thread's channel j
+        if (threadIdx.x + j * kGrnThreads < C) local += s[j];
     }
     local = warp_sum(local);
     if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = local;
@@ -151,15 +179,15 @@ __global__ void __launch_bounds__(kGrnThreads) grn_factor_kernel(const float* __
     }
     __syncthreads();
     const float inv_den = scratch[0];
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float s = 0.f;
-        for (int k = 0; k < nparts; ++k) s += pb[(int64_t)k * C + c];
-        fac_out[(int64_t)b * C + c] = 1.f + gamma[c] * (sqrtf(s) * inv_den);
+#pragma unroll
+    for (int j = 0; j < kGrnFactorCh; ++j) {
+        const int c = threadIdx.x + j * kGrnThreads;
+        if (c < C) fac_out[(int64_t)b * C + c] = 1.f + gamma[c] * (s[j] * inv_den);
     }
 }
 
 template <typename T, typename YT>
-__global__ void __launch_bounds__(kGrnThreads, kGrnScaleCtasPerSm) grn_scale8_kernel(
+__global__ void __launch_bounds__(kGrnThreads, grn_scale_ctas_per_sm<T>()) grn_scale8_kernel(
     const T* __restrict__ x, const float* __restrict__ fac, const float* __restrict__ beta,
     YT* __restrict__ y, int C, uint32_t per_image, uint32_t nvec) {
     const uint32_t G8 = (uint32_t)C >> 3, stride = gridDim.x * blockDim.x;
@@ -169,7 +197,10 @@ __global__ void __launch_bounds__(kGrnThreads, kGrnScaleCtasPerSm) grn_scale8_ke
 #pragma unroll
     for (int e = 0; e < 8; ++e) bt[e] = beta[c + e];
     for (uint32_t v = v0; v < nvec; v += stride * kGrnScaleUnroll) {
+        // 16-bit x: the factors of each vector are loaded with it, so neither waits for the other.
+        constexpr bool kEarly = sizeof(T) != 4;
         uint4 raw[kGrnScaleUnroll][sizeof(T) == 4 ? 2 : 1];
+        float4 fa[kEarly ? kGrnScaleUnroll : 1], fb[kEarly ? kGrnScaleUnroll : 1];
 #pragma unroll
         for (int u = 0; u < kGrnScaleUnroll; ++u) {
             const uint32_t vu = v + u * stride;
@@ -177,14 +208,26 @@ __global__ void __launch_bounds__(kGrnThreads, kGrnScaleCtasPerSm) grn_scale8_ke
                 const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)vu * 8);
 #pragma unroll
                 for (int h = 0; h < (sizeof(T) == 4 ? 2 : 1); ++h) raw[u][h] = __ldcs(src + h);
+                if constexpr (kEarly) {
+                    const float* f = fac + (size_t)(vu / per_image) * C + c;
+                    fa[u] = *reinterpret_cast<const float4*>(f);
+                    fb[u] = *reinterpret_cast<const float4*>(f + 4);
+                }
             }
         }
 #pragma unroll
         for (int u = 0; u < kGrnScaleUnroll; ++u) {
             const uint32_t vu = v + u * stride;
             if (vu >= nvec) break;
-            const float* f = fac + (size_t)(vu / per_image) * C + c;
-            const float4 f0 = *reinterpret_cast<const float4*>(f), f1 = *reinterpret_cast<const float4*>(f + 4);
+            float4 f0, f1;
+            if constexpr (kEarly) {
+                f0 = fa[u];
+                f1 = fb[u];
+            } else {
+                const float* f = fac + (size_t)(vu / per_image) * C + c;
+                f0 = *reinterpret_cast<const float4*>(f);
+                f1 = *reinterpret_cast<const float4*>(f + 4);
+            }
             float xv[8];
             load8(reinterpret_cast<const T*>(&raw[u][0]), xv);
             const float fv[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
@@ -800,10 +843,10 @@ extern "C" int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sum
     const uint32_t nvec = (uint32_t)(per_image * batch);
     const int threads = (channels / 8) * (kGrnThreads / (channels / 8));
     const int64_t want = (nvec + threads - 1) / threads;
-    const dim3 grid((unsigned)std::min<int64_t>(want, (int64_t)sm_count() * kGrnScaleCtasPerSm));
     auto run = [&](auto xt, auto yt) -> int {
         using T = decltype(xt);
         using YT = decltype(yt);
+        const dim3 grid((unsigned)std::min<int64_t>(want, (int64_t)sm_count() * grn_scale_ctas_per_sm<T>()));
         grn_scale8_kernel<T, YT><<<grid, threads, 0, st>>>(static_cast<const T*>(x), factors, beta,
                                                                static_cast<YT*>(y), channels,
                                                                (uint32_t)per_image, nvec);
