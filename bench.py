@@ -401,7 +401,8 @@ def roofline_depthwise(device, iters=10):
     reads bf16 x and writes bf16 y (4 B); gate (7x7) also reads the bf16 gate (6 B); bias (5x5)
     4 B; resid_add (cpe, 3x3) reads fp32 x and the bf16 pending branch and writes fp32 (10 B);
     grn_apply (bf16 in and out, sums from the gelu call) 4 B; grn is the standalone cluster
-    kernel on the same tensor (4 B)."""
+    kernel on the same tensor (4 B); gate + position (the gated 7x7 and the 5x5 position term
+    in one call, 14x14 and 7x7 images) reads x and the gate and writes both outputs (8 B)."""
     from visionhope_b200.utils.dwconv import depthwise_fused
     from visionhope_b200.utils.grn_cuda import grn_apply, grn_forward
 
@@ -432,6 +433,11 @@ def roofline_depthwise(device, iters=10):
                      ("dwconv gate (7x7)", xl, 6, lambda: depthwise_fused(xl, cl, "gate", gate=gate)),
                      ("dwconv bias (5x5)", xl, 4, lambda: depthwise_fused(xl, cp, "bias")),
                      ("dwconv resid_add (3x3, fp32)", xr, 10, lambda: depthwise_fused(xr, cc, "resid", addend=pend)))
+            if H in (14, 7):  # whole images per CTA: the gated 7x7 and the position 5x5 in one call
+                def gate_pos():
+                    with torch.autocast("cuda", dtype=bf):  # the mode's eligibility rule asks for it
+                        return depthwise_fused(xl, cl, "gate_pos", gate=gate, pos_conv=cp)
+                cases += (("dwconv gate + position (7x7, 5x5)", xl, 8, gate_pos),)
             for name, t, bpe, fn in cases:
                 ms, launches = _time_calls(fn, iters, flush)
                 nbytes = t.numel() * bpe

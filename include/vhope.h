@@ -242,13 +242,19 @@ int vh_layernorm_fwd(const void* x, int32_t x_dtype, const float* weight, const 
  *   VH_DW_GELU   h = gelu(x);  y = gelu(h + conv(h) + b)      (gelu: exact erf form)
  *   VH_DW_RESID_ADD  s = x + r (r in `gate`, gate_dtype);  y = s + (conv(s) + b): the block's
  *                cpe applied to the previous block's output without materialising it
+ *   VH_DW_GATE_POS  y as VH_DW_GATE, then pos_y = conv_pos(y) + pos_bias from the same CTA's
+ *                copy of y (the block's local features followed by its output position
+ *                term, models/block.py:57-62 and :78).  bf16 only, ksize 7, pos_ksize 5, and
+ *                whole images per CTA: H = W = 14 or H = W = 7.  Bit-identical to VH_DW_GATE
+ *                followed by VH_DW_BIAS on y.
  * x, gate, y: dense [B, H, W, C] of `dtype` (VH_F32 or VH_BF16), 16-byte aligned, y distinct
  * from the inputs; weight fp32 [C, K, K] (nn.Conv2d's [C, 1, K, K]); bias fp32 [C];
  * C a multiple of 8.  The convolution reads input, weight and bias rounded to bf16 and sums in
  * fp32 (a bf16 convolution under autocast); the residual and gate terms use x and gate as
  * given; y is rounded once.
  * -------------------------------------------------------------------------------------*/
-enum vh_dw_mode { VH_DW_BIAS = 0, VH_DW_RESID = 1, VH_DW_GATE = 2, VH_DW_GELU = 3, VH_DW_RESID_ADD = 4 };
+enum vh_dw_mode { VH_DW_BIAS = 0, VH_DW_RESID = 1, VH_DW_GATE = 2, VH_DW_GELU = 3, VH_DW_RESID_ADD = 4,
+                  VH_DW_GATE_POS = 5 };
 
 typedef struct {
     const void* x;
@@ -265,6 +271,12 @@ typedef struct {
      * pixel tile, the sum over the tile of y^2 per channel, with y as stored (the statistics
      * pass of a GRN that follows, see vh_grn_apply_fwd).  Written, not accumulated. */
     float* sumsq;
+    /* VH_DW_GATE_POS only (NULL / 0 otherwise): the second depthwise convolution's weight fp32
+     * [C, pos_ksize, pos_ksize], bias fp32 [C] and output [B, H, W, C] of `dtype`. */
+    const float* pos_weight;
+    const float* pos_bias;
+    void* pos_y;
+    int32_t pos_ksize;
 } vh_dwconv_args;
 
 int vh_dwconv_fwd(const vh_dwconv_args* args, vh_stream_t stream);

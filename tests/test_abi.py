@@ -195,12 +195,37 @@ def test_harness_entry_points_validate_without_a_gpu():
     assert lib.vh_grn_apply_fwd(p, 1, p, 1, p, p, 1e-6, p, p, 1, 2, 4, 4, 4096, None) == -2
 
 
+def test_dwconv_gate_pos_validates_without_a_gpu():
+    """The fused local-features + position mode rejects missing operands, other dtypes, other
+    kernel sizes and images that a CTA does not hold whole, before any CUDA call."""
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+
+    def args(**kw):
+        a = dict(x=p, gate=p, weight=p, bias=p, y=p + 4096, dtype=1, mode=5, ksize=7, batch=2, height=14,
+                 width=14, channels=32, gate_dtype=0, sumsq=None, pos_weight=p, pos_bias=p, pos_y=p + 8192,
+                 pos_ksize=5)
+        a.update(kw)
+        return _lib.VhDwconvArgs(**a)
+
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(pos_y=None)), None) == -1
+    assert "pos_y" in _err(lib)
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(dtype=0)), None) == -3
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(pos_ksize=3)), None) == -2
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(height=56, width=56)), None) == -2
+    assert "14 x 14 or 7 x 7" in _err(lib)
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(pos_y=p)), None) == -1  # aliases x
+    assert lib.vh_dwconv_fwd(ctypes.byref(args(mode=6)), None) == -1
+
+
 def test_dwconv_tile_count_query():
     from visionhope_b200 import _lib
 
     lib = _lib.load()
     assert lib.vh_dwconv_tiles(56, 56) == 16   # 14 x 14 tiles
     assert lib.vh_dwconv_tiles(14, 14) == 1
-    assert lib.vh_dwconv_tiles(7, 7) == 1      # one 8 x 8 tile
+    assert lib.vh_dwconv_tiles(7, 7) == 1      # whole images, four per CTA
     assert lib.vh_dwconv_tiles(32, 32) == 4    # 16 x 16 tiles
     assert lib.vh_dwconv_tiles(0, 5) == 0

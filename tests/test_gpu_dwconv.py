@@ -145,6 +145,46 @@ def test_dwconv_gelu_tile_sums(shape, dt, cuda):
         assert rel_err(ss[:, 0].double().cpu().numpy(), yd[:, :, :14, :14].pow(2).sum(dim=(2, 3)).cpu().numpy()) < 1e-6
 
 
+@pytest.mark.parametrize("shape", [(5, 128, 14, 14), (3, 40, 14, 14), (6, 256, 7, 7), (3, 24, 7, 7)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_dwconv_gate_pos_matches_gate_then_bias(shape, cuda):
+    """The fused local features + output position term ("gate_pos") is bit-identical to the
+    gated 7x7 call followed by the 5x5 bias call on its output (same operands, same order of
+    sums), for whole 14 x 14 images and four 7 x 7 images per CTA, with batches and channel
+    counts that leave CTAs partly empty."""
+    from visionhope_b200.utils.dwconv import depthwise_fused, gate_pos_ok
+
+    B, C, H, W = shape
+    torch.manual_seed(zlib.crc32(repr(shape).encode()))
+    conv, pos = (torch.nn.Conv2d(C, C, 7, padding=3, groups=C).to(cuda),
+                 torch.nn.Conv2d(C, C, 5, padding=2, groups=C).to(cuda))
+    with torch.no_grad():
+        conv.bias.normal_(0, 0.3)
+        pos.bias.normal_(0, 0.3)
+    x = torch.randn(B, C, H, W, device=cuda).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    gate = torch.randn_like(x)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        assert gate_pos_ok(x, conv, pos)
+        y, p = depthwise_fused(x, conv, "gate_pos", gate=gate, pos_conv=pos)
+        y0 = depthwise_fused(x, conv, "gate", gate=gate)
+        p0 = depthwise_fused(y0, pos, "bias")
+    assert torch.equal(y, y0)
+    assert torch.equal(p, p0)
+    assert rel_err(p.double().cpu().numpy(), _expected(y0, pos, "bias", None).cpu().numpy()) < 4e-3
+
+
+def test_dwconv_gate_pos_rejects_other_shapes(cuda):
+    from visionhope_b200.utils.dwconv import depthwise_fused, gate_pos_ok
+
+    conv = torch.nn.Conv2d(32, 32, 7, padding=3, groups=32).to(cuda)
+    pos = torch.nn.Conv2d(32, 32, 5, padding=2, groups=32).to(cuda)
+    x = torch.randn(1, 32, 28, 28, device=cuda).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        assert not gate_pos_ok(x, conv, pos)
+        with pytest.raises(RuntimeError):
+            depthwise_fused(x, conv, "gate_pos", gate=torch.randn_like(x), pos_conv=pos)
+
+
 def test_dwconv_sumsq_needs_gelu(cuda):
     from visionhope_b200.utils.dwconv import depthwise_fused
 

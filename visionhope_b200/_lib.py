@@ -59,7 +59,8 @@ class VhDwconvArgs(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("gate", c_void_p), ("weight", c_void_p), ("bias", c_void_p),
                 ("y", c_void_p), ("dtype", c_int32), ("mode", c_int32), ("ksize", c_int32),
                 ("batch", c_int32), ("height", c_int32), ("width", c_int32), ("channels", c_int32),
-                ("gate_dtype", c_int32), ("sumsq", c_void_p)]
+                ("gate_dtype", c_int32), ("sumsq", c_void_p), ("pos_weight", c_void_p), ("pos_bias", c_void_p),
+                ("pos_y", c_void_p), ("pos_ksize", c_int32)]
 
 
 _lib = None

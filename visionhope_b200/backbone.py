@@ -20,7 +20,7 @@ from .operator import VisionHOPEOperator
 from .srnl import SRNL, trunc_normal_
 from .utils.grn import GlobalResponseNorm
 from .utils.bias_act import add_cast, add_cast_ok, bias_act, stem_conv, stem_conv_ok
-from .utils.dwconv import depthwise_fused, fusable
+from .utils.dwconv import depthwise_fused, fusable, gate_pos_ok
 from .utils.grn_cuda import grn_apply, grn_apply_ok, grn_forward
 from .utils.inference import cache_half_weights, linear_cached, norm_linear_cached
 from .utils.layer_norm_cuda import add_layernorm_rows, layernorm_rows
@@ -325,29 +325,39 @@ class VisionHOPEBlock(nn.Module):
         return None if inner is None else inner.permute(0, 3, 1, 2)
 
     def _local_features(self, x, inner=None):
+        return self._local_and_position(x, inner, False)[0]
+
+    def _local_and_position(self, x, inner, want_position):
+        """(x_local, position term or None).  With ``want_position``, the gated local features
+        and the output position term conv5x5(x_local) + b come from one depthwise kernel where
+        it applies (whole 14 x 14 or 7 x 7 images, bf16); the term is NHWC in x_local's dtype."""
         if inner is None:
             inner = pointwise(self.proj_in, x)
         if self.local_mode == "gated_dwconv7":
             gate = pointwise(self.local_gate, inner)
             if fusable(inner, self.local_conv) and gate.dtype == inner.dtype:
-                return depthwise_fused(inner, self.local_conv, "gate", gate=gate)
-            return inner + torch.sigmoid(gate) * self.local_conv(inner)
+                if (want_position and self.local_position is not None
+                        and gate_pos_ok(inner, self.local_conv, self.local_position)):
+                    x_local, pos = depthwise_fused(inner, self.local_conv, "gate_pos", gate=gate,
+                                                   pos_conv=self.local_position)
+                    return x_local, pos.permute(0, 2, 3, 1)
+                return depthwise_fused(inner, self.local_conv, "gate", gate=gate), None
+            return inner + torch.sigmoid(gate) * self.local_conv(inner), None
         conv = self.local_act(self.local_conv(inner))
-        return conv if self.local_mode == "silu_dwconv" else inner + conv
+        return (conv if self.local_mode == "silu_dwconv" else inner + conv), None
 
     def spatial_branch(self, x, *, inner=None):
         """The mixer branch on x = norm1(block input); ``inner`` = proj_in(x) when the caller
         already computed it (then x only supplies the memory format)."""
         channels_last = x.is_contiguous(memory_format=torch.channels_last)
-        x_local = self._local_features(x, inner)
+        x_local, lepe = self._local_and_position(x, inner, self._inference_prepared)
         if self._inference_prepared:
             path, _ = self.operator._inference_path(x_local)
             if path != "ordinary":
                 # The scan launch adds the output position term and writes the dtype the output
                 # projection consumes: (out + lepe) rounded once, as the reference's fp32 add
                 # followed by autocast's cast.
-                lepe = None
-                if self.local_position is not None:
+                if lepe is None and self.local_position is not None:
                     if fusable(x_local, self.local_position):
                         lepe = depthwise_fused(x_local, self.local_position, "bias").permute(0, 2, 3, 1)
                     else:

@@ -92,8 +92,8 @@ struct DwGeom {
 template <int K, int MODE, typename T, int TC, int RG, int R, bool MI = false>
 struct DwCenter {
     using G = DwGeom<K, TC, RG, R, MI>;
-    static constexpr bool kGate = MODE == VH_DW_GATE;
-    static constexpr bool kExact = std::is_same<T, float>::value && MODE == VH_DW_GATE;
+    static constexpr bool kGate = MODE == VH_DW_GATE || MODE == VH_DW_GATE_POS;
+    static constexpr bool kExact = std::is_same<T, float>::value && kGate;
     static constexpr size_t kPix = (size_t)G::TH * TC * kDwCG;  // elements per region
     static constexpr size_t kGateOffset = kExact ? kPix * 4 : 0;  // bytes
     static constexpr size_t kBytes = kGateOffset + (kGate ? kPix * sizeof(T) : 0);
@@ -105,7 +105,10 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, T* __restrict__ y,
                                                                 float* __restrict__ sumsq,
-                                                                int H, int W, int C, int tiles_w, int B) {
+                                                                int H, int W, int C, int tiles_w, int B,
+                                                                const float* __restrict__ pos_w,
+                                                                const float* __restrict__ pos_b,
+                                                                T* __restrict__ pos_y) {
     using G = DwGeom<K, TC, RG, R, MI>;
     constexpr int TH = G::TH, P = G::P, IW = G::IW, NT = G::NT, SR = G::SR;
     extern __shared__ __align__(16) float dw_smem[];
@@ -241,6 +244,11 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
 
     // GELU mode with `sumsq`: this thread's sums of y^2 (as stored) over its rows, 4 channels.
     float2 ss[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    // GATE_POS: this thread's outputs as stored (bf16-rounded), the position conv's input.
+    constexpr int KR = MODE == VH_DW_GATE_POS ? R : 1;
+    float2 keep[KR][2];
+#pragma unroll
+    for (int r = 0; r < KR; ++r) keep[r][0] = keep[r][1] = make_float2(0.f, 0.f);
     float2 bv[2];
     lds4(bs + 4 * q, bv);
     const int64_t off0 = img + ((int64_t)(oy0 + (MI ? 0 : r0)) * W + ox) * C + c, row = (int64_t)W * C;
@@ -250,7 +258,7 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
         if (!out_ok || oy >= H) break;
         const int64_t off = off0 + r * row;
         float2 o[2] = {fadd2(acc[r][0], bv[0]), fadd2(acc[r][1], bv[1])};
-        if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || MODE == VH_DW_GATE) {
+        if (MODE == VH_DW_RESID || MODE == VH_DW_RESID_ADD || CT::kGate) {
             // The centre value itself: from the staged tile when the input is bf16 (staged
             // exactly), else from the exact copy staged for the gated epilogue, or from global
             // memory.
@@ -269,7 +277,7 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
                 xc[0] = make_float2(t4.x, t4.y);
                 xc[1] = make_float2(t4.z, t4.w);
             }
-            if (MODE != VH_DW_GATE) {
+            if (!CT::kGate) {
                 o[0] = fadd2(xc[0], o[0]);
                 o[1] = fadd2(xc[1], o[1]);
             } else {
@@ -298,7 +306,71 @@ __global__ void __launch_bounds__(8 * TC * RG, (K == 7 && R >= 7) ? 2 : (K == 7 
             ss[0] = ffma2(o[0], o[0], ss[0]);
             ss[1] = ffma2(o[1], o[1], ss[1]);
         }
+        if constexpr (MODE == VH_DW_GATE_POS) {
+            keep[MODE == VH_DW_GATE_POS ? r : 0][0] = make_float2(round_bf16(o[0].x), round_bf16(o[0].y));
+            keep[MODE == VH_DW_GATE_POS ? r : 0][1] = make_float2(round_bf16(o[1].x), round_bf16(o[1].y));
+        }
         store4(y + off, make_float4(o[0].x, o[0].y, o[1].x, o[1].y));
+    }
+    if constexpr (MODE == VH_DW_GATE_POS) {
+        // The output position term: a K2 x K2 convolution of y (as stored) with its own weights
+        // and bias, from a copy of this CTA's outputs in shared memory.  The CTA holds whole
+        // images, so the copy's zero border is the convolution's zero padding, and the sums run
+        // in the order of the VH_DW_BIAS mode: bit-identical to that mode applied to y.
+        constexpr int K2 = 5, P2 = K2 / 2, SR2 = R + K2 - 1, IW2 = TC + K2 - 1;
+        constexpr int IH2 = MI ? RG * SR2 : TH + K2 - 1, OH = MI ? R : TH;
+        static_assert(IH2 * IW2 <= G::IH * IW, "the position input fits where the tile was staged");
+        static_assert(K2 <= K, "the position weights fit where the first weights were staged");
+        __syncthreads();  // every read of the staged tile, weights and bias is done
+        float* ps = xs;   // [IH2][IW2][32]
+        for (int i = tid; i < IH2 * IW2 * 8; i += NT) {
+            const int pix = i >> 3, py = pix / IW2, px = pix % IW2, ly = MI ? py % SR2 : py;
+            if (ly < P2 || ly >= P2 + OH || px < P2 || px >= P2 + TC)
+                *reinterpret_cast<float4*>(ps + pix * kDwCG + 4 * (i & 7)) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const int prow = MI ? rg * SR2 : r0;  // this thread's first row in the copy, less P2
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            *reinterpret_cast<float4*>(ps + ((prow + P2 + r) * IW2 + col + P2) * kDwCG + 4 * q) =
+                make_float4(keep[r][0].x, keep[r][0].y, keep[r][1].x, keep[r][1].y);
+        for (int i = tid; i < K2 * K2 * kDwCG; i += NT) {
+            const int tap = i / kDwCG, cc = i % kDwCG, ch = c0 + cc;
+            ws[i] = ch < C ? round_bf16(pos_w[(int64_t)ch * K2 * K2 + tap]) : 0.f;
+        }
+        if (tid < kDwCG) bs[tid] = c0 + tid < C ? round_bf16(pos_b[c0 + tid]) : 0.f;
+        __syncthreads();
+        float2 acc2[R][2];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc2[r][0] = acc2[r][1] = make_float2(0.f, 0.f);
+        const float* pt = ps + (prow * IW2 + col) * kDwCG + 4 * q;
+#pragma unroll
+        for (int kx = 0; kx < K2; ++kx) {
+            float2 wk[K2][2];
+#pragma unroll
+            for (int ky = 0; ky < K2; ++ky) lds4(wt + (ky * K2 + kx) * kDwCG, wk[ky]);
+#pragma unroll
+            for (int iy = 0; iy < R + K2 - 1; ++iy) {
+                float2 in[2];
+                lds4(pt + (iy * IW2 + kx) * kDwCG, in);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int ky = iy - r;
+                    if (ky >= 0 && ky < K2) {
+                        acc2[r][0] = ffma2(wk[ky][0], in[0], acc2[r][0]);
+                        acc2[r][1] = ffma2(wk[ky][1], in[1], acc2[r][1]);
+                    }
+                }
+            }
+        }
+        float2 bv2[2];
+        lds4(bs + 4 * q, bv2);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int oy = oy0 + (MI ? 0 : r0) + r;
+            if (!out_ok || oy >= H) break;
+            const float2 o0 = fadd2(acc2[r][0], bv2[0]), o1 = fadd2(acc2[r][1], bv2[1]);
+            store4(pos_y + off0 + r * row, make_float4(o0.x, o0.y, o1.x, o1.y));
+        }
     }
     if (MI && MODE == VH_DW_GELU && sumsq) {
         // Per-image channel sums in a fixed order (the columns of the image's row group; a row
@@ -347,7 +419,8 @@ int dw_launch(const vh_dwconv_args& a, cudaStream_t st) {
         return fail(VH_E_DEVICE, "depthwise conv: cannot reserve %zu bytes of shared memory", smem);
     dwconv_kernel<K, MODE, T, GT, TC, RG, R, MI><<<grid, G::NT, smem, st>>>(
         static_cast<const T*>(a.x), static_cast<const GT*>(a.gate), a.weight, a.bias, static_cast<T*>(a.y),
-        MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w, a.batch);
+        MODE == VH_DW_GELU ? a.sumsq : nullptr, a.height, a.width, a.channels, tiles_w, a.batch, a.pos_weight,
+        a.pos_bias, static_cast<T*>(a.pos_y));
     return launch_status("depthwise conv");
 }
 
@@ -383,9 +456,21 @@ int dw_k(const vh_dwconv_args& a, cudaStream_t st) {
     }
 }
 
+// The gated local features and the output position term in one pass: bf16, 7x7 then 5x5,
+// whole images per CTA (the 14 x 14 tile of a 14 x 14 image, or four 7 x 7 images).
+template <typename T>
+int dw_gate_pos(const vh_dwconv_args& a, cudaStream_t st) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        if (a.height == 7 && a.width == 7) return dw_launch<7, VH_DW_GATE_POS, T, T, 7, kDwMiImages, 7, true>(a, st);
+        return dw_launch<7, VH_DW_GATE_POS, T, T, 14, 2, 7>(a, st);
+    }
+    return fail(VH_E_DTYPE, "vh_dwconv_fwd: VH_DW_GATE_POS needs bf16");
+}
+
 template <typename T>
 int dw_mode(const vh_dwconv_args& a, cudaStream_t st) {
     switch (a.mode) {
+        case VH_DW_GATE_POS: return dw_gate_pos<T>(a, st);
         case VH_DW_BIAS: return dw_k<VH_DW_BIAS, T>(a, st);
         case VH_DW_RESID: return dw_k<VH_DW_RESID, T>(a, st);
         case VH_DW_GATE: return dw_k<VH_DW_GATE, T>(a, st);
@@ -418,6 +503,12 @@ void dw_attr_mode() {
 
 template <typename T>
 void dw_attr_t() {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<7, VH_DW_GATE_POS, T, T, 14, 2, 7>),
+                    DwCenter<7, VH_DW_GATE_POS, T, 14, 2, 7>::kSmem);
+        dw_attr_one(reinterpret_cast<const void*>(&dwconv_kernel<7, VH_DW_GATE_POS, T, T, 7, kDwMiImages, 7, true>),
+                    DwCenter<7, VH_DW_GATE_POS, T, 7, kDwMiImages, 7, true>::kSmem);
+    }
     dw_attr_mode<VH_DW_BIAS, T>();
     dw_attr_mode<VH_DW_RESID, T>();
     dw_attr_mode<VH_DW_GATE, T>();
@@ -453,9 +544,22 @@ extern "C" int vh_dwconv_fwd(const vh_dwconv_args* a, vh_stream_t stream) {
     clear_error();
     if (!a) return fail(VH_E_ARG, "vh_dwconv_fwd: null args");
     if (!a->x || !a->weight || !a->bias || !a->y ||
-        ((a->mode == VH_DW_GATE || a->mode == VH_DW_RESID_ADD) && !a->gate))
+        ((a->mode == VH_DW_GATE || a->mode == VH_DW_GATE_POS || a->mode == VH_DW_RESID_ADD) && !a->gate))
         return fail(VH_E_ARG, "vh_dwconv_fwd: null pointer argument");
-    if (a->mode < VH_DW_BIAS || a->mode > VH_DW_RESID_ADD) return fail(VH_E_ARG, "vh_dwconv_fwd: bad mode %d", a->mode);
+    if (a->mode < VH_DW_BIAS || a->mode > VH_DW_GATE_POS) return fail(VH_E_ARG, "vh_dwconv_fwd: bad mode %d", a->mode);
+    if (a->mode == VH_DW_GATE_POS) {
+        if (!a->pos_weight || !a->pos_bias || !a->pos_y)
+            return fail(VH_E_ARG, "vh_dwconv_fwd: VH_DW_GATE_POS needs pos_weight, pos_bias and pos_y");
+        if (a->dtype != VH_BF16) return fail(VH_E_DTYPE, "vh_dwconv_fwd: VH_DW_GATE_POS needs bf16");
+        if (a->ksize != 7 || a->pos_ksize != 5)
+            return fail(VH_E_SHAPE, "vh_dwconv_fwd: VH_DW_GATE_POS takes ksize 7 and pos_ksize 5");
+        if (!((a->height == 14 && a->width == 14) || (a->height == 7 && a->width == 7)))
+            return fail(VH_E_SHAPE, "vh_dwconv_fwd: VH_DW_GATE_POS needs 14 x 14 or 7 x 7 images (got %d x %d)",
+                        a->height, a->width);
+        if (!aligned(a->pos_y, 16)) return fail(VH_E_ALIGN, "vh_dwconv_fwd: pos_y must be 16-byte aligned");
+        if (a->pos_y == a->x || a->pos_y == a->gate || a->pos_y == a->y)
+            return fail(VH_E_ARG, "vh_dwconv_fwd: pos_y must not alias x, gate or y");
+    }
     if (a->mode == VH_DW_RESID_ADD && a->gate_dtype != VH_F32 && a->gate_dtype != VH_BF16)
         return fail(VH_E_DTYPE, "vh_dwconv_fwd: the addend must be fp32 or bf16");
     if (a->mode == VH_DW_RESID_ADD && a->dtype == VH_BF16 && a->gate_dtype == VH_F32)

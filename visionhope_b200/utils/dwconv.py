@@ -9,7 +9,7 @@ import torch
 from .. import _lib
 from .cuda import on_tensor_device
 
-MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3, "resid_add": 4}
+MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3, "resid_add": 4, "gate_pos": 5}
 
 
 def fusable(x, conv):
@@ -27,20 +27,33 @@ def fusable(x, conv):
             and conv.padding == (k // 2, k // 2) and conv.dilation == (1, 1) and conv.bias is not None)
 
 
+def gate_pos_ok(x, conv, pos_conv):
+    """Whether the gated 7x7 ``conv`` and the 5x5 ``pos_conv`` on its output can run as one
+    "gate_pos" call: both fusable, bf16, and whole 14 x 14 or 7 x 7 images (one CTA holds an
+    image, so the second convolution reads the first one's output from shared memory)."""
+    H, W = x.shape[-2:]
+    return (x.dtype == torch.bfloat16 and (H, W) in ((14, 14), (7, 7)) and conv.kernel_size == (7, 7)
+            and pos_conv.kernel_size == (5, 5) and fusable(x, conv) and fusable(x, pos_conv))
+
+
 @on_tensor_device
-def depthwise_fused(x, conv, mode, gate=None, addend=None, with_sumsq=False):
+def depthwise_fused(x, conv, mode, gate=None, addend=None, with_sumsq=False, pos_conv=None):
     """Apply depthwise ``conv`` to channels-last NCHW ``x`` with epilogue ``mode``:
     "bias": conv(x) + b;  "resid": s + (conv(s) + b) with s = x, or s = x + addend when an
     addend (fp32/bf16, x's shape) is given;  "gate": x + sigmoid(gate) * (conv(x) + b);
-    "gelu": h = gelu(x), gelu(h + conv(h) + b).  Returns a channels-last tensor of x's dtype,
-    and with ``with_sumsq`` ("gelu" only) also the fp32 [B, tiles, C] sums of y^2 per pixel
-    tile that a following GRN needs (``grn_cuda.grn_apply``)."""
+    "gelu": h = gelu(x), gelu(h + conv(h) + b);  "gate_pos": y as "gate", and also
+    pos_conv(y) + pos_b (see ``gate_pos_ok``), returned as a second tensor.  Returns a
+    channels-last tensor of x's dtype, and with ``with_sumsq`` ("gelu" only) also the fp32
+    [B, tiles, C] sums of y^2 per pixel tile that a following GRN needs
+    (``grn_cuda.grn_apply``)."""
     _lib.ensure_device(x)
     B, C, H, W = x.shape
     if mode not in MODES:
         raise ValueError(f"unknown depthwise epilogue {mode!r}")
     gate_dtype = 0
-    if mode == "gate":
+    if mode == "gate_pos" and (pos_conv is None or not gate_pos_ok(x, conv, pos_conv)):
+        raise RuntimeError("gate_pos needs bf16 14x14 or 7x7 images, a 7x7 conv and a 5x5 pos_conv")
+    if mode in ("gate", "gate_pos"):
         if gate is None or gate.shape != x.shape or gate.dtype != x.dtype:
             raise RuntimeError("the gated epilogue needs a gate of x's shape and dtype")
         gate = gate.contiguous(memory_format=torch.channels_last)
@@ -58,8 +71,16 @@ def depthwise_fused(x, conv, mode, gate=None, addend=None, with_sumsq=False):
         if mode != "gelu":
             raise RuntimeError("tile statistics go with the gelu epilogue")
         sumsq = torch.empty((B, int(_lib.load().vh_dwconv_tiles(H, W)), C), device=x.device, dtype=torch.float32)
+    pw = pb = pos = None
+    if mode == "gate_pos":
+        pw = pos_conv.weight.detach().float().contiguous()
+        pb = pos_conv.bias.detach().float().contiguous()
+        pos = torch.empty_like(x, memory_format=torch.channels_last)
     args = _lib.VhDwconvArgs(x.data_ptr(), _lib.ptr(gate), w.data_ptr(), b.data_ptr(), y.data_ptr(),
                              _lib.dtype_code(x.dtype), MODES[mode], conv.kernel_size[0], B, H, W, C, gate_dtype,
-                             _lib.ptr(sumsq))
+                             _lib.ptr(sumsq), _lib.ptr(pw), _lib.ptr(pb), _lib.ptr(pos),
+                             5 if mode == "gate_pos" else 0)
     _lib.check(_lib.load().vh_dwconv_fwd(args, _lib.stream_handle(x.device)), "vh_dwconv_fwd")
+    if mode == "gate_pos":
+        return y, pos
     return (y, sumsq) if with_sumsq else y
