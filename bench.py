@@ -186,25 +186,32 @@ def run_cpu(args, steps, warmup):
 
 # ----------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region (every 50 ms; entering waits,
-    up to 5 s, for the first sample, so that the sampler runs before the timed region starts)."""
+    """nvidia-smi clock/throttle samples of every visible GPU during the timed region (every
+    ``interval_ms``; entering waits, up to 5 s, for the first sample, so that the sampler runs
+    before the timed region starts).  Under torchrun only rank 0 samples (``enabled``), at a
+    longer interval: one nvidia-smi per rank, each polling all eight GPUs, took driver time
+    from the ranks' own launches."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, enabled=True, interval_ms=50):
+        self.enabled = enabled
+        self.interval_ms = interval_ms
         self.proc = None
         self.path = None
         self.skip = 0
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", str(self.interval_ms)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
         t0 = time.time()
@@ -486,7 +493,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
-        with ClockSampler() as clk:
+        with ClockSampler(enabled=rank == 0, interval_ms=50 if world == 1 else 100) as clk:
             for a, b in evs:
                 flush.fill_(1.0)
                 a.record()
