@@ -487,13 +487,16 @@ def run_ours(args, world, rank, local):
 
         for _ in range(args.warmup):
             step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
         with ClockSampler(enabled=rank == 0, interval_ms=50 if world == 1 else 100) as clk:
+            # The barrier comes after the sampler has started (rank 0 waits for its first
+            # sample): ranks that entered the timed loop earlier would otherwise time their
+            # all-gather waiting for rank 0.
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
             for a, b in evs:
                 flush.fill_(1.0)
                 a.record()
