@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--model", default="visionhope_tiny")
-    ap.add_argument("--cpu-sample", type=int, default=2, help="images per CPU baseline step")
+    ap.add_argument("--cpu-sample", type=int, default=8, help="images per CPU baseline step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-scan", action="store_true",
                     help="time only the fused SRNL operator at the stage-1 shape (profiling aid)")
@@ -79,50 +79,47 @@ def config(args, world):
 
 
 # ----------------------------------------------------------------------------------------
-# CPU stand-in for the reference: the reference has no CPU SRNL path (models/srnl.py:113-114),
-# so SRNL runs on the oracle port (oracle/vhope_oracle.c, float arithmetic, OpenMP); LayerNorm
-# and GRN use the reference's own CPU formulas (models/layers.py:25-35, utils/grn.py:26-38).
+# The reference on the host CPU: the reference's own modules (staged unmodified by
+# oracle/build_ref.py, imported by oracle/refmodel.py), prepared for inference exactly as on a
+# GPU.  They have no CPU SRNL recurrence (SRNL._run rejects CPU tensors, models/srnl.py:113-114),
+# so that one method is routed to the oracle's float port of the reference kernels
+# (oracle/vhope_oracle.c, OpenMP over chains); everything else -- the four serialized scans,
+# W_q, the PyTorch direction fusion of the ordinary path (operator.py:121-139), LayerNorm's
+# F.layer_norm, grn_reference, the convolutions -- is the reference's own CPU code.
+def reference_cpu_model(name, **kwargs):
+    """(reference namespace, prepared reference model on CPU), weights from seed 3."""
+    from oracle import refmodel
+
+    ref = refmodel.load("native")  # on CPU none of the reference's kernels is ever reached
+    torch.manual_seed(3)
+    model = ref.create_model(name, **kwargs).to(memory_format=torch.channels_last)
+    ref.prepare_for_inference(model)
+    return ref, model
+
+
 @contextlib.contextmanager
-def cpu_reference_patches():
+def oracle_srnl(ref):
+    """Run the reference SRNL module's recurrence (SRNL._run) on the oracle's float port."""
     import numpy as np
-    import torch.nn.functional as F
 
     from oracle import oracle as orc
-    from visionhope_b200 import backbone, operator
-    from visionhope_b200.utils import grn as grn_mod
 
-    saved = (backbone.LayerNorm2d.forward, grn_mod.GlobalResponseNorm.forward,
-             operator.VisionHOPEOperator._forward_fast, operator.VisionHOPEOperator._inference_path)
+    saved = ref.SRNL._run
 
-    def ln_forward(self, x):
-        return F.layer_norm(x.permute(0, 2, 3, 1), (self.weight.numel(),), self.weight, self.bias,
-                            self.eps).permute(0, 3, 1, 2)
+    def run(self, x, queries, spatial_shape):
+        height, width = spatial_shape if spatial_shape is not None else (None, None)
+        chunk = self.chunk_size if self.chunk_size is not None else (width or 64)
+        chunks = [chunk] * x.shape[1]
+        if self.chunk_size is None and spatial_shape is not None:
+            chunks = [width, width, height, height]
+        y = orc.srnl_sequence([m.detach() for m in self.initial_memories], x, queries, chunks, use_f32=True)
+        return torch.from_numpy(y.astype(np.float32))
 
-    def grn_forward(self, x):
-        return grn_mod.grn_reference(x, self.gamma, self.beta, self.eps)
-
-    def fast(self, x, path, *, addend=None, final_dtype=None):
-        H, W = x.shape[-2:]
-        seq_hw = x.flatten(2).transpose(1, 2)
-        xs = self.serialize(x, seq_hw)
-        q = self.project_queries(seq_hw, H, W)
-        out = orc.srnl_spatial([m.detach() for m in self.srnl.initial_memories], xs, q,
-                               self.d_skip.detach(), self._fusion_weights(), H, W, self.head_dim,
-                               use_f32=True)
-        out = torch.from_numpy(out.astype(np.float32))
-        if addend is not None:
-            out = out + addend
-        return out if final_dtype is None else out.to(final_dtype)
-
-    backbone.LayerNorm2d.forward = ln_forward
-    grn_mod.GlobalResponseNorm.forward = grn_forward
-    operator.VisionHOPEOperator._forward_fast = fast
-    operator.VisionHOPEOperator._inference_path = lambda self, x: ("spatial", None)
+    ref.SRNL._run = run
     try:
         yield
     finally:
-        (backbone.LayerNorm2d.forward, grn_mod.GlobalResponseNorm.forward,
-         operator.VisionHOPEOperator._forward_fast, operator.VisionHOPEOperator._inference_path) = saved
+        ref.SRNL._run = saved
 
 
 def build_model(name, device):
@@ -163,15 +160,15 @@ def cpu_threads():
 
 
 def run_cpu(args, steps, warmup):
-    """Time the CPU stand-in: returns (images/s, per-step seconds list, cores, sample text)."""
+    """Time the reference on the host CPU: returns (images/s, per-step seconds, cores, sample)."""
     cores = cpu_threads()
     torch.set_num_threads(cores)
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    model = build_model(args.model, torch.device("cpu"))
+    ref, model = reference_cpu_model(args.model)
     gen = torch.Generator().manual_seed(3)
     x = torch.randn(args.cpu_sample, 3, IMG, IMG, generator=gen).contiguous(memory_format=torch.channels_last)
     times = []
-    with cpu_reference_patches(), torch.inference_mode():
+    with oracle_srnl(ref), torch.inference_mode():
         for i in range(warmup + steps):
             t0 = time.perf_counter()
             model(x)
@@ -179,8 +176,9 @@ def run_cpu(args, steps, warmup):
             if i >= warmup:
                 times.append(dt)
     ips = args.cpu_sample * len(times) / sum(times)
-    sample = (f"{args.cpu_sample} images/step of the same {args.model} forward at {IMG}x{IMG}, fp32 on CPU "
-              f"(SRNL: oracle port, float, OpenMP; LN/GRN/convs: PyTorch CPU), {steps} timed steps")
+    sample = (f"{args.cpu_sample} image(s)/step of the same {args.model} forward at {IMG}x{IMG}, fp32 on "
+              f"{cores} host threads: the reference's own modules (prepared), SRNL recurrence on the oracle's "
+              f"float port (the reference has no CPU SRNL), {steps} timed steps after {warmup} warm-up")
     return ips, times, cores, sample
 
 
@@ -194,7 +192,7 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,pci.bus_id")
 
     def __init__(self, enabled=True, interval_ms=50):
         self.enabled = enabled
@@ -230,30 +228,56 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self, devices):
+    def summary(self, bus_ids):
+        """Clock record of the GPUs the job ran on, named by PCI bus id ("domain:bus:device",
+        from every rank's own device), so GPUs of the node that the job does not use never
+        enter the figures; per-GPU medians are listed so an idle GPU would show."""
         if self.proc is None or not self.path:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        mhz, mx, reasons, power = [], [], set(), []
+        mhz, mx, reasons, power, per_gpu = [], [], set(), [], {}
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in Path(self.path).read_text().splitlines()[self.skip:]:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
+                continue
+            bus = normalize_bus_id(parts[9])
+            if bus not in bus_ids:
                 continue
             try:
-                if int(parts[0]) not in devices:
-                    continue
                 mhz.append(float(parts[1]))
                 mx.append(float(parts[2]))
                 power.append(float(parts[3]))
             except ValueError:
                 continue
+            per_gpu.setdefault(bus, []).append(float(parts[1]))
             for n, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
                 "power_w_max": max(power) if power else None, "samples": len(mhz),
-                "reasons": sorted(reasons)}
+                "per_gpu_sm_mhz": {b: statistics.median(v) for b, v in sorted(per_gpu.items())},
+                "gpus": sorted(bus_ids), "reasons": sorted(reasons)}
+
+
+def normalize_bus_id(text):
+    """nvidia-smi's "00000000:1B:00.0" -> "0:1b:0" (domain, bus and device as hex numbers)."""
+    try:
+        dom, bus, rest = text.strip().split(":")
+        return f"{int(dom, 16):x}:{int(bus, 16):x}:{int(rest.split('.')[0], 16):x}"
+    except ValueError:
+        return text.strip().lower()
+
+
+def job_bus_ids(device, world):
+    """PCI bus ids of the GPUs of every rank of the job (one all_gather at set-up)."""
+    p = torch.cuda.get_device_properties(device)
+    mine = f"{p.pci_domain_id:x}:{p.pci_bus_id:x}:{p.pci_device_id:x}"
+    if world == 1:
+        return {mine}
+    ids = [None] * world
+    dist.all_gather_object(ids, mine)
+    return set(ids)
 
 
 def measure_ffma_peak(device):
@@ -462,6 +486,7 @@ def run_ours(args, world, rank, local):
 
     model = build_model(args.model, device)
     sync_model(model, world)
+    bus_ids = job_bus_ids(device, world)
     static_in = rank_inputs(args.batch, rank, device)
 
     def fwd():
@@ -508,7 +533,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
         ms_max = max_over_ranks(ms, device, world)
-        clocks = clk.summary(set(range(torch.cuda.device_count())) if world > 1 else {device.index})
+        clocks = clk.summary(bus_ids)
 
         # ---- end to end: pinned host batch in, logits out, every step inside the timed run ----
         # A serving pipeline: batch i+1 crosses PCIe on a copy stream into a staging buffer
@@ -594,7 +619,11 @@ def main():
         if args.impl == "reference":
             if rank != 0:
                 return
-            ips, times, cores, sample = run_cpu(args, args.steps, args.warmup)
+            try:
+                ips, times, cores, sample = run_cpu(args, args.steps, args.warmup)
+            except FileNotFoundError as exc:  # the reference package was not staged with the repo
+                print(json.dumps({"impl": "reference", "unavailable": str(exc)}), flush=True)
+                return
             line = {"metric": METRIC, "value": ips, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(times),
                     "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -621,9 +650,12 @@ def main():
         result = run_ours(args, world, rank, local)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
-                ips, times, cores, sample = run_cpu(args, steps=2, warmup=1)
-                result["cpu_baseline"] = {"value": ips, "unit": UNIT, "cores": cores, "kind": "port",
-                                          "sample": sample}
+                try:
+                    ips, times, cores, sample = run_cpu(args, steps=5, warmup=1)
+                    result["cpu_baseline"] = {"value": ips, "unit": UNIT, "cores": cores, "kind": "port",
+                                              "sample": sample}
+                except FileNotFoundError as exc:
+                    result["cpu_baseline"] = {"value": None, "unavailable": str(exc)}
             print(json.dumps(result), flush=True)
     finally:
         if world > 1 and dist.is_initialized():

@@ -192,16 +192,6 @@ int vh_grn_fwd(const void* x, int32_t x_dtype, const float* gamma, const float* 
                void* y, int32_t y_dtype, float* gx, float* inv_den, void* workspace, int64_t workspace_bytes,
                int32_t batch, int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
 
-/* GRN that allocates nothing (no counterpart in the reference).  Same result as vh_grn_fwd,
- * for callers that cannot allocate device memory when they run -- plugin or serving hosts
- * whose op interface provides only input and output buffers, and deployments that fix their
- * device memory at start-up.  The partial sums live in a 4 MiB array built into the library
- * (held on every device that loads it until the process exits), so batch * channels must not
- * exceed 1,048,576; larger calls are rejected with VH_E_RANGE.  The first call on each device
- * looks up that array's device address once (make that first call before any stream capture).
- * All calls share the one array: calls that may overlap on the GPU (different streams, or
- * different host threads on one device) race and must be serialized by the caller; the array
- * keeps the last call's contents, which no call relies on. */
 /* GRN from precomputed statistics: the apply pass of vh_grn_fwd when the sums of x^2 per
  * (image, channel) were produced with x itself (vh_dwconv_fwd's `sumsq`).  sumsq: fp32
  * [B, nparts, C], sums over disjoint pixel slices of each image, added in slice order;
@@ -213,9 +203,25 @@ int vh_grn_apply_fwd(const void* x, int32_t x_dtype, const float* sumsq, int32_t
                      int32_t y_dtype, int32_t batch, int32_t height, int32_t width, int32_t channels,
                      vh_stream_t stream);
 
+/* GRN that allocates nothing (no counterpart in the reference).  Same result as vh_grn_fwd,
+ * for callers that cannot allocate device memory when they run -- plugin or serving hosts
+ * whose op interface provides only input and output buffers, and deployments that fix their
+ * device memory at start-up.  The partial sums live in a 4 MiB array built into the library
+ * (held on every device that loads it until the process exits), so batch * channels must not
+ * exceed 1,048,576; larger calls are rejected with VH_E_RANGE.  The first call on each device
+ * looks up that array's device address once (make that first call before any stream capture).
+ * All calls share the one array: calls that may overlap on the GPU (different streams, or
+ * different host threads on one device) race and must be serialized by the caller; the array
+ * keeps the last call's contents, which no call relies on.  The looked-up address is kept for
+ * the life of the process: after cudaDeviceReset, or after the device's primary context is
+ * destroyed and created again, the array may sit at another address, so such a caller must
+ * call vh_grn_noalloc_reset() (on any thread) before its next call. */
 int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma, const float* beta,
                        float eps, float* y, float* gx, float* inv_den, int32_t batch,
                        int32_t height, int32_t width, int32_t channels, vh_stream_t stream);
+/* Forget the device addresses vh_grn_fwd_noalloc looked up (see above); the next call on
+ * each device looks its array up again.  No counterpart in the reference. */
+void vh_grn_noalloc_reset(void);
 
 /* ---------------------------------------------------------------------------------------
  * LayerNorm over the channel axis of channels-last rows, fp32 output; replaces the Triton

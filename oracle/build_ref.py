@@ -16,6 +16,13 @@ extensions, run on a B200.  This recipe:
 
 The reference's own JIT loaders are not called; only the build flags it uses
 (``-O3 --use_fast_math``) are mirrored, plus an explicit ``-gencode`` for sm_100a.
+
+``stage_python`` also copies the reference's Python package, unmodified (its ``models/``
+and ``utils/`` trees with the kernel sources they read at import, ``inference/prepare.py``),
+into ``oracle/_ref/pyref/visionhope/`` (git-ignored, like the built kernels), so that tests
+on the GPU box, where no reference checkout exists, can run the reference's own modules:
+with its own kernels (``oracle/refmodel.py``, mode "native") and over this repository's
+drop-in modules (mode "dropin").
 Nothing in the product imports this module or its outputs.
 """
 from __future__ import annotations
@@ -26,17 +33,24 @@ import tempfile
 import types
 from pathlib import Path
 
-REF_ROOT = Path(os.environ.get("VHOPE_REFERENCE", "/root/reference"))
+# The reference checkout: the VHOPE_REFERENCE environment variable (no default location).
+REF_ROOT = Path(os.environ["VHOPE_REFERENCE"]) if os.environ.get("VHOPE_REFERENCE") else None
 OUT_DIR = Path(__file__).resolve().parent / "_ref"
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def _install_reference():
-    import torch
-
     base = tempfile.mkdtemp(prefix="vhref_")
     os.symlink(REF_ROOT, os.path.join(base, "visionhope"))
     sys.path.insert(0, base)
+    install_timm_shim()
+
+
+def install_timm_shim():
+    """timm is not installed; the reference uses only these five names from it
+    (trunc_normal_, DropPath, register_model and the ImageNet mean/std)."""
+    import torch
+
     if "timm" not in sys.modules:
         timm = types.ModuleType("timm")
         models = types.ModuleType("timm.models")
@@ -108,8 +122,8 @@ def build_parallel(workers=None):
     import concurrent.futures as cf
     import multiprocessing as mp
 
-    if not REF_ROOT.is_dir():
-        raise FileNotFoundError(f"reference tree not found at {REF_ROOT}")
+    if REF_ROOT is None or not REF_ROOT.is_dir():
+        raise FileNotFoundError(f"reference tree not found (VHOPE_REFERENCE={REF_ROOT})")
     _install_reference()
     names = _names()
     workers = workers or max(1, min(len(names), (os.cpu_count() or 2) // 2))
@@ -121,8 +135,8 @@ def build_parallel(workers=None):
 
 
 def build(only=None):
-    if not REF_ROOT.is_dir():
-        raise FileNotFoundError(f"reference tree not found at {REF_ROOT}")
+    if REF_ROOT is None or not REF_ROOT.is_dir():
+        raise FileNotFoundError(f"reference tree not found (VHOPE_REFERENCE={REF_ROOT})")
     _install_reference()
     from torch.utils.cpp_extension import load, load_inline
 
@@ -154,20 +168,53 @@ def build(only=None):
     return built
 
 
+PYREF_DIR = OUT_DIR / "pyref"
+_STAGED = ("__init__.py", "models", "utils", "inference/__init__.py", "inference/prepare.py")
+
+
+def stage_python():
+    """Copy the reference's Python package (unmodified) into ``oracle/_ref/pyref/visionhope``."""
+    import shutil
+
+    if REF_ROOT is None or not REF_ROOT.is_dir():
+        raise FileNotFoundError(f"reference tree not found (VHOPE_REFERENCE={REF_ROOT})")
+    dst = PYREF_DIR / "visionhope"
+    if dst.exists():
+        shutil.rmtree(dst)
+    keep = shutil.ignore_patterns("__pycache__", "*.pyc", "*.md", "*.png")
+    for rel in _STAGED:
+        src = REF_ROOT / rel
+        out = dst / rel
+        out.parent.mkdir(parents=True, exist_ok=True)
+        if src.is_dir():
+            shutil.copytree(src, out, ignore=keep)
+        else:
+            shutil.copy2(src, out)
+    return dst
+
+
+_loaded = {}
+
+
 def load_built(name):
-    """Import a previously built reference extension from ``oracle/_ref/<name>/``."""
+    """Import a previously built reference extension from ``oracle/_ref/<name>/`` (once per
+    process; an extension module cannot be initialised twice)."""
     import importlib.util
 
     import torch  # noqa: F401  (the extension links against libtorch)
 
+    if name in _loaded:
+        return _loaded[name]
     path = OUT_DIR / name / f"{name}.so"
     if not path.is_file():
         raise FileNotFoundError(f"reference extension {name} not built at {path}")
     spec = importlib.util.spec_from_file_location(name, path)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
+    _loaded[name] = module
     return module
 
 
 if __name__ == "__main__":
+    print("staged:", stage_python())
     print("built:", build(sys.argv[1:]) if sys.argv[1:] else build_parallel())

@@ -23,6 +23,29 @@ def oracle():
     return o
 
 
+def reference(mode):
+    """The reference's own modules (``oracle/refmodel.py``): "native" on the reference's own
+    kernels, "dropin" over this repository's modules.  Skips when they were not staged (no
+    reference checkout when ``__graft_entry__.build()`` ran)."""
+    from oracle import refmodel
+
+    if not refmodel.available():
+        pytest.skip("reference package not staged (oracle/build_ref.py stage_python)")
+    if mode == "native" and not refmodel.kernels_available():
+        pytest.skip("reference kernels not built (oracle/build_ref.py)")
+    return refmodel.load(mode)
+
+
+@pytest.fixture
+def ref_dropin():
+    return reference("dropin")
+
+
+@pytest.fixture
+def ref_native():
+    return reference("native")
+
+
 @pytest.fixture(scope="session")
 def cuda():
     import torch

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -26,8 +27,11 @@ OUT = Path(__file__).resolve().parent
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("VHOPE_REFERENCE"),
+                    help="reference checkout (default: the VHOPE_REFERENCE environment variable)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set VHOPE_REFERENCE")
     import oracle.build_ref as br
 
     br.REF_ROOT = Path(args.reference)

@@ -11,7 +11,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 def declared_symbols():
     text = (ROOT / "include" / "vhope.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(vh_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|void|const char\*)\s+(vh_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_entry_points():

@@ -1,7 +1,8 @@
 """Multi-process host logic of the batch-sharded bench on CPU (gloo, world size 2):
 weights synchronised from rank 0, distinct per-rank input shards, an all-gather of the logits
 equal to a single-process forward of the concatenated batch, and max-over-ranks timing.
-The forward runs the CPU stand-in (oracle SRNL), so no GPU is needed."""
+The forward is the bench's CPU reference arm (the reference's own modules with the SRNL
+recurrence on the oracle port), so no GPU is needed."""
 import os
 import socket
 import sys
@@ -29,15 +30,15 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
         import bench
-        from visionhope_b200.backbone import create_model, prepare_for_inference
 
-        torch.manual_seed(100 + rank)  # different local init on purpose
-        model = create_model("visionhope_tiny", depths=(1, 1, 1, 1), num_classes=10)
-        model = model.to(memory_format=torch.channels_last)
-        prepare_for_inference(model)
+        ref, model = bench.reference_cpu_model("visionhope_tiny", depths=(1, 1, 1, 1), num_classes=10)
+        if rank:
+            torch.manual_seed(100 + rank)  # a different local init on purpose
+            for p in model.parameters():
+                p.data.normal_(0, 0.02)
         bench.sync_model(model, world)
         x = bench.rank_inputs(1, rank, torch.device("cpu"))
-        with bench.cpu_reference_patches(), torch.inference_mode():
+        with bench.oracle_srnl(ref), torch.inference_mode():
             logits = model(x)
         gathered = [torch.empty_like(logits) for _ in range(world)]
         dist.all_gather(gathered, logits)
@@ -52,19 +53,20 @@ def _worker(rank, world, port, out_dir):
 
 
 def test_two_rank_batch_sharding(tmp_path):
+    from oracle import refmodel
+
+    if not refmodel.available():
+        pytest.skip("reference package not staged (oracle/build_ref.py stage_python)")
     world, port = 2, _free_port()
     mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     res = torch.load(tmp_path / "rank0.pt")
     assert res["ms"] == 11.0
     import bench
-    from visionhope_b200.backbone import create_model, prepare_for_inference
 
-    model = create_model("visionhope_tiny", depths=(1, 1, 1, 1), num_classes=10)
-    model = model.to(memory_format=torch.channels_last)
-    prepare_for_inference(model)
+    ref, model = bench.reference_cpu_model("visionhope_tiny", depths=(1, 1, 1, 1), num_classes=10)
     model.load_state_dict(res["state"])
     assert not torch.equal(res["inputs"][0], res["inputs"][1])
-    with bench.cpu_reference_patches(), torch.inference_mode():
+    with bench.oracle_srnl(ref), torch.inference_mode():
         ref = model(res["inputs"].contiguous(memory_format=torch.channels_last))
     torch.testing.assert_close(res["gathered"], ref, rtol=1e-4, atol=1e-5)

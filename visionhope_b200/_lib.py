@@ -8,6 +8,8 @@ thread-local message of ``vh_last_error`` surface as ``RuntimeError`` (the refer
 from __future__ import annotations
 
 import ctypes
+import functools
+import itertools
 import os
 import threading
 from ctypes import c_float, c_int32, c_int64, c_void_p
@@ -192,3 +194,20 @@ def memories(states, per_chain: bool = False) -> VhMemories:
 
 def env_flag(name: str, default: str = "0") -> bool:
     return os.environ.get(name, default) not in ("", "0", "false", "False")
+
+
+def on_input_device(fn):
+    """Decorator: run ``fn`` with the device of its first CUDA tensor argument current, so that
+    ``stream_handle()`` and torch allocations inside refer to the inputs' GPU.  Calls whose
+    inputs are all on the current device (or on no GPU, which the entry points then reject)
+    run unchanged."""
+    @functools.wraps(fn)
+    def call(*args, **kwargs):
+        for value in itertools.chain(args, kwargs.values()):
+            if isinstance(value, torch.Tensor) and value.is_cuda:
+                if value.device.index != torch.cuda.current_device():
+                    with torch.cuda.device(value.device):
+                        return fn(*args, **kwargs)
+                break
+        return fn(*args, **kwargs)
+    return call

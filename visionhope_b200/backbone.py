@@ -16,8 +16,7 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
-from .operator import VisionHOPEOperator
-from .srnl import SRNL, trunc_normal_
+from .mixer import ScanMemories, ScanMixer
 from .utils.grn import GlobalResponseNorm
 from .utils.bias_act import add_cast, add_cast_ok, bias_act, stem_conv, stem_conv_ok
 from .utils.dwconv import depthwise_fused, fusable, gate_pos_ok
@@ -290,8 +289,9 @@ class VisionHOPEBlock(nn.Module):
         self.proj_in = nn.Conv2d(dim, mixer_dim, 1)
         if use_direction_scale and direction_merge == "sum":
             direction_merge = "scale"
-        self.operator = VisionHOPEOperator(mixer_dim, head_dim, chunk_size, direction_merge,
-                                           share_direction_skip, _initialize=False)
+        if chunk_size is not None:
+            raise NotImplementedError("the harness runs image-aligned chunks (chunk_size=None) only")
+        self.operator = ScanMixer(mixer_dim, head_dim, direction_merge, share_direction_skip)
         k = 7 if local_mode == "gated_dwconv7" else 3
         self.local_conv = nn.Conv2d(mixer_dim, mixer_dim, k, padding=k // 2, groups=mixer_dim)
         self.local_gate = nn.Conv2d(mixer_dim, mixer_dim, 1) if local_mode == "gated_dwconv7" else None
@@ -299,8 +299,7 @@ class VisionHOPEBlock(nn.Module):
         self.local_position = (nn.Conv2d(mixer_dim, mixer_dim, 5, padding=2, groups=mixer_dim)
                                if use_output_lepe else None)
         self.proj_out = nn.Linear(mixer_dim, dim)
-        self.operator.reset_parameters()
-        trunc_normal_(self.proj_out.weight, std=0.02)
+        nn.init.trunc_normal_(self.proj_out.weight, std=0.02, a=-2.0, b=2.0)
         nn.init.zeros_(self.proj_out.bias)
         self.drop_path = nn.Identity()  # inference only: stochastic depth is the identity
         self.drop_path_rate = float(drop_path)
@@ -351,27 +350,24 @@ class VisionHOPEBlock(nn.Module):
         already computed it (then x only supplies the memory format)."""
         channels_last = x.is_contiguous(memory_format=torch.channels_last)
         x_local, lepe = self._local_and_position(x, inner, self._inference_prepared)
-        if self._inference_prepared:
-            path, _ = self.operator._inference_path(x_local)
-            if path != "ordinary":
-                # The scan launch adds the output position term and writes the dtype the output
-                # projection consumes: (out + lepe) rounded once, as the reference's fp32 add
-                # followed by autocast's cast.
-                if lepe is None and self.local_position is not None:
-                    if fusable(x_local, self.local_position):
-                        lepe = depthwise_fused(x_local, self.local_position, "bias").permute(0, 2, 3, 1)
-                    else:
-                        lepe = self.local_position(x_local).permute(0, 2, 3, 1)
-                    if lepe.dtype != x_local.dtype:
-                        lepe = lepe.to(x_local.dtype)
-                out = self.operator._forward_fast(x_local, path, addend=lepe,
-                                                  final_dtype=_autocast_dtype() or torch.float32)
-                out = linear_cached(self.proj_out, out)
-                # NHWC storage viewed as NCHW (channels-last); the reference copies it to
-                # contiguous NCHW here, which only costs a layout pass before the residual add.
-                out = out.permute(0, 3, 1, 2)
-                return out if channels_last else out.contiguous()
-        out = self.operator(x_local, channels_last=channels_last)
+        if self._inference_prepared and x_local.dtype == (_autocast_dtype() or x_local.dtype):
+            # The reference's prepared fast branch (block.py:73-80): the scan launch adds the
+            # output position term and writes the dtype the output projection consumes,
+            # (out + lepe) rounded once, as the reference's fp32 add followed by autocast's cast.
+            if lepe is None and self.local_position is not None:
+                if fusable(x_local, self.local_position):
+                    lepe = depthwise_fused(x_local, self.local_position, "bias").permute(0, 2, 3, 1)
+                else:
+                    lepe = self.local_position(x_local).permute(0, 2, 3, 1)
+            out = self.operator(x_local, addend=lepe, out_dtype=_autocast_dtype() or torch.float32)
+            out = linear_cached(self.proj_out, out)
+            # NHWC storage viewed as NCHW (channels-last); the reference copies it to
+            # contiguous NCHW here, which only costs a layout pass before the residual add.
+            out = out.permute(0, 3, 1, 2)
+            return out if channels_last else out.contiguous()
+        # The unprepared order (block.py:82-88): fp32 operator output, the position term added
+        # in NCHW, then proj_out as a 1x1 convolution.
+        out = self.operator(x_local).permute(0, 3, 1, 2)
         if self.local_position is not None:
             out = out + self.local_position(x_local)
         out = F.conv2d(out, self.proj_out.weight[:, :, None, None], self.proj_out.bias)
@@ -415,7 +411,7 @@ class VisionHOPEBlock(nn.Module):
 
 def initialize_weights(module):
     if isinstance(module, (nn.Linear, nn.Conv2d)):
-        trunc_normal_(module.weight, std=0.02)
+        nn.init.trunc_normal_(module.weight, std=0.02, a=-2.0, b=2.0)
         if module.bias is not None:
             nn.init.constant_(module.bias, 0)
 
@@ -525,15 +521,10 @@ def prepare_for_inference(model):
     model.eval()
     counts = dict(line_mixer=0, srnl=0, operator=0, layernorm2d=0, grn=0, layerscale=0)
     for m in model.modules():
-        if isinstance(m, SRNL):
-            m.fast_inference = True
+        if isinstance(m, ScanMemories):
             counts["srnl"] += 1
-            # A model converted to channels_last stores the 4-D memory matrices permuted; the
-            # scan reads them dense, so store them dense once instead of copying every call.
-            for mem in m.initial_memories:
-                if not mem.is_contiguous():
-                    mem.data = mem.data.contiguous()
-        elif isinstance(m, VisionHOPEOperator):
+            m.densify()  # read dense by the scan, instead of a copy every call
+        elif isinstance(m, ScanMixer):
             counts["operator"] += 1
         elif isinstance(m, LayerNorm2d):
             m.inference_layout = True

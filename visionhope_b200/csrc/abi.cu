@@ -1,4 +1,5 @@
 // libvhope: library-wide entry points (init, error text, version) and host helpers.
+#include <atomic>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -62,15 +63,16 @@ bool ensure_smem_attr(const void* func, size_t bytes) {
 }
 
 int sm_count() {
-    static int counts[64] = {0};
+    // Per device; concurrent first calls may both query the count and store the same value.
+    static std::atomic<int> counts[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (counts[dev] == 0) {
-        int n = 0;
+    int n = counts[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        counts[dev] = n;
+        counts[dev].store(n, std::memory_order_relaxed);
     }
-    return counts[dev];
+    return n;
 }
 
 // Defined in the kernel translation units: set every kernel's attributes for `device`.

@@ -20,6 +20,7 @@
 // variance take two quad shuffles.  Each normalized value is rounded to bf16 as the LayerNorm
 // kernel would store it for the projection, so the GEMM sees the same operand; the normalized
 // activations never go to HBM.
+#include <atomic>
 #include <algorithm>
 
 #include "abi_util.h"
@@ -219,11 +220,17 @@ int rows_gemm_run(const void* x, const float* lnw, const float* lnb, float eps, 
     const void* fn = reinterpret_cast<const void*>(&rows_gemm_kernel<K, N, LN>);
     if (!ensure_smem_attr(fn, smem))
         return fail(VH_E_DEVICE, "row gemm: cannot reserve %zu bytes of shared memory", smem);
-    static int per_sm = 0;  // resident CTAs per SM of this instantiation
+    // Resident CTAs per SM of this instantiation, per device (GPUs of a process may differ);
+    // concurrent first calls may both query it, and store the same value.
+    static std::atomic<int> per_sm_cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    int per_sm = per_sm_cache[dev].load(std::memory_order_relaxed);
     if (per_sm == 0) {
         int n = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kRgThreads, smem) != cudaSuccess || n <= 0) n = 1;
         per_sm = n;
+        per_sm_cache[dev].store(n, std::memory_order_relaxed);
     }
     const int64_t tiles = (M + 15) / 16;
     const int64_t want = (tiles + kRgWarps - 1) / kRgWarps;

@@ -945,6 +945,11 @@ int noalloc_scratch(float** out) {
 }  // namespace
 }  // namespace vh
 
+extern "C" void vh_grn_noalloc_reset(void) {
+    std::lock_guard<std::mutex> lock(vh::g_noalloc_mu);
+    for (float*& p : vh::g_noalloc_ptr) p = nullptr;
+}
+
 extern "C" int vh_grn_fwd_noalloc(const void* x, int32_t x_dtype, const float* gamma,
                                   const float* beta, float eps, float* y, float* gx, float* inv_den,
                                   int32_t batch, int32_t height, int32_t width, int32_t channels,

@@ -12,7 +12,6 @@ import os
 import torch
 
 from .. import _lib
-from ..utils.cuda import on_tensor_device
 
 MAX_CHUNK = 64
 SUPPORTED_HEAD_DIMS = (4, 8, 16, 32, 64)
@@ -118,7 +117,7 @@ def _check_tracing():
         raise RuntimeError("SRNL TorchScript tracing is unsupported; use eager or CUDA Graph inference.")
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _normalized_query_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q, chunk_size):
     _check_tracing()
     if not x.is_cuda:
@@ -151,7 +150,7 @@ def srnl_normalized_query(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q, chunk_s
 srnl_normalized_query.supports_broadcast_state = True
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _raw_query_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, chunk_size, num_heads,
                        head_dim):
     _check_tracing()

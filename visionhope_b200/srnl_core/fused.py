@@ -11,7 +11,6 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ..utils.cuda import on_tensor_device
 from .chunk import SUPPORTED_HEAD_DIMS, recurrence_constants, run_sequence
 
 
@@ -124,7 +123,7 @@ class _FusedModule:
         if M_m_0.dtype != torch.float32 or D_skip.dtype != torch.float32 or Dir_weight.dtype != torch.float32:
             raise RuntimeError("line fused HOPE forward expects fp32 state, skip, and direction weights.")
 
-    @on_tensor_device
+    @_lib.on_input_device
     def srnl_line_forward_seq_noatomic(self, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, X, Q_raw,
                                        D_skip, Dir_weight, H, W, D_int):
         """X, Q_raw [B, 4, L, C] -> fp32 [B, H, W, C] (fused.cu:307-351)."""
@@ -134,7 +133,7 @@ class _FusedModule:
 
     srnl_line_forward_seq = srnl_line_forward_seq_noatomic
 
-    @on_tensor_device
+    @_lib.on_input_device
     def srnl_line_forward_noatomic(self, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, X, Q_raw,
                                    D_skip, Dir_weight, H, W, D_int):
         """X packed [B, 4, heads, L, D], Q_raw [B, 4, L, C] -> fp32 [B, H, W, C] (fused.cu:221-262)."""
@@ -144,7 +143,7 @@ class _FusedModule:
 
     srnl_line_forward = srnl_line_forward_noatomic
 
-    @on_tensor_device
+    @_lib.on_input_device
     def srnl_sequence_forward(self, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, X, Q_raw, chunk_sizes):
         """X [B, R, heads, N, D], Q_raw [B, R, N, C] -> [B, R, heads, N, D] in X's dtype."""
         if not (X.is_cuda and X.dim() == 5):
@@ -184,7 +183,7 @@ def load_fused_cuda(io_dtype=torch.bfloat16):
     return _extensions[io_dtype]
 
 
-@on_tensor_device
+@_lib.on_input_device
 def srnl_sequence_inference(states, x, queries, chunk_sizes):
     """Read a packed sequence without allocating backward intermediates (fused.py:96-106)."""
     if torch.jit.is_tracing():

@@ -9,14 +9,14 @@ from __future__ import annotations
 
 import torch
 
+from .. import _lib
 from . import chunk as _base
-from ..utils.cuda import on_tensor_device
 
 MAX_LOGICAL_CHUNK = None
 SUPPORTED_HEAD_DIMS = _base.SUPPORTED_HEAD_DIMS
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _long_chunk_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, chunk_size, num_heads,
                         head_dim):
     _base._check_tracing()
@@ -49,7 +49,7 @@ def srnl_long_chunk(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, chunk_siz
                         M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _variable_lines_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, row_chunk_size,
                             col_chunk_size, num_heads, head_dim):
     _base._check_tracing()

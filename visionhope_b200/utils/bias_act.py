@@ -4,12 +4,11 @@ residual add with a cast (``vh_add_cast_fwd``): y = (dtype)(x + r)."""
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 ACTS = {None: 0, "gelu": 1}
 
 
-@on_tensor_device
+@_lib.on_input_device
 def bias_act(x, bias, act=None, out_dtype=None):
     """x: channels-last NCHW CUDA tensor (C a multiple of 8); bias: [C].  Returns a channels-last
     tensor of ``out_dtype`` (default x's dtype)."""
@@ -35,7 +34,7 @@ def add_cast_ok(x, r):
             and dense(x) and dense(r) and (x.dim() != 4 or x.stride() == r.stride()))
 
 
-@on_tensor_device
+@_lib.on_input_device
 def add_cast(x, r, out_dtype):
     """(out_dtype)(x + r), summed in fp32 and rounded once, laid out as x."""
     _lib.ensure_device(x)
@@ -59,7 +58,7 @@ def stem_conv_ok(x, conv):
             and conv.dilation == (1, 1) and conv.bias is not None)
 
 
-@on_tensor_device
+@_lib.on_input_device
 def stem_conv(x, conv, act=None, out_dtype=torch.bfloat16):
     """act(bf16(conv(x)) + b) of a 3-channel channels-last fp32 image (``vh_stem_conv_fwd``):
     the first stem convolution with its folded BatchNorm and GELU.  Returns a channels-last

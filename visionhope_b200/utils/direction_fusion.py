@@ -8,10 +8,9 @@ logical NCHW, channels-last storage when requested.  Forward only.
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _postprocess_forward(y, x, d_skip, direction_scale, height, width, channels_last):
     _lib.ensure_device(y)
     if y.dtype != x.dtype:

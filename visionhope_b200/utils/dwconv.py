@@ -7,7 +7,6 @@ Inference only (no autograd); channels-last CUDA tensors of fp32 or bf16.
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 MODES = {"bias": 0, "resid": 1, "gate": 2, "gelu": 3, "resid_add": 4, "gate_pos": 5}
 
@@ -36,7 +35,7 @@ def gate_pos_ok(x, conv, pos_conv):
             and pos_conv.kernel_size == (5, 5) and fusable(x, conv) and fusable(x, pos_conv))
 
 
-@on_tensor_device
+@_lib.on_input_device
 def depthwise_fused(x, conv, mode, gate=None, addend=None, with_sumsq=False, pos_conv=None):
     """Apply depthwise ``conv`` to channels-last NCHW ``x`` with epilogue ``mode``:
     "bias": conv(x) + b;  "resid": s + (conv(s) + b) with s = x, or s = x + addend when an

@@ -6,10 +6,9 @@ statistics workspace comes from PyTorch's caching allocator.  Forward only.
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 
-@on_tensor_device
+@_lib.on_input_device
 def grn_forward(x, gamma, beta, eps, *, want_stats=False, out_dtype=torch.float32):
     """x logical [B, C, H, W] stored channels-last -> channels-last y (and Gx, 1/den).
 

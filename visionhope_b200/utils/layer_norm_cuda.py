@@ -6,10 +6,9 @@ Forward only.
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 
-@on_tensor_device
+@_lib.on_input_device
 def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False, out_dtype=torch.float32):
     """x_rows [rows, C] (any float dtype, contiguous) -> [rows, C] (and mean, rstd).
 
@@ -30,7 +29,7 @@ def layernorm_rows(x_rows, weight, bias, eps, *, want_stats=False, out_dtype=tor
     return (y, mean, rstd) if want_stats else y
 
 
-@on_tensor_device
+@_lib.on_input_device
 def add_layernorm_rows(x_rows, r_rows, weight, bias, eps, *, out_dtype=torch.float32, sum_out=None):
     """s = x + r (written to ``sum_out``, default x itself) and LayerNorm(s): the block's
     residual add followed by its second norm (models/block.py:105-106).  x, r: contiguous
@@ -50,7 +49,7 @@ def add_layernorm_rows(x_rows, r_rows, weight, bias, eps, *, out_dtype=torch.flo
     return s, y
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _layernorm2d_forward(x, weight, bias, eps):
     batch, channels, height, width = x.shape
     rows = x.permute(0, 2, 3, 1).reshape(batch * height * width, channels)

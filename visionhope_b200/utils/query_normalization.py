@@ -6,10 +6,9 @@
 import torch
 
 from .. import _lib
-from .cuda import on_tensor_device
 
 
-@on_tensor_device
+@_lib.on_input_device
 def _qnorm_forward(q_raw, num_heads, head_dim):
     _lib.ensure_device(q_raw)
     q = q_raw.contiguous()
