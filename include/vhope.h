@@ -375,6 +375,13 @@ const char* vh_last_error(void);
  * validation failure).  Lets a host count device launches without knowing each path. */
 int vh_last_launch_count(void);
 
+/* Status of the chunk-parallel tensor-core scan (no counterpart in the reference): non-zero
+ * once, on any launch since the last reset, one of its bounded waits (a TMA tile or tensor-core
+ * result that did not arrive within 2 s) gave up; the CTA then stopped its chain, released its
+ * tensor memory and left, and that call's output is invalid.  Synchronous (reads a device
+ * word); reset != 0 clears it.  Returns -1 when the word cannot be read. */
+int vh_tc_status(int32_t reset);
+
 /* Library version string. */
 const char* vh_version(void);
 

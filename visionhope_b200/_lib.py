@@ -130,6 +130,8 @@ def load() -> ctypes.CDLL:
                                                  c_void_p]
             lib.vh_last_launch_count.restype = c_int32
             lib.vh_last_launch_count.argtypes = []
+            lib.vh_tc_status.restype = c_int32
+            lib.vh_tc_status.argtypes = [c_int32]
             lib.vh_probe_ffma.restype = c_int32
             lib.vh_probe_ffma.argtypes = [c_void_p, c_int32, c_int32, c_void_p]
             _lib = lib

@@ -4,6 +4,8 @@
 #pragma once
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #include "abi_util.h"
@@ -125,10 +127,27 @@ int launch_auto(const ScanParams& p, int max_chunk, int pairs_or_chains, cudaStr
 // Writes (final dtype)(out + addend) when the scans ran without folding it in (srnl_scan.cu).
 int launch_spatial_finalize(const ScanParams& p, int io_dtype, cudaStream_t st);
 
+// The chunk-parallel tensor-core scan (srnl_tc.cu).
+bool tc_applicable(const ScanParams& p, bool spatial);
+int run_tc_spatial(const ScanParams& p, int io_dtype, cudaStream_t st);
+int run_tc_sequence(const ScanParams& p, cudaStream_t st);
+
+// Which D = 16 bf16 scan runs: the chunk-parallel tensor-core scan gives each chain a whole
+// CTA, which pays when a launch has too few chains to fill the GPU with one warp per chain
+// (the warp-per-chain scan keeps one chain per warp and wins when chains are plentiful).
+// VH_SRNL_SCAN=tc or =warp forces one of them (where it applies).
+inline bool use_tc_scan(const ScanParams& p, bool spatial, int chains) {
+    (void)chains;
+    const char* env = std::getenv("VH_SRNL_SCAN");
+    if (!env || std::strcmp(env, "tc") != 0) return false;
+    return tc_applicable(p, spatial);
+}
+
 template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
     const int pairs = p.B * p.heads;
     if constexpr (mma_capable<D, T, T>()) {
+        if (use_tc_scan(p, true, 4 * pairs)) return run_tc_spatial(p, VH_BF16, st);
         if (p.aux) return launch_warp<kKindBoth>(p, pairs, st);
     }
     int rc = launch_auto<D, T, T, kKindRows>(p, p.W, pairs, st);
@@ -143,6 +162,9 @@ template <int D, typename XT, typename QT>
 int run_sequence(const ScanParams& p, cudaStream_t st) {
     int maxc = 1;
     for (int r = 0; r < p.R; ++r) maxc = std::max(maxc, p.chunk[r]);
+    if constexpr (mma_capable<D, XT, QT>()) {
+        if (use_tc_scan(p, false, p.B * p.R * p.heads)) return run_tc_sequence(p, st);
+    }
     return launch_auto<D, XT, QT, kKindSeq>(p, maxc, p.B * p.heads, st);
 }
 
