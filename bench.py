@@ -13,9 +13,12 @@ event times.  Extra keys:
                   overlapping the previous step's forward, then device to device into the
                   graph's input) and its logits are copied back to pinned host memory;
   roofline     -- the dominant kernel (the fused SRNL operator at the stage-1 shape of this
-                  batch) timed alone with CUDA events, against the measured FP32 FMA peak;
-  cpu_baseline -- the CPU stand-in for the reference (oracle port of SRNL + PyTorch CPU
-                  LayerNorm/GRN/convolutions) on a small sample, rank 0 at N = 1 only;
+                  batch) timed alone with CUDA events, against the measured bf16 tensor peak
+                  (MEASURED_PEAKS.json); roofline.kernels lists every hot-path kernel (the scan
+                  at each stage, qnorm, direction fusion, GRN, LayerNorm) against its peak;
+  ref_kernel   -- the reference's own fused operator kernel timed beside ours per stage;
+  cpu_baseline -- the reference's own modules on the host CPU (SRNL recurrence on the oracle's
+                  float port: the reference has none) on a small sample, rank 0 at N = 1 only;
   clocks       -- nvidia-smi samples taken during the timed region.
 --impl reference runs only that CPU workload (rank 0), timed per step, and prints its line.
 """
@@ -40,7 +43,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "VisionHOPE-T fwd images/sec @224"
 UNIT = "images/s"
-IMG = 224
+IMG = 224          # classification input side
+IMG_HW = (224, 224)  # this run's input (H, W): --image
+# Per-stage (mixer heads) of the model configurations (models/factory.py:9-16, head_dim 16).
+STAGE_HEADS = {"visionhope_tiny": (2, 4, 8, 16), "visionhope_small": (2, 5, 10, 16),
+               "visionhope_base": (3, 6, 14, 20)}
 
 
 def parse():
@@ -51,6 +58,10 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--model", default="visionhope_tiny")
+    ap.add_argument("--task", choices=("classify", "dense"), default="classify",
+                    help="classify: logits (config 4); dense: forward_intermediates, the four stage "
+                         "feature maps of the dense-prediction backbone (config 5)")
+    ap.add_argument("--image", default="224", help="input size: S or HxW (config 5: 512x2048)")
     ap.add_argument("--cpu-sample", type=int, default=8, help="images per CPU baseline step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-scan", action="store_true",
@@ -59,7 +70,19 @@ def parse():
                     help="time the block's depthwise kernels and GRN apply at the model's shapes and exit")
     ap.add_argument("--only-norms", action="store_true",
                     help="time only GRN and LayerNorm at the GRN/LN configuration's shapes")
-    return ap.parse_args()
+    args = ap.parse_args()
+    global IMG_HW
+    hw = [int(v) for v in args.image.lower().split("x")]
+    IMG_HW = (hw[0], hw[-1])
+    return args
+
+
+def metric_name(args):
+    if args.task == "dense":
+        return f"{args.model} backbone (forward_intermediates) images/sec @{IMG_HW[0]}x{IMG_HW[1]}"
+    if args.model == "visionhope_tiny" and IMG_HW == (224, 224):
+        return METRIC
+    return f"{args.model} fwd images/sec @{IMG_HW[0]}x{IMG_HW[1]}"
 
 
 def dist_env():
@@ -70,10 +93,13 @@ def dist_env():
 
 
 def config(args, world):
-    return {"workload": f"{args.model} classification forward, {IMG}x{IMG}, batch {args.batch}/GPU",
+    H, W = IMG_HW
+    kind = "classification forward" if args.task == "classify" else "backbone forward_intermediates"
+    gathered = "logits" if args.task == "classify" else "the four stage feature maps"
+    return {"workload": f"{args.model} {kind}, {H}x{W}, batch {args.batch}/GPU",
             "model": args.model, "global_batch": args.batch * world, "batch_per_gpu": args.batch,
-            "image_size": IMG, "precision": "bf16 autocast, fp32 params", "channels_last": True,
-            "execution": "cuda_graph", "parallelism": f"dp{world} (batch-sharded, all_gather logits)",
+            "image_size": [H, W], "precision": "bf16 autocast, fp32 params", "channels_last": True,
+            "execution": "cuda_graph", "parallelism": f"dp{world} (batch-sharded, all_gather {gathered})",
             "l2": "256 MiB buffer rewritten between timed steps; activations >> L2",
             "seed": 3}
 
@@ -144,7 +170,7 @@ def sync_model(model, world):
 def rank_inputs(batch, rank, device, generator_device=None):
     """This rank's shard of the synthetic batch: N(0,1) images from seed 3 + rank."""
     gen = torch.Generator(device=generator_device or device).manual_seed(3 + rank)
-    x = torch.randn(batch, 3, IMG, IMG, device=generator_device or device, generator=gen)
+    x = torch.randn(batch, 3, *IMG_HW, device=generator_device or device, generator=gen)
     return x.to(device).contiguous(memory_format=torch.channels_last)
 
 
@@ -159,24 +185,36 @@ def cpu_threads():
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
+def cpu_plan(args, steps, warmup):
+    """(steps, warm-up) of the CPU reference sample, bounded to tens of seconds: a dense
+    512 x 2048 image takes tens of seconds on the host, so that task times one image per step,
+    at most two steps, without warm-up."""
+    if args.task == "dense":
+        args.cpu_sample = 1
+        return max(1, min(steps, 2)), 0
+    return steps, warmup
+
+
 def run_cpu(args, steps, warmup):
     """Time the reference on the host CPU: returns (images/s, per-step seconds, cores, sample)."""
+    steps, warmup = cpu_plan(args, steps, warmup)
     cores = cpu_threads()
     torch.set_num_threads(cores)
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     ref, model = reference_cpu_model(args.model)
     gen = torch.Generator().manual_seed(3)
-    x = torch.randn(args.cpu_sample, 3, IMG, IMG, generator=gen).contiguous(memory_format=torch.channels_last)
+    x = torch.randn(args.cpu_sample, 3, *IMG_HW, generator=gen).contiguous(memory_format=torch.channels_last)
     times = []
     with oracle_srnl(ref), torch.inference_mode():
         for i in range(warmup + steps):
             t0 = time.perf_counter()
-            model(x)
+            model(x) if args.task == "classify" else model.forward_intermediates(x)
             dt = time.perf_counter() - t0
             if i >= warmup:
                 times.append(dt)
     ips = args.cpu_sample * len(times) / sum(times)
-    sample = (f"{args.cpu_sample} image(s)/step of the same {args.model} forward at {IMG}x{IMG}, fp32 on "
+    sample = (f"{args.cpu_sample} image(s)/step of the same {args.model} {args.task} forward at "
+              f"{IMG_HW[0]}x{IMG_HW[1]}, fp32 on "
               f"{cores} host threads: the reference's own modules (prepared), SRNL recurrence on the oracle's "
               f"float port (the reference has no CPU SRNL), {steps} timed steps after {warmup} warm-up")
     return ips, times, cores, sample
@@ -313,59 +351,177 @@ def srnl_flops(B, H, W, heads, D=16):
     return 2.0 * macs
 
 
-def roofline_scan(args, device, steps):
-    """Time the fused SRNL operator alone at the stage-1 shape of this batch."""
-    from visionhope_b200.srnl_core.fused import spatial_forward
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(path.read_text()) if path.exists() else {}
 
-    B, H, W, D = args.batch, IMG // 4, IMG // 4, 16
-    heads = 32 // D  # VisionHOPE-T stage 1: mixer_dim 32
+
+def _event_ms(fn, iters, flush=None):
+    """Mean CUDA-event time (ms) of fn over `iters` back-to-back calls after 3 warm-up calls
+    (the inputs of every shape timed here are larger than L2 or rewritten by `flush`)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if flush is not None:
+        times = []
+        for _ in range(iters):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.mean(times)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def _scan_inputs(device, B, H, W, heads, D=16, seed=1):
+    g = torch.Generator(device=device).manual_seed(seed)
     C = heads * D
-    g = torch.Generator(device=device).manual_seed(1)
     x = torch.randn(B, H, W, C, device=device, generator=g).to(torch.bfloat16)
     q = torch.randn(B, H, W, C, device=device, generator=g).to(torch.bfloat16)
     mems = [torch.randn(4, heads, D, D, device=device, generator=g) * 0.01 for _ in range(3)]
     mems += [torch.zeros(4, heads, D, device=device) for _ in range(2)]
-    skip = torch.zeros(C, device=device)
-    wts = torch.ones(4, C, device=device)
-    out = torch.empty(B, H, W, C, device=device)
-    for _ in range(3):
-        spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", out=out)
-    torch.cuda.synchronize()
-    n = max(steps, 5)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(n):
-        spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", out=out)
-    b.record()
-    b.synchronize()
-    ms = a.elapsed_time(b) / n
+    return x, q, mems, torch.zeros(C, device=device), torch.ones(4, C, device=device)
+
+
+def scan_roofline(device, B, H, W, heads, iters, label):
+    """The fused four-direction operator (one vh_srnl_spatial_fwd call, bf16 in, fp32 out) at
+    one shape: algorithmic FLOPs (2 x the reference's analytic MACs) and bytes (read x and q
+    once, write the fp32 result once) per call over its CUDA-event time, against the measured
+    bf16 tensor and HBM peaks."""
+    from visionhope_b200 import _lib
+    from visionhope_b200.srnl_core.fused import spatial_forward
+
+    D = 16
+    x, q, mems, skip, wts = _scan_inputs(device, B, H, W, heads, D)
+    out = torch.empty(B, H, W, heads * D, device=device)
+    fn = lambda: spatial_forward(mems, x, q, skip, wts, H, W, D, layout="image", out=out)
+    n0 = _lib.launch_count
+    fn()
+    launches = _lib.launch_count - n0
+    ms = _event_ms(fn, max(iters, 5))
+    pk = measured_peaks()
     flops = srnl_flops(B, H, W, heads, D)
-    peak = measure_ffma_peak(device)
-    achieved = flops / (ms * 1e-3) / 1e12
-    alg_bytes = B * H * W * C * (2 + 2 + 4)
-    peaks = {}
-    peaks_path = ROOT / "MEASURED_PEAKS.json"
-    if peaks_path.exists():
-        peaks = json.loads(peaks_path.read_text())
-    traffic = None
-    prof = ROOT / "profiles" / "srnl_warp_kernel_stage1_b256.md"
-    if prof.exists() and B == 256:
-        for line in prof.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                traffic = int(line.split(":")[1])
+    nbytes = B * H * W * heads * D * (2 + 2 + 4)
+    tfs, gbs = flops / (ms * 1e-3) / 1e12, nbytes / (ms * 1e-3) / 1e9
+    return {"kernel": "srnl scan (fused 4-direction operator)", "shape": label, "B": B, "H": H, "W": W,
+            "heads": heads, "ms": ms, "launches": launches, "flops": flops, "alg_bytes": nbytes,
+            "tflops": tfs, "gbs": gbs,
+            "tensor_frac": tfs / pk["bf16_tflops"] if "bf16_tflops" in pk else None,
+            "hbm_frac": gbs / pk["hbm_gbs"] if "hbm_gbs" in pk else None}
+
+
+def roofline_scan(args, device, steps):
+    """The dominant kernel of the forward (the SRNL operator at the stage-1 shape of this batch),
+    timed alone with CUDA events, against the measured bf16 tensor peak (its contractions run
+    on the tensor cores); the HBM fraction and the FP32-FMA fraction (own probe, not in
+    MEASURED_PEAKS.json) are listed beside it."""
+    H, W = IMG_HW[0] // 4, IMG_HW[1] // 4
+    heads = STAGE_HEADS[args.model][0]
+    r = scan_roofline(device, args.batch, H, W, heads, steps, f"{args.model} stage 1")
+    pk = measured_peaks()
+    ffma = measure_ffma_peak(device)
+    peak = pk.get("bf16_tflops")
     return {
-        "kernel": "srnl_warp_kernel<kKindBoth> (fused 4-direction SRNL operator, one launch)",
-        "shape": f"B={B} H={H} W={W} C={C} heads={heads} D={D} bf16 in, fp32 out",
-        "bound": "fp32", "unit": "TFLOP/s", "achieved": achieved, "peak": peak,
-        "frac": achieved / peak if peak else None,
-        "peak_source": "measured FP32 FFMA probe on this GPU (vh_probe_ffma), no tensor cores",
-        "traffic": traffic, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-        "of this workload (profiles/srnl_warp_kernel_stage1_b256.md)" if traffic else None,
-        "launch_ms": ms, "flops_per_launch": flops,
-        "alg_bytes_per_launch": alg_bytes,
-        "hbm_frac_of_measured": (alg_bytes / (ms * 1e-3) / 1e9) / peaks["hbm_gbs"] if "hbm_gbs" in peaks else None,
-        "tensor_frac_of_measured": (achieved / peaks["bf16_tflops"]) if "bf16_tflops" in peaks else None,
+        "kernel": "SRNL operator, one vh_srnl_spatial_fwd call (warp-per-chain scan, or the tensor-core "
+                  "scan plus its fold where a launch has few chains)",
+        "shape": f"B={args.batch} H={H} W={W} C={16 * heads} heads={heads} D=16 bf16 in, fp32 out",
+        "launches_per_call": r["launches"],
+        "bound": "tensor", "unit": "TFLOP/s", "achieved": r["tflops"], "peak": peak,
+        "frac": r["tflops"] / peak if peak else None,
+        "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 GEMM burst) -- of measured",
+        "traffic": None,
+        "traffic_note": "not measured in this run (ncu is not run inside the bench); one launch's DRAM "
+                        "bytes from an ncu capture are in profiles/srnl_warp_kernel_stage1_b256.md",
+        "launch_ms": r["ms"], "flops_per_launch": r["flops"], "alg_bytes_per_launch": r["alg_bytes"],
+        "hbm_frac_of_measured": r["hbm_frac"], "tensor_frac_of_measured": r["tensor_frac"],
+        "fp32_ffma_peak_tflops": ffma, "fp32_ffma_frac": r["tflops"] / ffma if ffma else None,
     }
+
+
+def roofline_fusion(device, iters=5):
+    """Query normalization and direction fusion (the ordinary path's bandwidth kernels) at the
+    operator configuration's shape, B = 64, 56 x 56, C = 96: qnorm reads bf16 q [B, 4, L, C] and
+    writes fp32 [B, 4, heads, L, D] (6 B per element); dirfuse reads fp32 y and x
+    [B, 4, heads, L, D] and writes the fp32 NCHW output (36 B per output element)."""
+    from visionhope_b200.utils.direction_fusion import visionhope_postprocess_scale
+    from visionhope_b200.utils.query_normalization import visionhope_qnorm
+
+    B, H, W, heads, D = 64, 56, 56, 6, 16
+    L, C = H * W, heads * D
+    g = torch.Generator(device=device).manual_seed(2)
+    hbm = measured_peaks().get("hbm_gbs")
+    qr = torch.randn(B, 4, L, C, device=device, generator=g).to(torch.bfloat16)
+    y = torch.randn(B, 4, heads, L, D, device=device, generator=g)
+    xx = torch.randn(B, 4, heads, L, D, device=device, generator=g)
+    skip = torch.randn(heads, D, device=device, generator=g)
+    scale = torch.randn(4, C, device=device, generator=g)
+    rows = []
+    for name, fn, nbytes in (
+            ("qnorm", lambda: visionhope_qnorm(qr, heads, D), qr.numel() * 6),
+            ("dirfuse (NCHW out)", lambda: visionhope_postprocess_scale(y, xx, skip, scale, H, W, False),
+             B * L * C * 36),
+            ("dirfuse (channels-last out)", lambda: visionhope_postprocess_scale(y, xx, skip, scale, H, W, True),
+             B * L * C * 36)):
+        ms = _event_ms(fn, iters)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        rows.append({"kernel": name, "shape": [B, 4, heads, L, D], "ms": ms, "alg_bytes": nbytes,
+                     "achieved_gbs": gbs, "hbm_frac": gbs / hbm if hbm else None})
+    return rows
+
+
+def ref_kernel_compare(device, B, iters=3):
+    """The reference's own fused operator kernel (srnl_line_forward_seq_noatomic, built from its
+    sources into oracle/_ref) beside ours at VisionHOPE-T's four stage shapes and this batch:
+    the reference gets its four serialized scans (materialised outside the timed call), ours
+    the channels-last image; both bf16 in, fp32 out."""
+    from oracle.build_ref import load_built
+    from visionhope_b200.srnl_core.fused import spatial_forward
+
+    try:
+        ext = load_built("vhref_fused_bf16")
+    except (FileNotFoundError, ImportError, OSError) as exc:
+        return {"unavailable": str(exc)}
+    rows = []
+    for stage, (H, heads) in enumerate(((56, 2), (28, 4), (14, 8), (7, 16)), 1):
+        x, q, mems, skip, wts = _scan_inputs(device, B, H, H, heads)
+        C = heads * 16
+
+        def serialize(t):
+            hw = t.reshape(B, H * H, C)
+            wh = t.transpose(1, 2).reshape(B, H * H, C)
+            return torch.stack([hw, hw.flip(1), wh, wh.flip(1)], dim=1).contiguous()
+
+        xs, qs = serialize(x), serialize(q)
+        t_ref = _event_ms(lambda: ext.srnl_line_forward_seq_noatomic(*mems, xs, qs, skip, wts, H, H, 16), iters)
+        t_ours = _event_ms(lambda: spatial_forward(mems, x, q, skip, wts, H, H, 16, layout="image"), iters)
+        del xs, qs
+        rows.append({"stage": stage, "shape": [B, H, H, C], "reference_ms": t_ref, "ours_ms": t_ours,
+                     "speedup": t_ref / t_ours})
+    return {"kernel": "reference srnl_line_token_parallel + merge (fused.cu:307-351) vs vh_srnl_spatial_fwd",
+            "stages": rows}
+
+
+def per_kernel_rooflines(args, device):
+    """roofline.kernels: every hot-path kernel against MEASURED_PEAKS.json (the scan at each of
+    this model's stage shapes, then the operator configuration's shape, qnorm, direction fusion,
+    GRN and LayerNorm)."""
+    B = args.batch
+    rows = [scan_roofline(device, B, IMG_HW[0] >> (i + 1), IMG_HW[1] >> (i + 1), heads, 5,
+                          f"{args.model} stage {i}")
+            for i, heads in enumerate(STAGE_HEADS[args.model], 1)]
+    rows.append(scan_roofline(device, 64, 56, 56, 6, 5, "operator configuration (B=64, C=96)"))
+    rows += roofline_fusion(device)
+    rows += roofline_norms(device, 5)["norms_roofline"]
+    return rows
 
 
 def roofline_norms(device, iters=10):
@@ -491,7 +647,9 @@ def run_ours(args, world, rank, local):
 
     def fwd():
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            return model(static_in)
+            if args.task == "dense":
+                return list(model.forward_intermediates(static_in))
+            return [model(static_in)]
 
     with torch.inference_mode():
         for _ in range(2):
@@ -500,15 +658,19 @@ def run_ours(args, world, rank, local):
         c0 = _lib.launch_count
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            static_out = fwd()
+            static_outs = fwd()
         launches_per_step = _lib.launch_count - c0
-        gathered = [torch.empty_like(static_out) for _ in range(world)] if world > 1 else None
+        gathered = [[torch.empty_like(o) for _ in range(world)] for o in static_outs] if world > 1 else None
         flush = torch.empty(64 * 1024 * 1024, device=device)  # 256 MiB
+
+        def gather():
+            for g_list, o in zip(gathered, static_outs):
+                dist.all_gather(g_list, o)
 
         def step():
             graph.replay()
             if world > 1:
-                dist.all_gather(gathered, static_out)
+                gather()
 
         for _ in range(args.warmup):
             step()
@@ -541,9 +703,9 @@ def run_ours(args, world, rank, local):
         # input (device to device) and copies its logits back to pinned host memory.  The
         # timed region spans the whole run, from the first host-to-device copy to the last
         # logits copy, so all K copies in and out are inside it.
-        host_in = torch.randn(args.batch, 3, IMG, IMG, generator=torch.Generator().manual_seed(3 + rank)
+        host_in = torch.randn(args.batch, 3, *IMG_HW, generator=torch.Generator().manual_seed(3 + rank)
                               ).contiguous(memory_format=torch.channels_last).pin_memory()
-        host_out = torch.empty(static_out.shape, dtype=static_out.dtype).pin_memory()
+        host_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in static_outs]
         staging = torch.empty_like(static_in)
         copy_stream = torch.cuda.Stream(device)
         main = torch.cuda.current_stream(device)
@@ -566,8 +728,9 @@ def run_ours(args, world, rank, local):
                         copied.record()
                 graph.replay()
                 if world > 1:
-                    dist.all_gather(gathered, static_out)
-                host_out.copy_(static_out, non_blocking=True)
+                    gather()
+                for h, o in zip(host_outs, static_outs):
+                    h.copy_(o, non_blocking=True)
 
         e2e_run(2)
         torch.cuda.synchronize()
@@ -579,25 +742,31 @@ def run_ours(args, world, rank, local):
         b.record()
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, device, world)
-        if not torch.isfinite(host_out).all():
-            raise RuntimeError("non-finite logits")
+        if not all(torch.isfinite(h).all() for h in host_outs):
+            raise RuntimeError("non-finite outputs")
 
-        roof = roofline_scan(args, device, args.steps) if rank == 0 else None
+        roof = ref_cmp = None
+        if rank == 0:
+            roof = roofline_scan(args, device, args.steps)
+            if world == 1:
+                roof["kernels"] = per_kernel_rooflines(args, device)
+                ref_cmp = ref_kernel_compare(device, args.batch) if args.model == "visionhope_tiny" else None
         del graph
     result = None
     if rank == 0:
         result = {
-            "metric": METRIC, "value": world * args.batch * 1000.0 / ms_max, "unit": UNIT,
+            "metric": metric_name(args), "value": world * args.batch * 1000.0 / ms_max, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1) images, random-init weights (seed 3)",
             "config": config(args, world),
             "e2e": {"value": world * args.batch * 1000.0 / e2e_ms, "unit": UNIT,
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
-                    "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
+                    "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in host_outs),
                     "ms_per_step": e2e_ms,
                     "pipeline": "host-to-device copy of batch i+1 on a copy stream overlaps the forward of "
-                                "batch i; timed from the first copy in to the last logits copy out"},
+                                "batch i; timed from the first copy in to the last output copy out"},
+            "ref_kernel": ref_cmp,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_per_step": launches_per_step,
             "roofline": roof, "clocks": clocks,
@@ -624,7 +793,7 @@ def main():
             except FileNotFoundError as exc:  # the reference package was not staged with the repo
                 print(json.dumps({"impl": "reference", "unavailable": str(exc)}), flush=True)
                 return
-            line = {"metric": METRIC, "value": ips, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            line = {"metric": metric_name(args), "value": ips, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(times),
                     "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                     "data": "synthetic N(0,1) images, random-init weights (seed 3)", "impl": "reference",
@@ -640,7 +809,9 @@ def main():
                 torch.cuda.set_device(local)
                 dev = torch.device("cuda", local)
                 if args.only_scan:
-                    res = roofline_scan(args, dev, args.steps)
+                    res = {"roofline": roofline_scan(args, dev, args.steps),
+                           "kernels": per_kernel_rooflines(args, dev),
+                           "ref_kernel": ref_kernel_compare(dev, args.batch)}
                 elif args.only_norms:
                     res = roofline_norms(dev, args.steps)
                 else:

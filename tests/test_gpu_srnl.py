@@ -14,6 +14,14 @@ from tests.conftest import make_memories, rel_err, serialize_np
 pytestmark = pytest.mark.gpu
 
 TORCH_DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+@pytest.fixture(autouse=True)
+def _warp_scan(monkeypatch):
+    """These cases pin the warp-per-chain and CTA-lockstep scans; the chunk-parallel
+    tensor-core scan, which the library picks for launches with few chains, has its own
+    tests (test_gpu_tc.py)."""
+    monkeypatch.setenv("VH_SRNL_SCAN", "warp")
 OUT_TOL = {"f32": 1e-4, "bf16": 1e-2, "f16": 2e-3}
 
 

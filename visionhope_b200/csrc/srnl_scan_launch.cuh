@@ -133,14 +133,18 @@ int run_tc_spatial(const ScanParams& p, int io_dtype, cudaStream_t st);
 int run_tc_sequence(const ScanParams& p, cudaStream_t st);
 
 // Which D = 16 bf16 scan runs: the chunk-parallel tensor-core scan gives each chain a whole
-// CTA, which pays when a launch has too few chains to fill the GPU with one warp per chain
-// (the warp-per-chain scan keeps one chain per warp and wins when chains are plentiful).
-// VH_SRNL_SCAN=tc or =warp forces one of them (where it applies).
+// CTA, which pays when a launch has too few chains to fill the GPU with one warp per chain;
+// the warp-per-chain scan wins when chains are plentiful.  Measured on B200 (bf16, image
+// layout): 24 chains of 128 x 512 tokens 3.36 against 6.89 ms, 48 chains of 64 x 256 1.21
+// against 1.65 ms, but 112 chains of 32 x 128 0.54 against 0.45 ms -- so the tensor-core scan
+// runs up to a third of an SM per chain.  VH_SRNL_SCAN=tc or =warp forces one of them (where
+// it applies).
 inline bool use_tc_scan(const ScanParams& p, bool spatial, int chains) {
-    (void)chains;
     const char* env = std::getenv("VH_SRNL_SCAN");
-    if (!env || std::strcmp(env, "tc") != 0) return false;
-    return tc_applicable(p, spatial);
+    if (env && std::strcmp(env, "warp") == 0) return false;
+    if (!tc_applicable(p, spatial)) return false;
+    if (env && std::strcmp(env, "tc") == 0) return true;
+    return 3 * chains <= sm_count();
 }
 
 template <int D, typename T>
