@@ -100,7 +100,8 @@ def config(args, world):
             "model": args.model, "global_batch": args.batch * world, "batch_per_gpu": args.batch,
             "image_size": [H, W], "precision": "bf16 autocast, fp32 params", "channels_last": True,
             "execution": "cuda_graph", "parallelism": f"dp{world} (batch-sharded, all_gather {gathered})",
-            "l2": "256 MiB buffer rewritten between timed steps; activations >> L2",
+            "l2": "L2 evicted between timed steps (a 256 MiB buffer written, then another 256 MiB read, "
+                  "outside the timed events); activations >> L2",
             "seed": 3}
 
 
@@ -356,30 +357,49 @@ def measured_peaks():
     return json.loads(path.read_text()) if path.exists() else {}
 
 
+class L2Flush:
+    """Evicts the L2 cache (126 MB on B200) between timed kernel launches, outside the timed
+    events: a 256 MiB buffer is written, then a second 256 MiB buffer is read.  The read pass
+    writes the first buffer's dirty lines back before the timed launch, so the timed kernel
+    starts from a cache that holds none of its data and no dirty lines to write back (after a
+    write-only flush, a short kernel pays ~126 MB of someone else's write-backs, ~19 us)."""
+
+    def __init__(self, device):
+        self.a = torch.empty(64 * 1024 * 1024, device=device)
+        self.b = torch.ones(64 * 1024 * 1024, device=device)
+        self.sink = torch.empty((), device=device)
+
+    def __call__(self):
+        self.a.fill_(1.0)
+        torch.amax(self.b, dim=0, out=self.sink)
+
+
+_flush = {}
+
+
+def l2_flush(device):
+    if device not in _flush:
+        _flush[device] = L2Flush(device)
+    return _flush[device]
+
+
 def _event_ms(fn, iters, flush=None):
-    """Mean CUDA-event time (ms) of fn over `iters` back-to-back calls after 3 warm-up calls
-    (the inputs of every shape timed here are larger than L2 or rewritten by `flush`)."""
+    """Mean CUDA-event time (ms) of one call of fn over `iters` calls after 3 warm-up calls,
+    with the L2 cache evicted before each call (outside the events)."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
-    if flush is not None:
-        times = []
-        for _ in range(iters):
-            flush.fill_(1.0)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            b.synchronize()
-            times.append(a.elapsed_time(b))
-        return statistics.mean(times)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
+    flush = flush or l2_flush(torch.cuda.current_device())
+    times = []
     for _ in range(iters):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
         fn()
-    b.record()
-    b.synchronize()
-    return a.elapsed_time(b) / iters
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.mean(times)
 
 
 def _scan_inputs(device, B, H, W, heads, D=16, seed=1):
@@ -530,15 +550,15 @@ def roofline_norms(device, iters=10):
     the algorithmic bytes (one read of x, one write of y) against the measured copy bandwidth.
     "grn" is the standalone op (statistics and apply from x); "grn_apply" is the apply pass
     fed with per-slice sums of x^2, as the model runs it after the FFN depthwise kernel (the
-    sums come from an untimed pre-pass here).  A 256 MiB buffer is rewritten before every timed
-    launch (outside the events)."""
+    sums come from an untimed pre-pass here).  The L2 cache is evicted before every timed
+    launch (outside the events, L2Flush)."""
     from visionhope_b200 import _lib
     from visionhope_b200.utils.grn_cuda import grn_apply, grn_forward
     from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
 
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = peaks.get("hbm_gbs")
-    flush = torch.empty(64 * 1024 * 1024, device=device)
+    flush = l2_flush(device)
     g = torch.Generator(device=device).manual_seed(2)
     rows = []
     for (B, H, W, C) in ((128, 56, 56, 96), (128, 7, 7, 768)):
@@ -562,8 +582,8 @@ def roofline_norms(device, iters=10):
 
 
 def _time_calls(fn, iters, flush):
-    """Median CUDA-event time (ms) of fn over `iters` calls after 3 warm-up calls, with `flush`
-    rewritten before each (outside the events), and libvhope launches per call."""
+    """Median CUDA-event time (ms) of fn over `iters` calls after 3 warm-up calls, with the L2
+    cache evicted before each (outside the events, L2Flush), and libvhope launches per call."""
     from visionhope_b200 import _lib
 
     for _ in range(3):
@@ -571,7 +591,7 @@ def _time_calls(fn, iters, flush):
     times = []
     n0 = _lib.launch_count
     for _ in range(iters):
-        flush.fill_(1.0)
+        flush()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
@@ -595,7 +615,7 @@ def roofline_depthwise(device, iters=10):
 
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = peaks.get("hbm_gbs")
-    flush = torch.empty(64 * 1024 * 1024, device=device)
+    flush = l2_flush(device)
     g = torch.Generator(device=device).manual_seed(5)
     B, bf = 256, torch.bfloat16
     rows = []
@@ -661,7 +681,7 @@ def run_ours(args, world, rank, local):
             static_outs = fwd()
         launches_per_step = _lib.launch_count - c0
         gathered = [[torch.empty_like(o) for _ in range(world)] for o in static_outs] if world > 1 else None
-        flush = torch.empty(64 * 1024 * 1024, device=device)  # 256 MiB
+        flush = l2_flush(device)  # evicts L2 between steps, outside the timed events
 
         def gather():
             for g_list, o in zip(gathered, static_outs):
@@ -685,7 +705,7 @@ def run_ours(args, world, rank, local):
                 dist.barrier()
             torch.cuda.synchronize()
             for a, b in evs:
-                flush.fill_(1.0)
+                flush()
                 a.record()
                 step()
                 b.record()
@@ -716,8 +736,9 @@ def run_ours(args, world, rank, local):
             with torch.cuda.stream(copy_stream):
                 staging.copy_(host_in, non_blocking=True)
                 copied.record()
+            # No L2 eviction inside this timed run: every step's batch is a fresh copy from the host
+            # and every forward moves far more than L2 through the cache.
             for i in range(k):
-                flush.fill_(1.0)
                 main.wait_event(copied)
                 static_in.copy_(staging, non_blocking=True)
                 freed.record()
