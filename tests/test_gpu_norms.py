@@ -321,3 +321,33 @@ def test_rows_gemm_rejects_shapes(cuda):
     x = torch.zeros(8, 48, device=cuda, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError):
         rows_gemm(x, torch.zeros(32, 48, device=cuda, dtype=torch.bfloat16))
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("shape", [(128, 56, 56, 96), (128, 7, 7, 768)], ids=["128x56x56x96", "128x7x7x768"])
+def test_grn_layernorm_config3_full_shapes(shape, dt, oracle, cuda):
+    """The GRN/LN configuration at its stated shapes and batch (128), seed 2: LN gamma ~ N(1, 0.02),
+    beta ~ N(0, 0.02); GRN gamma, beta ~ N(0, 0.02).  GRN (standalone and statistics-fed apply)
+    and LayerNorm against the oracle, 1e-5 normwise (fp32 outputs)."""
+    from visionhope_b200.utils.grn_cuda import grn_apply, grn_forward
+    from visionhope_b200.utils.layer_norm_cuda import layernorm_rows
+
+    B, H, W, C = shape
+    gen = np.random.default_rng(2)
+    x_nhwc = gen.normal(size=(B, H, W, C)).astype(np.float32)
+    x = _dev(x_nhwc, cuda, DT[dt])
+    xr = x.float().cpu().numpy()  # the values the kernels see
+    lw, lb = gen.normal(1, 0.02, size=C), gen.normal(0, 0.02, size=C)
+    gg, gb = gen.normal(0, 0.02, size=C), gen.normal(0, 0.02, size=C)
+
+    y = layernorm_rows(x.reshape(-1, C), _dev(lw, cuda), _dev(lb, cuda), 1e-6)
+    exp = oracle.layernorm_rows(xr.reshape(-1, C), lw, lb)
+    assert rel_err(y.cpu().numpy(), exp) < 1e-5
+
+    xc = x.permute(0, 3, 1, 2)  # channels-last logical NCHW
+    exp = oracle.grn_nhwc(xr, gg, gb)
+    g = grn_forward(xc, _dev(gg, cuda), _dev(gb, cuda), 1e-6)
+    assert rel_err(g.permute(0, 2, 3, 1).cpu().numpy(), exp) < 1e-5
+    sums = x.float().pow(2).sum(dim=(1, 2)).reshape(B, 1, C)
+    ga = grn_apply(xc, sums, _dev(gg, cuda), _dev(gb, cuda), 1e-6)
+    assert rel_err(ga.permute(0, 2, 3, 1).cpu().numpy(), exp) < 1e-5
