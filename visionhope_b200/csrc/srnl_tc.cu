@@ -53,10 +53,7 @@ constexpr int kCols = 64;       // accumulator columns per MMA (N): 16 y, 16 v, 
 constexpr int kBoxMax = 256;    // TMA box limit along the token dimension
 constexpr int kRec = 20;        // floats per token record row (80-byte rows)
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
-// The projection MMA in two parts: q channels against M_m (16 accumulator columns: y), x
-// channels against [M_v; M_k; e^T; a^T] (48 columns from column 16: v, k~, x.e, x.a, zeros).
-constexpr uint32_t kIdescQ = tcu::idesc_bf16_f32(kST, 16);
-constexpr uint32_t kIdescX = tcu::idesc_bf16_f32(kST, 48);
+constexpr uint32_t kIdesc = tcu::idesc_bf16_f32(kST, kCols);
 
 // Tensor maps of one launch: [0] rows (scans 0/1) or token order, [1] columns (scans 2/3).
 struct TcMaps {
@@ -333,14 +330,13 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
                         const unsigned char* aq = qt + size_t(s) * kST * 32;
                         const unsigned char* ax = xt + size_t(s) * kST * 32;
 #pragma unroll
-                        for (int k = 0; k < kSplits; ++k)  // y: rows 0-15 of the q-part operand
+                        for (int k = 0; k < kSplits; ++k)
                             tcu::mma_bf16(d, tcu::desc_kmajor_sw32(aq), tcu::desc_kmajor_sw32(bop + size_t(k) * 64 * 32),
-                                          kIdescQ, k > 0);
+                                          kIdesc, k > 0);
 #pragma unroll
-                        for (int k = 0; k < kSplits; ++k)  // rows 16-63 of the x-part operand
-                            tcu::mma_bf16(d + 16, tcu::desc_kmajor_sw32(ax),
-                                          tcu::desc_kmajor_sw32(bop + size_t(kSplits + k) * 64 * 32 + 16 * 32), kIdescX,
-                                          k > 0);
+                        for (int k = 0; k < kSplits; ++k)
+                            tcu::mma_bf16(d, tcu::desc_kmajor_sw32(ax),
+                                          tcu::desc_kmajor_sw32(bop + size_t(kSplits + k) * 64 * 32), kIdesc, 1);
                     }
                     tcu::mma_commit(&bars[2]);
                     ok = tcu::mbar_wait(&bars[2], gp & 1, kWaitNs);
@@ -357,92 +353,74 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
             tcu::tc_fence_after_sync();
 
             // ---- P1: one thread per token: gates and outputs from its accumulator row ----------
-            // A chunk of at most 128 tokens is one accumulator tile: warps 0-3 take the gates and
-            // warps 4-7 (the same TMEM lane quarters) the outputs of the same tokens.  Longer
-            // passes give each warp both for its tiles.
             const int qd = warp & 3;
-            auto gates_of = [&](int s) {
+            for (int s = warp >> 2; s * kST < n; s += 2) {
                 const int i = s * kST + qd * 32 + lane;  // buffer row (image / token order)
                 const uint32_t ta = tmem + (uint32_t(qd * 32) << 16) + uint32_t(s * kCols);
-                float vv[16], kv[16], ea[2];
+                float yv[16], vv[16], kv[16], ea[2];
+                tcu::tmem_ld16(ta, yv);
                 tcu::tmem_ld16(ta + 16, vv);
                 tcu::tmem_ld16(ta + 32, kv);
                 tcu::tmem_ld2(ta + 48, ea);
                 tcu::tmem_wait_ld();
-                if (i >= n) return;
-                const int t = ci.reversed ? n - 1 - i : i;  // pass-local scan index
-                const int64_t tok = (int64_t)c * ci.Lc + (int64_t)j * cap + t;
-                if (!kSpatial && tok >= p.L) {  // padding past the sequence end: a zero token
+                if (i < n) {
+                    const int t = ci.reversed ? n - 1 - i : i;  // pass-local scan index
+                    const int64_t tok = (int64_t)c * ci.Lc + (int64_t)j * cap + t;
+                    const bool real = kSpatial || tok < p.L;
+                    if (!real) {  // padding past the sequence end: a zero token (chunk.py:202-206)
 #pragma unroll
-                    for (int e = 0; e < kD; ++e) { vv[e] = 0.f; kv[e] = 0.f; }
-                    ea[0] = ea[1] = 0.f;
-                }
-                const float2 ga = token_gates(p.k, kv, vv, ea[0], ea[1]);
-                float* rkt = rk + t * kRec;
-                float* rdt = rd + t * kRec;
-#pragma unroll
-                for (int e = 0; e < kD; e += 4) {
-                    *reinterpret_cast<float4*>(rkt + e) = make_float4(kv[e], kv[e + 1], kv[e + 2], kv[e + 3]);
-                    *reinterpret_cast<float4*>(rdt + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
-                }
-                rea[t] = ga;
-            };
-            auto outputs_of = [&](int s) {
-                const int i = s * kST + qd * 32 + lane;
-                const uint32_t ta = tmem + (uint32_t(qd * 32) << 16) + uint32_t(s * kCols);
-                float yv[16];
-                tcu::tmem_ld16(ta, yv);
-                tcu::tmem_wait_ld();
-                if (i >= n) return;
-                const int t = ci.reversed ? n - 1 - i : i;
-                const int64_t tok = (int64_t)c * ci.Lc + (int64_t)j * cap + t;
-                if (!kSpatial && tok >= p.L) return;
-                float qv[16];
-                tile_row(qt, i, qv);
-                float qs = 0.f;
-#pragma unroll
-                for (int e = 0; e < kD; ++e) qs = fmaf(qv[e], qv[e], qs);
-                const float qinv = rsqrtf(fmaxf(qs, 1e-24f));  // 1 / max(||q||, 1e-12)
-                if (kSpatial) {
-                    float xv[16];
-                    tile_row(xt, i, xv);
-                    int pix;
-                    const int pos = start + i;  // position along this chunk's row / column
-                    if (g.layout == 0) {
-                        pix = ci.mapi == 0 ? (ci.dir == 0 ? c : p.H - 1 - c) * p.W + pos
-                                           : pos * p.W + (ci.dir == 2 ? c : p.W - 1 - c);
-                    } else {
-                        pix = scan_pixel(ci.dir, c, j * cap + t, p.H, p.W);
+                        for (int e = 0; e < kD; ++e) { vv[e] = 0.f; kv[e] = 0.f; }
+                        ea[0] = ea[1] = 0.f;
                     }
-                    float* op = plane + (int64_t)pix * p.C;
+                    const float2 ga = token_gates(p.k, kv, vv, ea[0], ea[1]);
+                    float* rkt = rk + t * kRec;
+                    float* rdt = rd + t * kRec;
 #pragma unroll
                     for (int e = 0; e < kD; e += 4) {
-                        float4 o;
-                        o.x = fw[e] * (yv[e] * qinv + fw[16 + e] * xv[e]);
-                        o.y = fw[e + 1] * (yv[e + 1] * qinv + fw[17 + e] * xv[e + 1]);
-                        o.z = fw[e + 2] * (yv[e + 2] * qinv + fw[18 + e] * xv[e + 2]);
-                        o.w = fw[e + 3] * (yv[e + 3] * qinv + fw[19 + e] * xv[e + 3]);
-                        *reinterpret_cast<float4*>(op + e) = o;
+                        *reinterpret_cast<float4*>(rkt + e) = make_float4(kv[e], kv[e + 1], kv[e + 2], kv[e + 3]);
+                        *reinterpret_cast<float4*>(rdt + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
                     }
-                } else {
-                    __nv_bfloat16* yo = static_cast<__nv_bfloat16*>(p.y) + ((int64_t)ci.chain * p.L + tok) * kD;
-                    uint32_t w[8];
+                    rea[t] = ga;
+                    if (real) {
+                        float qv[16];
+                        tile_row(qt, i, qv);
+                        float qs = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const __nv_bfloat162 h = __floats2bfloat162_rn(yv[2 * e] * qinv, yv[2 * e + 1] * qinv);
-                        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                        for (int e = 0; e < kD; ++e) qs = fmaf(qv[e], qv[e], qs);
+                        const float qinv = rsqrtf(fmaxf(qs, 1e-24f));  // 1 / max(||q||, 1e-12)
+                        if (kSpatial) {
+                            float xv[16];
+                            tile_row(xt, i, xv);
+                            int pix;
+                            const int pos = start + i;  // position along this chunk's row / column
+                            if (g.layout == 0) {
+                                pix = ci.mapi == 0 ? (ci.dir == 0 ? c : p.H - 1 - c) * p.W + pos
+                                                   : pos * p.W + (ci.dir == 2 ? c : p.W - 1 - c);
+                            } else {
+                                pix = scan_pixel(ci.dir, c, j * cap + t, p.H, p.W);
+                            }
+                            float* op = plane + (int64_t)pix * p.C;
+#pragma unroll
+                            for (int e = 0; e < kD; e += 4) {
+                                float4 o;
+                                o.x = fw[e] * (yv[e] * qinv + fw[16 + e] * xv[e]);
+                                o.y = fw[e + 1] * (yv[e + 1] * qinv + fw[17 + e] * xv[e + 1]);
+                                o.z = fw[e + 2] * (yv[e + 2] * qinv + fw[18 + e] * xv[e + 2]);
+                                o.w = fw[e + 3] * (yv[e + 3] * qinv + fw[19 + e] * xv[e + 3]);
+                                *reinterpret_cast<float4*>(op + e) = o;
+                            }
+                        } else {
+                            __nv_bfloat16* yo = static_cast<__nv_bfloat16*>(p.y) + ((int64_t)ci.chain * p.L + tok) * kD;
+                            uint32_t w[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const __nv_bfloat162 h = __floats2bfloat162_rn(yv[2 * e] * qinv, yv[2 * e + 1] * qinv);
+                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                            }
+                            reinterpret_cast<uint4*>(yo)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                            reinterpret_cast<uint4*>(yo)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        }
                     }
-                    reinterpret_cast<uint4*>(yo)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    reinterpret_cast<uint4*>(yo)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                }
-            };
-            if (n <= kST) {
-                if (warp < 4) gates_of(0);
-                else outputs_of(0);
-            } else {
-                for (int s = warp >> 2; s * kST < n; s += 2) {
-                    gates_of(s);
-                    outputs_of(s);
                 }
             }
             tcu::tc_fence_before_sync();
@@ -474,19 +452,10 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) x8[e] = ffma2(u2, k8[e], fmul2(a2, x8[e]));
                 }
-                float* sg = seg + warp * 512;
-                if (!qrow) {  // P row `lane` -> column `lane` of P^T (P^T[c][k] = P[k][c])
+                float* sr = seg + (warp * 32 + lane) * 16;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        sg[(2 * e) * 16 + lane] = x8[e].x;
-                        sg[(2 * e + 1) * 16 + lane] = x8[e].y;
-                    }
-                } else {  // Q row lane - 16, row-major
-                    float* qr = sg + 256 + (lane - 16) * 16;
-#pragma unroll
-                    for (int e = 0; e < 8; e += 2)
-                        *reinterpret_cast<float4*>(qr + 2 * e) = make_float4(x8[e].x, x8[e].y, x8[e + 1].x, x8[e + 1].y);
-                }
+                for (int e = 0; e < 8; e += 2)
+                    *reinterpret_cast<float4*>(sr + 2 * e) = make_float4(x8[e].x, x8[e].y, x8[e + 1].x, x8[e + 1].y);
             }
             __syncthreads();
 
@@ -496,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
                 float gv;
                 int s0;
                 if (j == 0) {  // G enters the chunk as I:  G = P_0 + Q_0
-                    gv = seg[cc * 16 + r] + seg[256 + r * 16 + cc];
+                    gv = seg[r * 16 + cc] + seg[(16 + r) * 16 + cc];
                     s0 = 1;
                 } else {
                     gv = gb[r * 16 + cc];  // carried from the previous pass (buffer 0)
@@ -507,18 +476,10 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
                     float* gcur = gb + ph * 256;
                     gcur[r * 16 + cc] = gv;
                     __syncthreads();
-                    const float* ps = seg + s * 512;
-                    const float4* grow = reinterpret_cast<const float4*>(gcur + r * 16);
-                    const float4* pcol = reinterpret_cast<const float4*>(ps + cc * 16);  // column cc of P_s
-                    float acc = ps[256 + r * 16 + cc];
+                    const float* ps = seg + s * 32 * 16;
+                    float acc = ps[(16 + r) * 16 + cc];
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        const float4 a = grow[v], b = pcol[v];
-                        acc = fmaf(a.x, b.x, acc);
-                        acc = fmaf(a.y, b.y, acc);
-                        acc = fmaf(a.z, b.z, acc);
-                        acc = fmaf(a.w, b.w, acc);
-                    }
+                    for (int k = 0; k < 16; ++k) acc = fmaf(gcur[r * 16 + k], ps[k * 16 + cc], acc);
                     gv = acc;
                     ph ^= 1;
                 }
