@@ -378,9 +378,13 @@ _flush = {}
 
 
 def l2_flush(device):
-    if device not in _flush:
-        _flush[device] = L2Flush(device)
-    return _flush[device]
+    """The L2Flush of `device` (one pair of buffers per GPU, however the device is named)."""
+    key = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    if key.index is None:
+        key = torch.device("cuda", torch.cuda.current_device())
+    if key not in _flush:
+        _flush[key] = L2Flush(key)
+    return _flush[key]
 
 
 def _event_ms(fn, iters, flush=None):

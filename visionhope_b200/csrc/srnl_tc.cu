@@ -63,7 +63,6 @@ struct TcMaps {
 
 // Launch-wide tile geometry (uniform over the chains of one launch).
 struct TcGeom {
-    int map_rank;     // 3 (sequence: [16 | C, L, chains]) or 4 (image / serialized scans)
     int layout;       // 0 image (remap), 1 serialized scans [B, 4, L, C], 2 packed sequence
     int box_rows;     // tokens per TMA box along rows / token order
     int box_cols;     // tokens per TMA box along columns
@@ -92,13 +91,6 @@ struct TcSmem {
 __device__ unsigned int g_tc_status;  // non-zero once a bounded wait gave up (cleared on read)
 
 __device__ __forceinline__ int swz32(int row, int half) { return row * 32 + ((half ^ ((row >> 2) & 1)) << 4); }
-
-// bf16 bits of element k of a 16-wide swizzled row.
-__device__ __forceinline__ float tile_elem(const unsigned char* tile, int row, int k) {
-    const __nv_bfloat16 h =
-        *reinterpret_cast<const __nv_bfloat16*>(tile + swz32(row, k >> 3) + (k & 7) * 2);
-    return __bfloat162float(h);
-}
 
 __device__ __forceinline__ void tile_row(const unsigned char* tile, int row, float (&v)[16]) {
 #pragma unroll
@@ -633,7 +625,6 @@ int run_tc_spatial(const ScanParams& p, int io_dtype, cudaStream_t st) {
     const int C = p.C;
     if (p.remap) {
         g.layout = 0;
-        g.map_rank = 4;
         g.box_rows = box_for(p.W, p.W);
         g.box_cols = box_for(p.H, p.H);
         const cuuint64_t xd[4] = {(cuuint64_t)C, (cuuint64_t)p.W, (cuuint64_t)p.H, (cuuint64_t)p.B};
@@ -646,7 +637,6 @@ int run_tc_spatial(const ScanParams& p, int io_dtype, cudaStream_t st) {
             return fail(VH_E_DEVICE, "srnl tc scan: tensor map encoding failed");
     } else {
         g.layout = 1;
-        g.map_rank = 4;
         g.box_rows = g.box_cols = box_for(std::max(p.W, p.H), p.L);
         // rows use chunks of W, columns chunks of H: one box size serves both when it covers
         // the longer one in at most two boxes per pass
@@ -677,7 +667,6 @@ int run_tc_sequence(const ScanParams& p, cudaStream_t st) {
     TcMaps maps{};
     TcGeom g{};
     g.layout = 2;
-    g.map_rank = 3;
     int maxc = 1;
     for (int r = 0; r < p.R; ++r) maxc = std::max(maxc, p.chunk[r]);
     g.box_rows = g.box_cols = box_for(maxc, p.L);
