@@ -33,6 +33,11 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
     return bits_f2(d);
 }
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
 __device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
 
 }  // namespace vh

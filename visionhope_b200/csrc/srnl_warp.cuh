@@ -15,9 +15,10 @@
 //       - k~ = M_k x, v = M_v x and M_m q_raw run as bf16 m16n8k16 tensor-core MMAs against
 //         the three-way bf16 split of the fp32 memories (fp32 accumulate, 24-bit operands);
 //         y = (M_m q_raw) / ||q_raw|| (models/srnl_core/csrc/inference_recurrence.cuh:40-60);
-//       - each token's own lane finishes the key norm, the eta/alpha gates, the injection
-//         cap and the spectral clamp in-thread (inference_recurrence.cuh:60-90,
-//         memory.cuh:219-233), and k_t . k_{t+1} for the lookahead below.
+//       - each token's own lane (a lane pair, in steps of at most 16 tokens) finishes the key
+//         norm, the eta/alpha gates, the injection cap and the spectral clamp
+//         (inference_recurrence.cuh:60-90, memory.cuh:219-233), and k_t . k_{t+1} for the
+//         lookahead below.
 //   P2  the gain recurrence r_t = (k_t - v_t) + G k_t, G <- alpha_t G - eta_t r_t k_t^T
 //       (inference_recurrence.cuh:92-106), two lanes per row of G, eight columns each.
 //       r_{t+1} is formed as d_{t+1} + alpha_t (G k_{t+1}) - u_t (k_t . k_{t+1}) with
@@ -97,16 +98,16 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
 
 // Exact three-way bf16 split of a pair of fp32 values by truncation: part k packs (lo, hi) of
 // the top 8 significant bits left after parts 0..k-1, so x = part0 + part1 + part2 exactly.
-// A part is the upper half of an fp32 word, so one byte permute packs a pair.
+// A part is the upper half of an fp32 word, so one byte permute packs a pair, and one packed
+// subtraction (exact: it only clears the leading bits) removes it from both values.
 __device__ __forceinline__ void split3(float lo, float hi, uint32_t (&parts)[kSplits]) {
+    float2 v = make_float2(lo, hi);
 #pragma unroll
     for (int k = 0; k < kSplits; ++k) {
-        const uint32_t ul = __float_as_uint(lo), uh = __float_as_uint(hi);
+        const uint32_t ul = __float_as_uint(v.x), uh = __float_as_uint(v.y);
         parts[k] = __byte_perm(ul, uh, 0x7632);
-        if (k + 1 < kSplits) {
-            lo -= __uint_as_float(ul & 0xffff0000u);
-            hi -= __uint_as_float(uh & 0xffff0000u);
-        }
+        if (k + 1 < kSplits)
+            v = fsub2(v, make_float2(__uint_as_float(ul & 0xffff0000u), __uint_as_float(uh & 0xffff0000u)));
     }
 }
 
@@ -221,6 +222,88 @@ __device__ __forceinline__ void gain_step(const CS& cs, int count, int row, int 
         case 14: gain_pass<14>(cs, count, row, half, g); break;
         case 7: gain_pass<7>(cs, count, row, half, g); break;
         default: gain_pass<0>(cs, count, row, half, g);
+    }
+}
+
+// The scalar gates of one token from (x.e, x.a), ||k||^2 after normalization and ||k - v||^2:
+// eta = step_scale softplus(x.e), alpha = min_ret + (1 - min_ret) sigmoid(x.a + bias), the
+// injection cap and the spectral clamp (inference_recurrence.cuh:60-90, memory.cuh:219-233).
+// The reference builds these kernels with --use_fast_math (models/srnl_core/fused.py:78,
+// chunk.py:121), so the exponentials, logarithm, divisions and square root use the
+// approximate hardware forms here too; expm1f and the clamp's nextafterf stay exact.
+__device__ __forceinline__ float2 token_gates(const ScanParams& p, float2 raw, float ke, float dns) {
+    const float ep = fminf(10.f, fmaxf(-10.f, raw.x));
+    const float ap = fminf(10.f, fmaxf(-10.f, raw.y + p.k.retention_bias));
+    const float eta = p.k.step_scale * (ep > 20.f ? ep : __logf(1.f + __expf(ep)));
+    const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * __fdividef(1.f, 1.f + __expf(-ap));
+    const float dsq = dns + 1e-12f;
+    const float dn = dsq * rsqrtf(dsq);
+    const float cap = __fdividef(p.k.injection_margin * (1.f - alpha), dn + 1e-6f);
+    float eff = cap * (-expm1f(-__fdividef(eta, cap)));
+    if (p.k.spectral_clamp) {
+        const float lim = nextafterf(__fdividef(p.k.spectral_factor * alpha, fmaxf(ke, 1e-20f)), 0.f);
+        eff = fminf(eff, lim);
+    }
+    return make_float2(eff, alpha);
+}
+
+// Gates of a step of at most 16 tokens, two lanes per token: lane (t, hf) holds channels
+// 8 hf .. 8 hf + 7 of token t, and the pair combines its partial sums with one shuffle.
+// k_t . k_{t+1} for the lookahead of the gain recurrence comes from the raw keys in the same
+// pass: (k~_t . k~_{t+1}) / (||k~_t|| ||k~_{t+1}||).
+template <class CS>
+__device__ __forceinline__ void gates_two_lane(CS& cs, const ScanParams& p, int count, int lane) {
+    const int t = lane & 15, hf = lane >> 4;
+    const bool live = t < count, nxt = t + 1 < count;
+    const int tt = live ? t : 0, tn = nxt ? t + 1 : 0;
+    float2 k[4], v[4], kn[4];
+    {
+        const float4 a0 = *reinterpret_cast<const float4*>(&cs.kt[tt][8 * hf]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&cs.kt[tt][8 * hf + 4]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&cs.dt[tt][8 * hf]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&cs.dt[tt][8 * hf + 4]);
+        const float4 c0 = *reinterpret_cast<const float4*>(&cs.kt[tn][8 * hf]);
+        const float4 c1 = *reinterpret_cast<const float4*>(&cs.kt[tn][8 * hf + 4]);
+        k[0] = make_float2(a0.x, a0.y); k[1] = make_float2(a0.z, a0.w);
+        k[2] = make_float2(a1.x, a1.y); k[3] = make_float2(a1.z, a1.w);
+        v[0] = make_float2(b0.x, b0.y); v[1] = make_float2(b0.z, b0.w);
+        v[2] = make_float2(b1.x, b1.y); v[3] = make_float2(b1.z, b1.w);
+        kn[0] = make_float2(c0.x, c0.y); kn[1] = make_float2(c0.z, c0.w);
+        kn[2] = make_float2(c1.x, c1.y); kn[3] = make_float2(c1.z, c1.w);
+    }
+    const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[tt]);
+    __syncwarp();  // every raw row is read before any lane overwrites its own
+    float2 skk = fmul2(k[0], k[0]), snn = fmul2(kn[0], kn[0]), skn = fmul2(k[0], kn[0]);
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+        skk = ffma2(k[i], k[i], skk);
+        snn = ffma2(kn[i], kn[i], snn);
+        skn = ffma2(k[i], kn[i], skn);
+    }
+    float ss = skk.x + skk.y, sn = snn.x + snn.y, sx = skn.x + skn.y;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+    sn += __shfl_xor_sync(0xffffffffu, sn, 16);
+    sx += __shfl_xor_sync(0xffffffffu, sx, 16);
+    const float kinv = rsqrtf(ss + 1e-6f), kinvn = rsqrtf(sn + 1e-6f);
+    const float2 kinv2 = splat2(kinv);
+    float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        k[i] = fmul2(k[i], kinv2);
+        v[i] = fadd2(k[i], make_float2(-v[i].x, -v[i].y));  // d = k - v
+        ke2 = ffma2(k[i], k[i], ke2);
+        dn2 = ffma2(v[i], v[i], dn2);
+    }
+    float ke = ke2.x + ke2.y, dns = dn2.x + dn2.y;
+    ke += __shfl_xor_sync(0xffffffffu, ke, 16);
+    dns += __shfl_xor_sync(0xffffffffu, dns, 16);
+    if (live) {
+        *reinterpret_cast<float4*>(&cs.kt[t][8 * hf]) = make_float4(k[0].x, k[0].y, k[1].x, k[1].y);
+        *reinterpret_cast<float4*>(&cs.kt[t][8 * hf + 4]) = make_float4(k[2].x, k[2].y, k[3].x, k[3].y);
+        *reinterpret_cast<float4*>(&cs.dt[t][8 * hf]) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+        *reinterpret_cast<float4*>(&cs.dt[t][8 * hf + 4]) = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
+        const float2 g = token_gates(p, raw, ke, dns);
+        if (hf == 0) cs.gate[t] = make_float4(g.x, g.y, nxt ? sx * kinv * kinvn : 0.f, 0.f);
     }
 }
 
@@ -409,65 +492,61 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmemT<TILE>
             if (j + 1 < tpc) prefetch(c, j + 1);
             else if (c + 1 < nchunks) prefetch(c + 1, 0);
 
-            // ------------------ P1: per-token gates (one lane per token) ---------------------
-            float2 kr[kD / 2];
-            if (lane < count) {
-                float2 vv[kD / 2];
+            // ------------------ P1: per-token gates ------------------------------------------
+            if constexpr (TILE == 16) {  // two lanes per token
+                gates_two_lane(cs, p, count, lane);
+                __syncwarp();
+            } else {  // one lane per token
+                float2 kr[kD / 2];
+                if (lane < count) {
+                    float2 vv[kD / 2];
 #pragma unroll
-                for (int i = 0; i < kD; i += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane][i]);
-                    const float4 v4 = *reinterpret_cast<const float4*>(&cs.dt[lane][i]);
-                    kr[i / 2] = make_float2(k4.x, k4.y);
-                    kr[i / 2 + 1] = make_float2(k4.z, k4.w);
-                    vv[i / 2] = make_float2(v4.x, v4.y);
-                    vv[i / 2 + 1] = make_float2(v4.z, v4.w);
-                }
-                float2 kn2 = fmul2(kr[0], kr[0]);
+                    for (int i = 0; i < kD; i += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane][i]);
+                        const float4 v4 = *reinterpret_cast<const float4*>(&cs.dt[lane][i]);
+                        kr[i / 2] = make_float2(k4.x, k4.y);
+                        kr[i / 2 + 1] = make_float2(k4.z, k4.w);
+                        vv[i / 2] = make_float2(v4.x, v4.y);
+                        vv[i / 2 + 1] = make_float2(v4.z, v4.w);
+                    }
+                    float2 kn2 = fmul2(kr[0], kr[0]);
 #pragma unroll
-                for (int i = 1; i < kD / 2; ++i) kn2 = ffma2(kr[i], kr[i], kn2);
-                const float kinv = 1.f / sqrtf((kn2.x + kn2.y) + 1e-6f);
-                const float2 kinv2 = splat2(kinv);
-                float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
+                    for (int i = 1; i < kD / 2; ++i) kn2 = ffma2(kr[i], kr[i], kn2);
+                    const float kinv = rsqrtf((kn2.x + kn2.y) + 1e-6f);
+                    const float2 kinv2 = splat2(kinv);
+                    float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
 #pragma unroll
-                for (int i = 0; i < kD / 2; ++i) {
-                    kr[i] = fmul2(kr[i], kinv2);
-                    vv[i] = fadd2(kr[i], make_float2(-vv[i].x, -vv[i].y));  // d = k - v
-                    ke2 = ffma2(kr[i], kr[i], ke2);
-                    dn2 = ffma2(vv[i], vv[i], dn2);
-                }
+                    for (int i = 0; i < kD / 2; ++i) {
+                        kr[i] = fmul2(kr[i], kinv2);
+                        vv[i] = fadd2(kr[i], make_float2(-vv[i].x, -vv[i].y));  // d = k - v
+                        ke2 = ffma2(kr[i], kr[i], ke2);
+                        dn2 = ffma2(vv[i], vv[i], dn2);
+                    }
 #pragma unroll
-                for (int i = 0; i < kD; i += 4) {
-                    *reinterpret_cast<float4*>(&cs.kt[lane][i]) = make_float4(kr[i / 2].x, kr[i / 2].y, kr[i / 2 + 1].x, kr[i / 2 + 1].y);
-                    *reinterpret_cast<float4*>(&cs.dt[lane][i]) = make_float4(vv[i / 2].x, vv[i / 2].y, vv[i / 2 + 1].x, vv[i / 2 + 1].y);
+                    for (int i = 0; i < kD; i += 4) {
+                        *reinterpret_cast<float4*>(&cs.kt[lane][i]) = make_float4(kr[i / 2].x, kr[i / 2].y, kr[i / 2 + 1].x, kr[i / 2 + 1].y);
+                        *reinterpret_cast<float4*>(&cs.dt[lane][i]) = make_float4(vv[i / 2].x, vv[i / 2].y, vv[i / 2 + 1].x, vv[i / 2 + 1].y);
+                    }
+                    const float ke = ke2.x + ke2.y;
+                    const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[lane]);
+                    const float2 gg = token_gates(p, raw, ke, dn2.x + dn2.y);
+                    const float eff = gg.x, alpha = gg.y;
+                    *reinterpret_cast<float2*>(&cs.gate[lane]) = make_float2(eff, alpha);
                 }
-                const float ke = ke2.x + ke2.y;
-                const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[lane]);
-                const float ep = fminf(10.f, fmaxf(-10.f, raw.x));
-                const float ap = fminf(10.f, fmaxf(-10.f, raw.y + p.k.retention_bias));
-                const float eta = p.k.step_scale * softplus_f(ep);
-                const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
-                const float dn = sqrtf((dn2.x + dn2.y) + 1e-12f);
-                const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
-                float eff = cap * (-expm1f(-(eta / cap)));
-                if (p.k.spectral_clamp) {
-                    const float lim = nextafterf(p.k.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f);
-                    eff = fminf(eff, lim);
-                }
-                *reinterpret_cast<float2*>(&cs.gate[lane]) = make_float2(eff, alpha);
-            }
-            __syncwarp();
-            if (lane + 1 < count) {  // k_t . k_{t+1} for the lookahead of the gain recurrence
-                float2 kk2 = splat2(0.f);
+                __syncwarp();
+                if (lane + 1 < count) {  // k_t . k_{t+1} for the lookahead of the gain recurrence
+                    float2 kk2 = splat2(0.f);
 #pragma unroll
-                for (int i = 0; i < kD; i += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane + 1][i]);
-                    kk2 = ffma2(kr[i / 2], make_float2(k4.x, k4.y), kk2);
-                    kk2 = ffma2(kr[i / 2 + 1], make_float2(k4.z, k4.w), kk2);
+                    for (int i = 0; i < kD; i += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(&cs.kt[lane + 1][i]);
+                        kk2 = ffma2(kr[i / 2], make_float2(k4.x, k4.y), kk2);
+                        kk2 = ffma2(kr[i / 2 + 1], make_float2(k4.z, k4.w), kk2);
+                    }
+                    cs.gate[lane].z = kk2.x + kk2.y;
                 }
-                cs.gate[lane].z = kk2.x + kk2.y;
-            }
 
-            __syncwarp();
+                __syncwarp();
+            }
 
             // ------------------ P2: gain recurrence ---------------------------------------------
             gain_step(cs, count, p2_row, p2_half, g8);
@@ -514,6 +593,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmemT<TILE>
             for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
+                    if (mt == 3 && h == 1) break;  // rows 56-63 are zero and stay zero
                     const int r = mt * 16 + qg + 8 * h;
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
