@@ -173,8 +173,34 @@ struct RowReg {
     }
 };
 
-// softplus as the reference writes it (models/srnl_core/csrc/inference_recurrence.cuh:74).
-__device__ __forceinline__ float softplus_f(float p) { return p > 20.f ? p : logf(1.f + expf(p)); }
+// The per-token gate arithmetic of every scan.  The reference builds its recurrence kernels
+// with --use_fast_math (models/srnl_core/fused.py:78, chunk.py:121), so the exponentials,
+// the logarithm, the divisions and the square roots use the approximate hardware forms here
+// too; expm1f and the clamp's nextafterf stay exact.
+
+// 1 / sqrt(||k~||^2 + 1e-6), the key normalization (inference_recurrence.cuh:60-66).
+__device__ __forceinline__ float key_inv_norm(float kn2) { return rsqrtf(kn2 + 1e-6f); }
+
+// (eta_eff, alpha) of one token from x.e and x.a (before clamping), ke = ||k||^2 of the
+// normalized key and dn2 = ||k - v||^2: eta = step_scale softplus(x.e) (softplus as the
+// reference writes it, log(1 + exp(p)), inference_recurrence.cuh:74), alpha = min_ret +
+// (1 - min_ret) sigmoid(x.a + bias), the injection cap and the spectral clamp
+// (inference_recurrence.cuh:66-90, memory.cuh:219-233).
+__device__ __forceinline__ float2 token_gate_scalars(const SrnlConsts& K, float xe, float xa, float ke, float dn2) {
+    const float ep = fminf(10.f, fmaxf(-10.f, xe));
+    const float ap = fminf(10.f, fmaxf(-10.f, xa + K.retention_bias));
+    const float eta = K.step_scale * (ep > 20.f ? ep : __logf(1.f + __expf(ep)));
+    const float alpha = K.min_retention + (1.f - K.min_retention) * __fdividef(1.f, 1.f + __expf(-ap));
+    const float dsq = dn2 + 1e-12f;
+    const float dn = dsq * rsqrtf(dsq);
+    const float cap = __fdividef(K.injection_margin * (1.f - alpha), dn + 1e-6f);
+    float eff = cap * (-expm1f(-__fdividef(eta, cap)));
+    if (K.spectral_clamp) {
+        const float lim = nextafterf(__fdividef(K.spectral_factor * alpha, fmaxf(ke, 1e-20f)), 0.f);
+        eff = fminf(eff, lim);
+    }
+    return make_float2(eff, alpha);
+}
 
 // ---- tensor-core helpers (bf16 m16n8k16, fp32 accumulate) ------------------------------
 // Rows of 16 bf16 (32 bytes) are stored with their two 16-byte halves swapped on rows whose
@@ -508,7 +534,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
                 }
 #pragma unroll
                 for (int i = 0; i < D; ++i) kn = fmaf(kr[i], kr[i], kn);
-                const float kinv = 1.f / sqrtf(kn + 1e-6f);
+                const float kinv = key_inv_norm(kn);
                 float ke = 0.f, dn2 = 0.f, ep = 0.f, ap = 0.f;
                 const float* ev = Sc + 3 * D * SP;
                 const float* avp = Sc + (3 * D + 1) * SP;
@@ -528,17 +554,8 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
                     *reinterpret_cast<float4*>(krow + i) = make_float4(kr[i], kr[i + 1], kr[i + 2], kr[i + 3]);
                     *reinterpret_cast<float4*>(drow + i) = make_float4(vv[i], vv[i + 1], vv[i + 2], vv[i + 3]);
                 }
-                ep = fminf(10.f, fmaxf(-10.f, ep));
-                ap = fminf(10.f, fmaxf(-10.f, ap + p.k.retention_bias));
-                const float eta = p.k.step_scale * softplus_f(ep);
-                const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
-                const float dn = sqrtf(dn2 + 1e-12f);
-                const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
-                float eff = cap * (-expm1f(-(eta / cap)));
-                if (p.k.spectral_clamp) {
-                    const float lim = nextafterf(p.k.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f);
-                    eff = fminf(eff, lim);
-                }
+                const float2 gg = token_gate_scalars(p.k, ep, ap, ke, dn2);
+                const float eff = gg.x, alpha = gg.y;
                 EFF[tid] = eff;
                 ALP[tid] = alpha;
             }
@@ -628,7 +645,7 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
                 vv[i] = av0 + av1;
                 kn = fmaf(kr[i], kr[i], kn);
             }
-            const float kinv = 1.f / sqrtf(kn + 1e-6f);
+            const float kinv = key_inv_norm(kn);
             float ke = 0.f, dn2 = 0.f, ep = 0.f, ap = 0.f;
             const float* ev = Sc + 3 * D * SP;
             const float* avp = Sc + (3 * D + 1) * SP;
@@ -648,17 +665,8 @@ __global__ void __launch_bounds__(kScanThreads, 4) srnl_scan_kernel(const ScanPa
                 *reinterpret_cast<float4*>(Kt + (size_t)row * SP + i) = make_float4(kr[i], kr[i + 1], kr[i + 2], kr[i + 3]);
                 *reinterpret_cast<float4*>(Dt + (size_t)row * SP + i) = make_float4(vv[i], vv[i + 1], vv[i + 2], vv[i + 3]);
             }
-            ep = fminf(10.f, fmaxf(-10.f, ep));
-            ap = fminf(10.f, fmaxf(-10.f, ap + p.k.retention_bias));
-            const float eta = p.k.step_scale * softplus_f(ep);
-            const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * (1.f / (1.f + expf(-ap)));
-            const float dn = sqrtf(dn2 + 1e-12f);
-            const float cap = p.k.injection_margin * (1.f - alpha) / (dn + 1e-6f);
-            float eff = cap * (-expm1f(-(eta / cap)));
-            if (p.k.spectral_clamp) {
-                const float lim = nextafterf(p.k.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f);
-                eff = fminf(eff, lim);
-            }
+            const float2 gg = token_gate_scalars(p.k, ep, ap, ke, dn2);
+            const float eff = gg.x, alpha = gg.y;
             EFF[row] = eff;
             ALP[row] = alpha;
         }

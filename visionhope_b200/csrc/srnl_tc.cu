@@ -200,7 +200,7 @@ __device__ __forceinline__ float2 token_gates(const SrnlConsts& K, float (&kt)[1
     float kn2 = 0.f;
 #pragma unroll
     for (int i = 0; i < kD; ++i) kn2 = fmaf(kt[i], kt[i], kn2);
-    const float kinv = 1.f / sqrtf(kn2 + 1e-6f);
+    const float kinv = key_inv_norm(kn2);
     float ke = 0.f, dn2 = 0.f;
 #pragma unroll
     for (int i = 0; i < kD; ++i) {
@@ -209,15 +209,7 @@ __device__ __forceinline__ float2 token_gates(const SrnlConsts& K, float (&kt)[1
         ke = fmaf(kt[i], kt[i], ke);
         dn2 = fmaf(v[i], v[i], dn2);
     }
-    const float ep = fminf(10.f, fmaxf(-10.f, xe));
-    const float ap = fminf(10.f, fmaxf(-10.f, xa + K.retention_bias));
-    const float eta = K.step_scale * softplus_f(ep);
-    const float alpha = K.min_retention + (1.f - K.min_retention) * (1.f / (1.f + expf(-ap)));
-    const float dn = sqrtf(dn2 + 1e-12f);
-    const float cap = K.injection_margin * (1.f - alpha) / (dn + 1e-6f);
-    float eff = cap * (-expm1f(-(eta / cap)));
-    if (K.spectral_clamp) eff = fminf(eff, nextafterf(K.spectral_factor * alpha / fmaxf(ke, 1e-20f), 0.f));
-    return make_float2(eff, alpha);
+    return token_gate_scalars(K, xe, xa, ke, dn2);
 }
 
 template <int NST, bool kSpatial>

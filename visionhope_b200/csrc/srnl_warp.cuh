@@ -225,28 +225,6 @@ __device__ __forceinline__ void gain_step(const CS& cs, int count, int row, int 
     }
 }
 
-// The scalar gates of one token from (x.e, x.a), ||k||^2 after normalization and ||k - v||^2:
-// eta = step_scale softplus(x.e), alpha = min_ret + (1 - min_ret) sigmoid(x.a + bias), the
-// injection cap and the spectral clamp (inference_recurrence.cuh:60-90, memory.cuh:219-233).
-// The reference builds these kernels with --use_fast_math (models/srnl_core/fused.py:78,
-// chunk.py:121), so the exponentials, logarithm, divisions and square root use the
-// approximate hardware forms here too; expm1f and the clamp's nextafterf stay exact.
-__device__ __forceinline__ float2 token_gates(const ScanParams& p, float2 raw, float ke, float dns) {
-    const float ep = fminf(10.f, fmaxf(-10.f, raw.x));
-    const float ap = fminf(10.f, fmaxf(-10.f, raw.y + p.k.retention_bias));
-    const float eta = p.k.step_scale * (ep > 20.f ? ep : __logf(1.f + __expf(ep)));
-    const float alpha = p.k.min_retention + (1.f - p.k.min_retention) * __fdividef(1.f, 1.f + __expf(-ap));
-    const float dsq = dns + 1e-12f;
-    const float dn = dsq * rsqrtf(dsq);
-    const float cap = __fdividef(p.k.injection_margin * (1.f - alpha), dn + 1e-6f);
-    float eff = cap * (-expm1f(-__fdividef(eta, cap)));
-    if (p.k.spectral_clamp) {
-        const float lim = nextafterf(__fdividef(p.k.spectral_factor * alpha, fmaxf(ke, 1e-20f)), 0.f);
-        eff = fminf(eff, lim);
-    }
-    return make_float2(eff, alpha);
-}
-
 // Gates of a step of at most 16 tokens, two lanes per token: lane (t, hf) holds channels
 // 8 hf .. 8 hf + 7 of token t, and the pair combines its partial sums with one shuffle.
 // k_t . k_{t+1} for the lookahead of the gain recurrence comes from the raw keys in the same
@@ -284,7 +262,7 @@ __device__ __forceinline__ void gates_two_lane(CS& cs, const ScanParams& p, int 
     ss += __shfl_xor_sync(0xffffffffu, ss, 16);
     sn += __shfl_xor_sync(0xffffffffu, sn, 16);
     sx += __shfl_xor_sync(0xffffffffu, sx, 16);
-    const float kinv = rsqrtf(ss + 1e-6f), kinvn = rsqrtf(sn + 1e-6f);
+    const float kinv = key_inv_norm(ss), kinvn = key_inv_norm(sn);
     const float2 kinv2 = splat2(kinv);
     float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
 #pragma unroll
@@ -302,7 +280,7 @@ __device__ __forceinline__ void gates_two_lane(CS& cs, const ScanParams& p, int 
         *reinterpret_cast<float4*>(&cs.kt[t][8 * hf + 4]) = make_float4(k[2].x, k[2].y, k[3].x, k[3].y);
         *reinterpret_cast<float4*>(&cs.dt[t][8 * hf]) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
         *reinterpret_cast<float4*>(&cs.dt[t][8 * hf + 4]) = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
-        const float2 g = token_gates(p, raw, ke, dns);
+        const float2 g = token_gate_scalars(p.k, raw.x, raw.y, ke, dns);
         if (hf == 0) cs.gate[t] = make_float4(g.x, g.y, nxt ? sx * kinv * kinvn : 0.f, 0.f);
     }
 }
@@ -512,7 +490,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmemT<TILE>
                     float2 kn2 = fmul2(kr[0], kr[0]);
 #pragma unroll
                     for (int i = 1; i < kD / 2; ++i) kn2 = ffma2(kr[i], kr[i], kn2);
-                    const float kinv = rsqrtf((kn2.x + kn2.y) + 1e-6f);
+                    const float kinv = key_inv_norm(kn2.x + kn2.y);
                     const float2 kinv2 = splat2(kinv);
                     float2 ke2 = splat2(0.f), dn2 = splat2(0.f);
 #pragma unroll
@@ -529,7 +507,7 @@ __device__ __forceinline__ void scan_chain(const ScanParams& p, ChainSmemT<TILE>
                     }
                     const float ke = ke2.x + ke2.y;
                     const float2 raw = *reinterpret_cast<const float2*>(&cs.gate[lane]);
-                    const float2 gg = token_gates(p, raw, ke, dn2.x + dn2.y);
+                    const float2 gg = token_gate_scalars(p.k, raw.x, raw.y, ke, dn2.x + dn2.y);
                     const float eff = gg.x, alpha = gg.y;
                     *reinterpret_cast<float2*>(&cs.gate[lane]) = make_float2(eff, alpha);
                 }
