@@ -411,7 +411,10 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
             __syncthreads();  // records complete; TMEM and this buffer's tiles are free
 
             // ---- P2a: segment transitions [P; Q], one warp per segment, one lane per row --------
-            const int seg_len = max(16, (n + kWarps - 1) / kWarps);
+            // Passes of at most 128 tokens run at most four segments: the recurrence saturates
+            // the FP32 pipe once eight warps share an SM (about 147 against 96 cycles per token
+            // per warp with four), and each segment adds one step to the composition below.
+            const int seg_len = n <= 128 ? max(16, (n + 3) / 4) : (n + kWarps - 1) / kWarps;
             const int nseg = (n + seg_len - 1) / seg_len;
             if (warp < nseg) {
                 const int t0 = warp * seg_len, t1 = min(n, t0 + seg_len);
@@ -420,7 +423,10 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
                 for (int e = 0; e < 8; ++e)
                     x8[e] = make_float2(lane == 2 * e ? 1.f : 0.f, lane == 2 * e + 1 ? 1.f : 0.f);
                 const bool qrow = lane >= 16;
-                for (int t = t0; t < t1; ++t) {
+                // One token of the segment; blocks of 16 tokens run fully unrolled, so the next
+                // tokens' key loads issue ahead of the current update (measured on B200, dense
+                // stage 1: 2.84 against 3.27 ms with the plain loop).
+                auto step = [&](int t) {
                     const float4* kr = reinterpret_cast<const float4*>(rk + t * kRec);
                     const float4 k0 = kr[0], k1 = kr[1], k2 = kr[2], k3 = kr[3];
                     const float2 k8[8] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w), make_float2(k1.x, k1.y),
@@ -435,7 +441,13 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
                     const float2 a2 = splat2(ga.y), u2 = splat2(u);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) x8[e] = ffma2(u2, k8[e], fmul2(a2, x8[e]));
+                };
+                int t = t0;
+                for (; t + 16 <= t1; t += 16) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) step(t + i);
                 }
+                for (; t < t1; ++t) step(t);
                 float* sr = seg + (warp * 32 + lane) * 16;
 #pragma unroll
                 for (int e = 0; e < 8; e += 2)
