@@ -132,26 +132,34 @@ bool tc_applicable(const ScanParams& p, bool spatial);
 int run_tc_spatial(const ScanParams& p, int io_dtype, cudaStream_t st);
 int run_tc_sequence(const ScanParams& p, cudaStream_t st);
 
-// Which D = 16 bf16 scan runs: the chunk-parallel tensor-core scan gives each chain a whole
-// CTA, which pays when a launch has too few chains to fill the GPU with one warp per chain;
-// the warp-per-chain scan wins when chains are plentiful.  Measured on B200 (bf16, image
-// layout): 24 chains of 128 x 512 tokens 3.36 against 6.89 ms, 48 chains of 64 x 256 1.21
-// against 1.65 ms, but 112 chains of 32 x 128 0.54 against 0.45 ms -- so the tensor-core scan
-// runs up to a third of an SM per chain.  VH_SRNL_SCAN=tc or =warp forces one of them (where
-// it applies).
-inline bool use_tc_scan(const ScanParams& p, bool spatial, int chains) {
+// Which D = 16 bf16 scan runs.  The chunk-parallel tensor-core scan gives each chain a whole
+// CTA (two per SM for chunks of up to 256 tokens, one above) and runs a chunk's tokens in
+// parallel, at a fixed cost per chunk; the warp-per-chain scan runs one token after the other
+// and wins when chains are plentiful or chunks short.  Measured on B200 (bf16, image layout,
+// tensor-core against warp scan, ms):
+//   chunks of 56+ tokens: 24 chains of 128 x 512 2.28 / 6.46; 64, 128 and 256 chains of
+//     56 x 56 0.21 / 0.32, 0.21 / 0.33, 0.27 / 0.33; 112 chains of 32 x 128 0.41 / 0.42;
+//     160 chains of 16 x 64 0.218 / 0.220;
+//   chunks of 14 and 28 tokens: 128 chains of 14 x 14 0.056 / 0.040, 256 chains of 28 x 28
+//     0.122 / 0.097; 2048+ chains at every VisionHOPE-T stage, several times slower.
+// So the tensor-core scan runs for chunks of 48+ tokens while every chain has a CTA slot in the
+// first wave, and for shorter chunks only up to a third of an SM per chain.  VH_SRNL_SCAN=tc or
+// =warp forces one of them (where it applies).
+inline bool use_tc_scan(const ScanParams& p, bool spatial, int chains, int max_chunk) {
     const char* env = std::getenv("VH_SRNL_SCAN");
     if (env && std::strcmp(env, "warp") == 0) return false;
     if (!tc_applicable(p, spatial)) return false;
     if (env && std::strcmp(env, "tc") == 0) return true;
-    return 3 * chains <= sm_count();
+    const int sms = sm_count();
+    if (max_chunk >= 48) return chains <= (max_chunk > 256 ? 1 : 2) * sms;
+    return 3 * chains <= sms;
 }
 
 template <int D, typename T>
 int run_spatial(const ScanParams& p, cudaStream_t st) {
     const int pairs = p.B * p.heads;
     if constexpr (mma_capable<D, T, T>()) {
-        if (use_tc_scan(p, true, 4 * pairs)) return run_tc_spatial(p, VH_BF16, st);
+        if (use_tc_scan(p, true, 4 * pairs, std::max(p.H, p.W))) return run_tc_spatial(p, VH_BF16, st);
         if (p.aux) return launch_warp<kKindBoth>(p, pairs, st);
     }
     int rc = launch_auto<D, T, T, kKindRows>(p, p.W, pairs, st);
@@ -167,7 +175,7 @@ int run_sequence(const ScanParams& p, cudaStream_t st) {
     int maxc = 1;
     for (int r = 0; r < p.R; ++r) maxc = std::max(maxc, p.chunk[r]);
     if constexpr (mma_capable<D, XT, QT>()) {
-        if (use_tc_scan(p, false, p.B * p.R * p.heads)) return run_tc_sequence(p, st);
+        if (use_tc_scan(p, false, p.B * p.R * p.heads, maxc)) return run_tc_sequence(p, st);
     }
     return launch_auto<D, XT, QT, kKindSeq>(p, maxc, p.B * p.heads, st);
 }

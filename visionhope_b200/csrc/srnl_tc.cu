@@ -217,7 +217,10 @@ __global__ void __launch_bounds__(kThreads, NST == 4 ? 1 : 2)
     srnl_tc_kernel(const ScanParams p, const TcGeom g, const __grid_constant__ TcMaps maps) {
     using S = TcSmem<NST>;
     extern __shared__ unsigned char smem_dyn[];
-    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    // The base rounded up to 1 KB (the swizzled operand tiles need it), as an offset from the
+    // shared array itself: the compiler then keeps every derived pointer in the shared address
+    // space (shared loads and stores, not generic ones).
+    unsigned char* sm = smem_dyn + ((1024u - (tcu::smem_u32(smem_dyn) & 1023u)) & 1023u);
     unsigned char* tiles = sm + S::TILES;
     unsigned char* bop = sm + S::BOP;
     float* s32 = reinterpret_cast<float*>(sm + S::S32);
