@@ -360,6 +360,55 @@ int vh_add_layernorm_fwd(const void* x, int32_t x_dtype, const void* r, int32_t 
                          const float* weight, const float* bias, float eps, void* y, int32_t y_dtype,
                          int64_t rows, int32_t channels, vh_stream_t stream);
 
+/* =======================================================================================
+ * Backward (training) entry points.  Every reduction runs in a fixed order, so gradients are
+ * bit-reproducible; the ones that reduce over pixels or rows take a caller-provided workspace
+ * of the size their *_workspace_bytes function gives.
+ * =====================================================================================*/
+
+/* Query normalization backward; replaces utils/csrc/query_normalization.cu:78-134, 180-221,
+ * 267-300 `visionhope_qnorm_backward` (utils/query_normalization.py:68-76):
+ *   grad_out, q_out fp32 [B, R, heads, L, D]; inv_norm fp32 [B*R*L*heads] (vh_qnorm_fwd's);
+ *   grad_q [B, R, L, C] of q_dtype = (g - q_out (q_out . g)) inv (g inv where the norm was
+ *   clamped, inv = 1e12). */
+int vh_qnorm_bwd(const float* grad_out, const float* q_out, const float* inv_norm, void* grad_q, int32_t q_dtype,
+                 int32_t batch, int32_t dirs, int32_t length, int32_t heads, int32_t head_dim, vh_stream_t stream);
+
+/* Direction restoration + fusion backward; replaces utils/csrc/direction_fusion.cu:123-502,
+ * 577-691 `visionhope_postprocess_scale_backward` (utils/direction_fusion.py:106-118):
+ *   grad_out fp32 logical [B, C, H, W] with element strides gs_b, gs_c, gs_h, gs_w (any layout);
+ *   y, x [B, 4, heads, L, D] of io_dtype; skip (C or 4*C values, skip_per_dir) and scale [4, C]
+ *   fp32.  Writes grad_y, grad_x (io_dtype, y's layout) and grad_skip, grad_scale (fp32, the
+ *   shapes of skip and scale).  workspace: vh_dirfuse_bwd_workspace_bytes(...) bytes. */
+int64_t vh_dirfuse_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t height, int32_t width,
+                                       int32_t head_dim);
+int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c, int64_t gs_h, int64_t gs_w, const void* y,
+                   const void* x, int32_t io_dtype, const float* skip, int32_t skip_per_dir, const float* scale,
+                   void* grad_y, void* grad_x, float* grad_skip, float* grad_scale, void* workspace,
+                   int64_t workspace_bytes, int32_t batch, int32_t heads, int32_t height, int32_t width,
+                   int32_t head_dim, vh_stream_t stream);
+
+/* LayerNorm over channels-last rows, backward; replaces the Triton kernels
+ * utils/layer_norm_cuda.py:59-119, 150-185 (`_layernorm2d_backward_kernel`,
+ * `_layernorm2d_reduce_kernel`):  grad_y fp32 [rows, C]; x [rows, C] of x_dtype; weight fp32
+ * [C]; mean, rstd fp32 [rows] (vh_layernorm_fwd's).  Writes grad_x (x_dtype) and grad_weight,
+ * grad_bias (fp32 [C]).  workspace: vh_layernorm_bwd_workspace_bytes(rows, C) bytes. */
+int64_t vh_layernorm_bwd_workspace_bytes(int64_t rows, int32_t channels);
+int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dtype, const float* weight, const float* mean,
+                     const float* rstd, void* grad_x, float* grad_weight, float* grad_bias, void* workspace,
+                     int64_t workspace_bytes, int64_t rows, int32_t channels, vh_stream_t stream);
+
+/* GRN backward; replaces utils/csrc/grn_cuda.cu:126-265, 322-359 `grn_backward_cuda`
+ * (utils/grn_cuda.py:49-80):  grad_y fp32 and x (x_dtype) channels-last [B, H, W, C]; gamma
+ * fp32 [C]; gx fp32 [B, C] and inv_den fp32 [B] (vh_grn_fwd's statistics).  Writes grad_x
+ * (x_dtype), grad_gamma and grad_beta (fp32 [C]).  workspace: vh_grn_bwd_workspace_bytes(B, C)
+ * bytes. */
+int64_t vh_grn_bwd_workspace_bytes(int32_t batch, int32_t channels);
+int vh_grn_bwd(const float* grad_y, const void* x, int32_t x_dtype, const float* gamma, const float* gx,
+               const float* inv_den, void* grad_x, float* grad_gamma, float* grad_beta, void* workspace,
+               int64_t workspace_bytes, int32_t batch, int32_t height, int32_t width, int32_t channels,
+               vh_stream_t stream);
+
 /* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
  * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it
  * to measure the device's FP32 (non-tensor) FMA peak. */

@@ -1,0 +1,128 @@
+"""Backward kernels (vh_qnorm_bwd, vh_dirfuse_bwd, vh_layernorm_bwd, vh_grn_bwd) through the
+autograd Functions of the drop-in modules, against fp64 CPU autograd of the gradient oracle
+(oracle/grad.py) on the same inputs.  Bar: normwise relative error 1e-5 for fp32 gradients,
+one 16-bit rounding (8e-3) where the gradient is returned in bf16/fp16 as the reference does."""
+import pytest
+import torch
+
+from oracle import grad as og
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda")
+
+
+def _rel(a, b):
+    a, b = a.detach().double().cpu(), b.detach().double().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _tol(dtype):
+    return 1e-5 if dtype == torch.float32 else 8e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("heads,D,L", [(2, 16, 49), (3, 8, 20), (1, 64, 7), (6, 4, 33)])
+def test_qnorm_backward(dtype, heads, D, L):
+    from visionhope_b200.utils.query_normalization import visionhope_qnorm
+
+    g = torch.Generator().manual_seed(heads * 100 + D + L)
+    q = torch.randn(2, 4, L, heads * D, generator=g).to(dtype)
+    q[1, 2, 3, :D] = 0  # a zero vector: the clamped branch
+    gout = torch.randn(2, 4, heads, L, D, generator=g)
+    qd = q.to(DEV).requires_grad_(True)
+    out = visionhope_qnorm(qd, heads, D)
+    out.backward(gout.to(DEV))
+    (exp,) = og.grads(lambda t: og.qnorm(t, heads, D), [q.float()], gout)
+    assert qd.grad.dtype == dtype and qd.grad.shape == q.shape
+    assert _rel(qd.grad, exp) < _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("channels_last", [False, True])
+@pytest.mark.parametrize("per_dir", [False, True])
+@pytest.mark.parametrize("B,heads,D,H,W", [(2, 2, 16, 7, 9), (1, 3, 8, 14, 14), (2, 1, 32, 5, 70)])
+def test_dirfuse_backward(dtype, channels_last, per_dir, B, heads, D, H, W):
+    from visionhope_b200.utils.direction_fusion import visionhope_postprocess_scale
+
+    g = torch.Generator().manual_seed(B * 1000 + heads * 100 + H + W + 7 * per_dir)
+    L, C = H * W, heads * D
+    y = torch.randn(B, 4, heads, L, D, generator=g).to(dtype)
+    x = torch.randn(B, 4, heads, L, D, generator=g).to(dtype)
+    skip = torch.randn((4, C) if per_dir else (C,), generator=g)
+    scale = torch.randn(4, C, generator=g)
+    gout = torch.randn(B, C, H, W, generator=g)
+    leaves = [t.to(DEV).requires_grad_(True) for t in (y, x, skip, scale)]
+    out = visionhope_postprocess_scale(*leaves, H, W, channels_last)
+    gd = gout.to(DEV)
+    if channels_last:
+        gd = gd.contiguous(memory_format=torch.channels_last)
+    out.backward(gd)
+    exp = og.grads(lambda a, b, c, d: og.dirfuse(a, b, c, d, H, W), [y.float(), x.float(), skip, scale], gout)
+    for leaf, e in zip(leaves, exp):
+        assert leaf.grad.shape == e.shape
+        tol = _tol(dtype) if leaf.dtype != torch.float32 else 2e-5
+        assert _rel(leaf.grad, e) < tol
+
+
+def test_dirfuse_backward_is_deterministic():
+    from visionhope_b200.utils.direction_fusion import postprocess_backward
+
+    g = torch.Generator().manual_seed(5)
+    B, heads, D, H, W = 4, 3, 16, 28, 28
+    y, x = (torch.randn(B, 4, heads, H * W, D, generator=g).to(DEV) for _ in range(2))
+    skip, scale = torch.randn(heads * D, generator=g).to(DEV), torch.randn(4, heads * D, generator=g).to(DEV)
+    gout = torch.randn(B, heads * D, H, W, generator=g).to(DEV)
+    r1 = postprocess_backward(gout, y, x, skip, scale, H, W)
+    r2 = postprocess_backward(gout, y, x, skip, scale, H, W)
+    assert all(torch.equal(a, b) for a, b in zip(r1, r2))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,C,H,W", [(2, 96, 14, 14), (3, 40, 5, 7), (1, 768, 7, 7), (2, 1000, 3, 3)])
+def test_layernorm_backward(dtype, B, C, H, W):
+    from visionhope_b200.utils.layer_norm_cuda import visionhope_layernorm2d
+
+    g = torch.Generator().manual_seed(B + C + H)
+    x = (torch.randn(B, C, H, W, generator=g) * 2 + 0.5).to(dtype).contiguous(memory_format=torch.channels_last)
+    w = torch.randn(C, generator=g)
+    b = torch.randn(C, generator=g)
+    gout = torch.randn(B, C, H, W, generator=g)
+    leaves = [x.to(DEV).requires_grad_(True), w.to(DEV).requires_grad_(True), b.to(DEV).requires_grad_(True)]
+    y = visionhope_layernorm2d(*leaves, 1e-6)
+    y.backward(gout.to(DEV))
+
+    def ln2d(a, ww, bb):
+        return og.layernorm_rows(a.permute(0, 2, 3, 1), ww, bb, 1e-6).permute(0, 3, 1, 2)
+
+    exp = og.grads(ln2d, [x.float(), w, b], gout)
+    assert leaves[0].grad.dtype == dtype and leaves[0].grad.is_contiguous(memory_format=torch.channels_last)
+    assert _rel(leaves[0].grad, exp[0]) < _tol(dtype)
+    assert _rel(leaves[1].grad, exp[1]) < 2e-5
+    assert _rel(leaves[2].grad, exp[2]) < 2e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,C,H,W", [(2, 96, 14, 14), (4, 64, 7, 7), (1, 2560, 4, 4), (3, 20, 9, 5)])
+def test_grn_backward(dtype, B, C, H, W):
+    from visionhope_b200.utils.grn_cuda import visionhope_grn
+
+    g = torch.Generator().manual_seed(B * 7 + C + H)
+    x = torch.randn(B, C, H, W, generator=g)
+    x[0, 1] = 0  # a channel with Gx = 0
+    x = x.to(dtype).contiguous(memory_format=torch.channels_last)
+    gamma = torch.randn(C, generator=g) * 0.5
+    beta = torch.randn(C, generator=g) * 0.5
+    gout = torch.randn(B, C, H, W, generator=g)
+    leaves = [x.to(DEV).requires_grad_(True), gamma.to(DEV).requires_grad_(True), beta.to(DEV).requires_grad_(True)]
+    y = visionhope_grn(*leaves, 1e-6)
+    y.backward(gout.to(DEV))
+    exp = og.grads(lambda a, b, c: og.grn(a, b, c, 1e-6), [x.float(), gamma, beta], gout)
+    # Where Gx = 0 the fp64 autograd of sqrt gives nan; the reference's kernel (grn_cuda.cu:
+    # 256-258) takes 1/Gx as 0 there, and so do we: compare the channels with Gx > 0.
+    dx = leaves[0].grad.double().cpu()
+    ok = torch.isfinite(exp[0])
+    assert torch.isfinite(dx).all()
+    assert _rel(dx[ok], exp[0][ok]) < _tol(dtype)
+    assert _rel(leaves[1].grad, exp[1].nan_to_num()) < 2e-5
+    assert _rel(leaves[2].grad, exp[2]) < 2e-5

@@ -134,6 +134,25 @@ def load() -> ctypes.CDLL:
             lib.vh_tc_status.argtypes = [c_int32]
             lib.vh_probe_ffma.restype = c_int32
             lib.vh_probe_ffma.argtypes = [c_void_p, c_int32, c_int32, c_void_p]
+            # backward (training) entry points
+            lib.vh_qnorm_bwd.restype = c_int32
+            lib.vh_qnorm_bwd.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32] + [c_int32] * 5 + [c_void_p]
+            lib.vh_dirfuse_bwd_workspace_bytes.restype = c_int64
+            lib.vh_dirfuse_bwd_workspace_bytes.argtypes = [c_int32] * 5
+            lib.vh_dirfuse_bwd.restype = c_int32
+            lib.vh_dirfuse_bwd.argtypes = ([c_void_p] + [c_int64] * 4 + [c_void_p, c_void_p, c_int32, c_void_p, c_int32,
+                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64]
+                                           + [c_int32] * 5 + [c_void_p])
+            lib.vh_layernorm_bwd_workspace_bytes.restype = c_int64
+            lib.vh_layernorm_bwd_workspace_bytes.argtypes = [c_int64, c_int32]
+            lib.vh_layernorm_bwd.restype = c_int32
+            lib.vh_layernorm_bwd.argtypes = ([c_void_p, c_void_p, c_int32] + [c_void_p] * 7 + [c_int64, c_int64, c_int32,
+                                             c_void_p])
+            lib.vh_grn_bwd_workspace_bytes.restype = c_int64
+            lib.vh_grn_bwd_workspace_bytes.argtypes = [c_int32, c_int32]
+            lib.vh_grn_bwd.restype = c_int32
+            lib.vh_grn_bwd.argtypes = ([c_void_p, c_void_p, c_int32] + [c_void_p] * 7 + [c_int64] + [c_int32] * 4
+                                       + [c_void_p])
             _lib = lib
     return _lib
 

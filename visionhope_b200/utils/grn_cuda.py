@@ -1,7 +1,8 @@
 """GRN on channels-last CUDA tensors with fp32 output (mirror of utils/grn_cuda.py).
 
 ``visionhope_grn`` calls ``vh_grn_fwd`` (replaces utils/csrc/grn_cuda.cu:267-300).  The
-statistics workspace comes from PyTorch's caching allocator.  Forward only.
+statistics workspace comes from PyTorch's caching allocator.  The autograd path saves the
+forward's statistics and runs ``vh_grn_bwd`` (replaces utils/csrc/grn_cuda.cu:126-265).
 """
 import torch
 
@@ -64,14 +65,42 @@ def grn_apply_ok(x):
     return C % 8 == 0 and C <= 2048
 
 
-class _GRNForwardOnly(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, gamma, beta, eps):
-        return grn_forward(x, gamma, beta, eps)
+@_lib.on_input_device
+def grn_backward(dout, x, gamma, gx, inv_den):
+    """Gradients of :func:`grn_forward` (``vh_grn_bwd``, replaces utils/csrc/grn_cuda.cu:126-265):
+    dout [B, C, H, W] (any float dtype and layout), the forward's x, gamma and its statistics
+    Gx [B, C], 1/den [B].  Returns (dx channels-last in x's dtype, dgamma, dbeta fp32 [C])."""
+    B, C, H, W = x.shape
+    g = dout.to(dtype=torch.float32, memory_format=torch.channels_last)
+    dx = torch.empty_like(x, memory_format=torch.channels_last)
+    dgamma = torch.empty((C,), device=x.device, dtype=torch.float32)
+    dbeta = torch.empty((C,), device=x.device, dtype=torch.float32)
+    nbytes = int(_lib.load().vh_grn_bwd_workspace_bytes(B, C))
+    ws = torch.empty((max(nbytes, 16) + 3) // 4, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().vh_grn_bwd(
+        g.data_ptr(), x.data_ptr(), _lib.dtype_code(x.dtype), gamma.data_ptr(), gx.data_ptr(), inv_den.data_ptr(),
+        dx.data_ptr(), dgamma.data_ptr(), dbeta.data_ptr(), ws.data_ptr(), ws.numel() * 4, B, H, W, C,
+        _lib.stream_handle(x.device)), "vh_grn_bwd")
+    return dx, dgamma, dbeta
+
+
+class _GRNFunction(torch.autograd.Function):
+    """GRN with its backward (utils/grn_cuda.py:33-80): saves x, gamma and the statistics."""
 
     @staticmethod
-    def backward(ctx, grad):
-        raise NotImplementedError("GRN backward is not implemented by visionhope_b200")
+    def forward(ctx, x, gamma, beta, eps):
+        y, gx, inv = grn_forward(x, gamma, beta, eps, want_stats=True)
+        g = gamma.detach().reshape(-1).contiguous().float()
+        ctx.save_for_backward(x, g, gx, inv)
+        ctx.param_shapes = (gamma.shape, gamma.dtype, beta.shape, beta.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, g, gx, inv = ctx.saved_tensors
+        dx, dgamma, dbeta = grn_backward(dout, x, g, gx, inv)
+        gshape, gdtype, bshape, bdtype = ctx.param_shapes
+        return dx, dgamma.view(gshape).to(gdtype), dbeta.view(bshape).to(bdtype), None
 
 
 def can_fuse_grn(x, gamma, beta):
@@ -90,5 +119,5 @@ def can_fuse_grn(x, gamma, beta):
 
 def visionhope_grn(x, gamma, beta, eps):
     if torch.is_grad_enabled() and any(t.requires_grad for t in (x, gamma, beta)):
-        return _GRNForwardOnly.apply(x, gamma, beta, eps)
+        return _GRNFunction.apply(x, gamma, beta, eps)
     return grn_forward(x, gamma, beta, eps)

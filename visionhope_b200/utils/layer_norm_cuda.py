@@ -1,7 +1,7 @@
 """Channels-last LayerNorm over C with fp32 output (mirror of utils/layer_norm_cuda.py).
 
-The reference's Triton kernel (layer_norm_cuda.py:31-57) is replaced by ``vh_layernorm_fwd``.
-Forward only.
+The reference's Triton kernels are replaced by ``vh_layernorm_fwd`` (layer_norm_cuda.py:31-57)
+and, on the autograd path, ``vh_layernorm_bwd`` (layer_norm_cuda.py:59-119).
 """
 import torch
 
@@ -50,21 +50,56 @@ def add_layernorm_rows(x_rows, r_rows, weight, bias, eps, *, out_dtype=torch.flo
 
 
 @_lib.on_input_device
-def _layernorm2d_forward(x, weight, bias, eps):
+def _layernorm2d_forward(x, weight, bias, eps, want_stats=False):
     batch, channels, height, width = x.shape
     rows = x.permute(0, 2, 3, 1).reshape(batch * height * width, channels)
-    y = layernorm_rows(rows, weight, bias, eps)
-    return y.view(batch, height, width, channels).permute(0, 3, 1, 2)
+    res = layernorm_rows(rows, weight, bias, eps, want_stats=want_stats)
+    y = res[0] if want_stats else res
+    y = y.view(batch, height, width, channels).permute(0, 3, 1, 2)
+    return (y, res[1], res[2]) if want_stats else y
 
 
-class _LayerNorm2dForwardOnly(torch.autograd.Function):
+@_lib.on_input_device
+def layernorm_rows_backward(dy_rows, x_rows, weight, mean, rstd):
+    """Gradients of :func:`layernorm_rows` (``vh_layernorm_bwd``, replaces the Triton kernels of
+    utils/layer_norm_cuda.py:59-119): dy_rows [rows, C] (cast to fp32), the forward's x_rows,
+    weight and statistics.  Returns (dx in x's dtype, dweight, dbias fp32 [C])."""
+    rows, C = x_rows.shape
+    g = dy_rows.contiguous().float()
+    x = x_rows.contiguous()
+    w = weight.detach().reshape(-1).contiguous().float()
+    dx = torch.empty_like(x)
+    dw = torch.empty((C,), device=x.device, dtype=torch.float32)
+    db = torch.empty((C,), device=x.device, dtype=torch.float32)
+    nbytes = int(_lib.load().vh_layernorm_bwd_workspace_bytes(rows, C))
+    ws = torch.empty((max(nbytes, 16) + 3) // 4, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().vh_layernorm_bwd(
+        g.data_ptr(), x.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), mean.data_ptr(), rstd.data_ptr(),
+        dx.data_ptr(), dw.data_ptr(), db.data_ptr(), ws.data_ptr(), ws.numel() * 4, rows, C,
+        _lib.stream_handle(x.device)), "vh_layernorm_bwd")
+    return dx, dw, db
+
+
+class _LayerNorm2dFunction(torch.autograd.Function):
+    """LayerNorm2d with its backward (utils/layer_norm_cuda.py:122-185)."""
+
     @staticmethod
     def forward(ctx, x, weight, bias, eps):
-        return _layernorm2d_forward(x, weight, bias, eps)
+        y, mean, rstd = _layernorm2d_forward(x, weight, bias, eps, want_stats=True)
+        ctx.save_for_backward(x, weight, mean, rstd)
+        ctx.param_meta = (weight.shape, weight.dtype, bias.shape, bias.dtype)
+        return y
 
     @staticmethod
-    def backward(ctx, grad):
-        raise NotImplementedError("LayerNorm2d backward is not implemented by visionhope_b200")
+    def backward(ctx, dy):
+        x, weight, mean, rstd = ctx.saved_tensors
+        batch, channels, height, width = x.shape
+        dy_rows = dy.contiguous(memory_format=torch.channels_last).permute(0, 2, 3, 1).reshape(-1, channels)
+        x_rows = x.permute(0, 2, 3, 1).reshape(-1, channels)
+        dx, dw, db = layernorm_rows_backward(dy_rows, x_rows, weight, mean, rstd)
+        dx = dx.view(batch, height, width, channels).permute(0, 3, 1, 2)
+        wshape, wdtype, bshape, bdtype = ctx.param_meta
+        return dx, dw.view(wshape).to(wdtype), db.view(bshape).to(bdtype), None
 
 
 def can_fuse_layernorm2d(x, weight, bias):
@@ -87,5 +122,5 @@ def visionhope_layernorm2d(x, weight, bias, eps):
     if not x.is_contiguous(memory_format=torch.channels_last):
         raise RuntimeError("visionhope_layernorm2d expects channels-last input")
     if torch.is_grad_enabled() and any(t.requires_grad for t in (x, weight, bias)):
-        return _LayerNorm2dForwardOnly.apply(x, weight, bias, float(eps))
+        return _LayerNorm2dFunction.apply(x, weight, bias, float(eps))
     return _layernorm2d_forward(x, weight, bias, float(eps))
