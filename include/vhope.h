@@ -366,6 +366,40 @@ int vh_add_layernorm_fwd(const void* x, int32_t x_dtype, const void* r, int32_t 
  * of the size their *_workspace_bytes function gives.
  * =====================================================================================*/
 
+/* SRNL recurrence backward for packed sequences (chunks of up to 64 tokens, head_dim 4, 8, 16
+ * or 32); replaces models/srnl_core/csrc/chunk.cu:511-1057, 1133-1206 `srnl_backward` /
+ * `srnl_backward_qraw` (chunk.py:286-359 SRNLNormalizedQueryFunction.backward, 507-588
+ * SRNLRawQueryFunction.backward).  The inputs are the forward's (mem, x, q, q_mode, sizes,
+ * chunks, consts: see vh_srnl_sequence_args); nothing from the forward is saved besides them:
+ * the chunk states and the gain sequence are recomputed.  grad_y fp32 [B, R, heads, L, D].
+ * Writes grad_x (fp32, x's shape), grad_q (fp32, q's shape: [B, R, L, C] for raw queries,
+ * through their normalization; [B, R, heads, L, D] for normalized ones) and grad_m, grad_v,
+ * grad_k, grad_eta, grad_alpha (fp32, the memories' shapes; shared memories get the sum over the
+ * batch).  workspace: vh_srnl_sequence_bwd_workspace_bytes(args) bytes. */
+typedef struct {
+    vh_srnl_memories mem;
+    const void* x;
+    const void* q;
+    int32_t x_dtype;
+    int32_t q_dtype;
+    int32_t q_mode;
+    const float* grad_y;
+    float* grad_x;
+    float* grad_q;
+    float* grad_m;
+    float* grad_v;
+    float* grad_k;
+    float* grad_eta;
+    float* grad_alpha;
+    int32_t batch, dirs, heads, length, head_dim;
+    int32_t chunk[4];
+    vh_srnl_consts consts;
+} vh_srnl_sequence_bwd_args;
+
+int64_t vh_srnl_sequence_bwd_workspace_bytes(const vh_srnl_sequence_bwd_args* args);
+int vh_srnl_sequence_bwd(const vh_srnl_sequence_bwd_args* args, void* workspace, int64_t workspace_bytes,
+                         vh_stream_t stream);
+
 /* Query normalization backward; replaces utils/csrc/query_normalization.cu:78-134, 180-221,
  * 267-300 `visionhope_qnorm_backward` (utils/query_normalization.py:68-76):
  *   grad_out, q_out fp32 [B, R, heads, L, D]; inv_norm fp32 [B*R*L*heads] (vh_qnorm_fwd's);

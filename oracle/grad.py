@@ -68,3 +68,59 @@ def grads(fn, inputs, grad_out):
     out = fn(*leaves)
     out.backward(grad_out.detach().double().cpu())
     return [t.grad if isinstance(t, torch.Tensor) and t.requires_grad else None for t in leaves]
+
+
+def srnl_sequence(mems, x, q, chunks, consts, q_normalized):
+    """The packed SRNL recurrence (oracle/srnl_core.inc restated in PyTorch, so that autograd
+    gives its gradients): mems = (M_m, M_v, M_k, e, a), shared [R, heads, D(, D)] or per chain
+    [B, R, heads, D(, D)]; x [B, R, heads, L, D]; q raw [B, R, L, C] or unit-norm
+    [B, R, heads, L, D]; chunks[r] the chunk length of direction r; consts = (step, min
+    retention, retention bias, injection margin, spectral factor, clamp flag).  Returns y
+    [B, R, heads, L, D].  Per token (models/srnl_core/csrc/inference_recurrence.cuh:40-106,
+    memory.cuh:219-233), then S <- S G at each chunk end (inference_recurrence.cuh:110-135).
+    The clamp limit carries the forward's one-ulp step toward zero (nextafter) in its value,
+    not in its gradient."""
+    step, minr, bias, margin, sfac, clamp = consts
+    B, R, H, L, D = x.shape
+    if not q_normalized:
+        q = qnorm(q, H, D)
+    per_chain = mems[0].dim() == 5
+    Mm, Mv, Mk, Me, Ma = mems if per_chain else (m.unsqueeze(0).expand(B, *m.shape) for m in mems)
+    eye = torch.eye(D, dtype=x.dtype)
+    ys = []
+    for r in range(R):
+        Lc = int(chunks[r])
+        n = (L + Lc - 1) // Lc
+        pad = n * Lc - L
+        xr = F.pad(x[:, r], (0, 0, 0, pad))
+        qr = F.pad(q[:, r], (0, 0, 0, pad))
+        Sm, Sv, Sk, e, a = Mm[:, r], Mv[:, r], Mk[:, r], Me[:, r], Ma[:, r]
+        outs = []
+        for c in range(n):
+            G = eye.expand(B, H, D, D)
+            for t in range(Lc):
+                xt, qt = xr[:, :, c * Lc + t], qr[:, :, c * Lc + t]
+                outs.append(torch.einsum("bhij,bhj->bhi", Sm, qt))
+                kt = torch.einsum("bhij,bhj->bhi", Sk, xt)
+                v = torch.einsum("bhij,bhj->bhi", Sv, xt)
+                k = kt / torch.sqrt((kt * kt).sum(-1, keepdim=True) + 1e-6)
+                d = k - v
+                ep = (xt * e).sum(-1).clamp(-10.0, 10.0)
+                ap = ((xt * a).sum(-1) + bias).clamp(-10.0, 10.0)
+                eta = step * torch.log1p(torch.exp(ep))
+                alpha = minr + (1.0 - minr) * torch.sigmoid(ap)
+                dn = torch.sqrt((d * d).sum(-1) + 1e-12)
+                cap = margin * (1.0 - alpha) / (dn + 1e-6)
+                eff = cap * (-torch.expm1(-eta / cap))
+                if clamp:
+                    ke = (k * k).sum(-1)
+                    lim = sfac * alpha / ke.clamp_min(1e-20)
+                    lim = lim - (lim - torch.nextafter(lim.detach(), torch.zeros_like(lim))).detach()
+                    eff = torch.minimum(eff, lim)
+                rr = d + torch.einsum("bhij,bhj->bhi", G, k)
+                G = alpha[..., None, None] * G - eff[..., None, None] * rr[..., :, None] * k[..., None, :]
+            Sm, Sv, Sk = Sm @ G, Sv @ G, Sk @ G
+            e = torch.einsum("bhl,bhlj->bhj", e, G)
+            a = torch.einsum("bhl,bhlj->bhj", a, G)
+        ys.append(torch.stack(outs, dim=2)[:, :, :L])
+    return torch.stack(ys, dim=1)

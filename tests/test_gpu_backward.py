@@ -126,3 +126,64 @@ def test_grn_backward(dtype, B, C, H, W):
     assert _rel(dx[ok], exp[0][ok]) < _tol(dtype)
     assert _rel(leaves[1].grad, exp[1].nan_to_num()) < 2e-5
     assert _rel(leaves[2].grad, exp[2]) < 2e-5
+
+
+def _srnl_case(seed, B, R, H, L, D, per_chain, q_normalized, dtype, mem_scale=0.35):
+    g = torch.Generator().manual_seed(seed)
+    lead = (B, R, H) if per_chain else (R, H)
+    mems = [torch.randn(*lead, D, D, generator=g) * mem_scale for _ in range(3)]
+    mems += [torch.randn(*lead, D, generator=g) * 0.6 for _ in range(2)]
+    x = torch.randn(B, R, H, L, D, generator=g).to(dtype)
+    if q_normalized:
+        q = torch.randn(B, R, H, L, D, generator=g)
+        q = q / q.norm(dim=-1, keepdim=True)
+    else:
+        q = torch.randn(B, R, L, H * D, generator=g).to(dtype)
+    gy = torch.randn(B, R, H, L, D, generator=g)
+    return mems, x, q, gy
+
+
+@pytest.mark.parametrize("q_normalized", [False, True])
+@pytest.mark.parametrize("per_chain", [False, True])
+@pytest.mark.parametrize("D,chunk,L,dtype,mem_scale", [
+    (16, 14, 30, torch.float32, 0.35), (8, 7, 20, torch.float32, 0.35), (16, 64, 70, torch.float32, 0.35),
+    (32, 5, 12, torch.float32, 0.35), (4, 9, 9, torch.float32, 0.35), (16, 12, 26, torch.float32, 1.0),
+    (16, 14, 28, torch.bfloat16, 0.35)])
+def test_srnl_sequence_backward(q_normalized, per_chain, D, chunk, L, dtype, mem_scale):
+    """The reference's training path (chunk.py SRNLNormalizedQueryFunction / SRNLRawQueryFunction)
+    through the drop-in functions: every input's gradient against fp64 autograd of the oracle
+    recurrence.  mem_scale 1.0 makes the spectral clamp bind on part of the tokens."""
+    from visionhope_b200.srnl_core.chunk import (recurrence_constants_tuple, srnl_normalized_query,
+                                                  srnl_raw_query)
+
+    B, R, H = 2, 4, 2
+    mems, x, q, gy = _srnl_case(D * 100 + chunk + L, B, R, H, L, D, per_chain, q_normalized, dtype, mem_scale)
+    leaves = [t.to(DEV).requires_grad_(True) for t in (*mems, x, q)]
+    if q_normalized:
+        y = srnl_normalized_query(*leaves, chunk)
+    else:
+        y = srnl_raw_query(*leaves, chunk, H, D)
+    y.backward(gy.to(DEV).to(y.dtype))
+
+    def fn(*t):
+        return og.srnl_sequence(t[:5], t[5], t[6], [chunk] * R, recurrence_constants_tuple(), q_normalized)
+
+    exp = og.grads(fn, [*mems, x.float(), q.float()], gy.to(dtype).float())
+    names = ["M_m", "M_v", "M_k", "M_eta", "M_alpha", "x", "q"]
+    for name, leaf, e in zip(names, leaves, exp):
+        assert leaf.grad is not None and leaf.grad.shape == e.shape, name
+        tol = 2e-4 if leaf.grad.dtype == torch.float32 else 1e-2
+        err = _rel(leaf.grad, e)
+        assert err < tol, f"{name}: {err:.3e}"
+
+
+def test_srnl_sequence_backward_is_deterministic():
+    from visionhope_b200.srnl_core.chunk import recurrence_constants, sequence_backward
+
+    mems, x, q, gy = _srnl_case(3, 3, 4, 2, 40, 16, False, False, torch.float32)
+    args = ([m.to(DEV) for m in mems], x.to(DEV), q.to(DEV), [14] * 4, gy.to(DEV))
+    r1 = sequence_backward(*args, q_normalized=False)
+    r2 = sequence_backward(*args, q_normalized=False)
+    flat1 = [*r1[0], r1[1], r1[2]]
+    flat2 = [*r2[0], r2[1], r2[2]]
+    assert all(torch.equal(a, b) for a, b in zip(flat1, flat2))

@@ -89,3 +89,25 @@ def test_gradients_match_finite_differences():
     gm = torch.randn(5, dtype=torch.float64, requires_grad=True)
     bt = torch.randn(5, dtype=torch.float64, requires_grad=True)
     assert torch.autograd.gradcheck(lambda a, b, c: og.grn(a, b, c, 1e-6), (xg, gm, bt))
+
+
+@pytest.mark.parametrize("q_normalized,per_chain", [(False, False), (True, True)])
+def test_srnl_sequence_matches_c_oracle(q_normalized, per_chain):
+    from visionhope_b200.srnl_core.chunk import recurrence_constants_tuple
+
+    g = np.random.default_rng(11 + per_chain)
+    B, R, H, L, D = 2, 4, 2, 23, 8
+    lead = (B, R, H) if per_chain else (R, H)
+    mems = [g.normal(0, 0.35, lead + (D, D)).astype(np.float32) for _ in range(3)]
+    mems += [g.normal(0, 0.6, lead + (D,)).astype(np.float32) for _ in range(2)]
+    x = g.normal(size=(B, R, H, L, D)).astype(np.float32)
+    if q_normalized:
+        q = g.normal(size=(B, R, H, L, D)).astype(np.float32)
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    else:
+        q = g.normal(size=(B, R, L, H * D)).astype(np.float32)
+    chunks = [6, 6, 5, 9]
+    exp = oracle.srnl_sequence(mems, x, q, chunks, q_normalized=q_normalized)
+    got = og.srnl_sequence([torch.from_numpy(m).double() for m in mems], torch.from_numpy(x).double(),
+                           torch.from_numpy(q).double(), chunks, recurrence_constants_tuple(), q_normalized)
+    assert _rel(got.numpy(), exp) < 1e-12

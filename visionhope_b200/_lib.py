@@ -57,6 +57,15 @@ class VhSequenceArgs(ctypes.Structure):
                 ("head_dim", c_int32), ("chunk", c_int32 * 4), ("consts", VhConsts)]
 
 
+class VhSequenceBwdArgs(ctypes.Structure):
+    _fields_ = [("mem", VhMemories), ("x", c_void_p), ("q", c_void_p),
+                ("x_dtype", c_int32), ("q_dtype", c_int32), ("q_mode", c_int32),
+                ("grad_y", c_void_p), ("grad_x", c_void_p), ("grad_q", c_void_p), ("grad_m", c_void_p),
+                ("grad_v", c_void_p), ("grad_k", c_void_p), ("grad_eta", c_void_p), ("grad_alpha", c_void_p),
+                ("batch", c_int32), ("dirs", c_int32), ("heads", c_int32), ("length", c_int32),
+                ("head_dim", c_int32), ("chunk", c_int32 * 4), ("consts", VhConsts)]
+
+
 class VhDwconvArgs(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("gate", c_void_p), ("weight", c_void_p), ("bias", c_void_p),
                 ("y", c_void_p), ("dtype", c_int32), ("mode", c_int32), ("ksize", c_int32),
@@ -148,6 +157,10 @@ def load() -> ctypes.CDLL:
             lib.vh_layernorm_bwd.restype = c_int32
             lib.vh_layernorm_bwd.argtypes = ([c_void_p, c_void_p, c_int32] + [c_void_p] * 7 + [c_int64, c_int64, c_int32,
                                              c_void_p])
+            lib.vh_srnl_sequence_bwd_workspace_bytes.restype = c_int64
+            lib.vh_srnl_sequence_bwd_workspace_bytes.argtypes = [ctypes.POINTER(VhSequenceBwdArgs)]
+            lib.vh_srnl_sequence_bwd.restype = c_int32
+            lib.vh_srnl_sequence_bwd.argtypes = [ctypes.POINTER(VhSequenceBwdArgs), c_void_p, c_int64, c_void_p]
             lib.vh_grn_bwd_workspace_bytes.restype = c_int64
             lib.vh_grn_bwd_workspace_bytes.argtypes = [c_int32, c_int32]
             lib.vh_grn_bwd.restype = c_int32

@@ -1,7 +1,7 @@
 """SRNL recurrence for chunks of up to 64 tokens, backed by libvhope.so.
 
-Mirror of models/srnl_core/chunk.py: same names, arguments, dtype rules and errors.
-Forward only -- the training backward (chunk.py:286-359, 507-588) is out of scope and raises.
+Mirror of models/srnl_core/chunk.py: same names, arguments, dtype rules and errors.  The
+autograd path runs the training backward ``vh_srnl_sequence_bwd`` (chunk.py:286-359, 507-588).
 Recurrence constants are read from the same environment variables (chunk.py:44-58) and
 passed to the kernels at run time instead of being compiled in.
 """
@@ -94,21 +94,53 @@ def run_sequence(states, x, q, chunk_sizes, *, q_normalized):
     return y
 
 
-class _ForwardOnly(torch.autograd.Function):
-    """Inference-only autograd node: the training backward is not part of this library."""
+def sequence_backward(states, x, q, chunk_sizes, grad_y, *, q_normalized):
+    """Gradients of :func:`run_sequence` (``vh_srnl_sequence_bwd``, replaces
+    models/srnl_core/csrc/chunk.cu:511-1057): returns (dM_m, dM_v, dM_k, dM_eta, dM_alpha) in the
+    memories' shapes, dx in x's shape and dq in q's shape, all fp32.  Chunks of up to 64 tokens,
+    head_dim up to 32."""
+    _lib.ensure_device(x)
+    B, R, heads, L, D = x.shape
+    mems, per_chain = _memories_f32(states, x)
+    x_c, q_c = x.contiguous(), q.contiguous()
+    g = grad_y.contiguous().float()
+    dx = torch.empty(x_c.shape, device=x.device, dtype=torch.float32)
+    dq = torch.empty(q_c.shape, device=x.device, dtype=torch.float32)
+    dm = [torch.empty_like(m) for m in mems]
+    chunks = list(int(c) for c in chunk_sizes) + [1] * (4 - len(chunk_sizes))
+    args = _lib.VhSequenceBwdArgs(
+        _lib.memories(mems, per_chain), x_c.data_ptr(), q_c.data_ptr(), _lib.dtype_code(x_c.dtype),
+        _lib.dtype_code(q_c.dtype), 1 if q_normalized else 0, g.data_ptr(), dx.data_ptr(), dq.data_ptr(),
+        *(t.data_ptr() for t in dm), B, R, heads, L, D, (_lib.c_int32 * 4)(*chunks), recurrence_constants())
+    lib = _lib.load()
+    nbytes = int(lib.vh_srnl_sequence_bwd_workspace_bytes(args))
+    ws = torch.empty((max(nbytes, 16) + 3) // 4, device=x.device, dtype=torch.float32)
+    _lib.check(lib.vh_srnl_sequence_bwd(args, ws.data_ptr(), ws.numel() * 4, _lib.stream_handle(x.device)),
+               "vh_srnl_sequence_bwd")
+    return tuple(m.view(s.shape) for m, s in zip(dm, states)), dx, dq
+
+
+class _SequenceFunction(torch.autograd.Function):
+    """The packed recurrence with its backward (chunk.py:172-359, 366-588): the forward saves
+    only its inputs; the backward recomputes the chunk states and the gain sequence."""
 
     @staticmethod
-    def forward(ctx, fn, *inputs):
-        return fn()
+    def forward(ctx, forward, chunks, q_normalized, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q):
+        ctx.save_for_backward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q)
+        ctx.cfg = (list(chunks), bool(q_normalized))
+        return forward()
 
     @staticmethod
-    def backward(ctx, *grads):
-        raise NotImplementedError("SRNL backward (training) is not implemented by visionhope_b200")
+    def backward(ctx, dy):
+        *states, x, q = ctx.saved_tensors
+        chunks, q_normalized = ctx.cfg
+        dms, dx, dq = sequence_backward(states, x, q, chunks, dy, q_normalized=q_normalized)
+        return (None, None, None, *(d.to(s.dtype) for d, s in zip(dms, states)), dx.to(x.dtype), dq.to(q.dtype))
 
 
-def _apply(fn, *tensors):
+def _apply(fn, chunks, q_normalized, *tensors):
     if torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
-        return _ForwardOnly.apply(fn, *tensors)
+        return _SequenceFunction.apply(fn, chunks, q_normalized, *tensors)
     return fn()
 
 
@@ -143,7 +175,7 @@ def srnl_normalized_query(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q, chunk_s
     if x.dtype in (torch.float16, torch.bfloat16, torch.float32) and q.dtype == torch.float32:
         return _apply(lambda: _normalized_query_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0,
                                                         x, q, int(chunk_size)),
-                      M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q)
+                      [int(chunk_size)] * x.shape[1], True, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q)
     raise RuntimeError("The release HOPE CUDA path expects fp16/bf16/fp32 x and fp32 normalized q.")
 
 
@@ -181,7 +213,7 @@ def srnl_raw_query(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, chunk_size
     """Four-direction recurrence with raw queries normalized in-kernel (chunk.py:622-625)."""
     return _apply(lambda: _raw_query_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw,
                                              int(chunk_size), int(num_heads), int(head_dim)),
-                  M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
+                  [int(chunk_size)] * 4, False, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
 
 
 def can_fuse_raw_query(x, q_raw, num_heads, head_dim):

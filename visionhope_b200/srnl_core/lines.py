@@ -3,7 +3,9 @@
 Mirror of models/srnl_core/lines.py (srnl_long_chunk, srnl_variable_lines): same names,
 arguments and errors.  One kernel serves every chunk length -- chunks longer than a
 shared-memory tile are processed tile by tile with the gain carried in registers -- so
-there is no separate "large"/"varline" kernel family.  Forward only.
+there is no separate "large"/"varline" kernel family.  The autograd path uses the sequence
+backward (``vh_srnl_sequence_bwd``), which takes chunks of up to 64 tokens; a backward through
+longer chunks raises.
 """
 from __future__ import annotations
 
@@ -46,7 +48,7 @@ def srnl_long_chunk(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, chunk_siz
     """Recurrence with chunks longer than MAX_CHUNK (lines.py:396-399)."""
     return _base._apply(lambda: _long_chunk_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw,
                                                     int(chunk_size), int(num_heads), int(head_dim)),
-                        M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
+                        [int(chunk_size)] * x.shape[1], False, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
 
 
 @_lib.on_input_device
@@ -82,6 +84,7 @@ def _variable_lines_forward(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, r
 def srnl_variable_lines(M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, row_chunk_size,
                         col_chunk_size, num_heads, head_dim):
     """Four scans with row chunk W for directions 0-1 and column chunk H for 2-3 (lines.py:646-671)."""
+    chunks = [int(row_chunk_size)] * 2 + [int(col_chunk_size)] * 2
     return _base._apply(lambda: _variable_lines_forward(
         M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw, int(row_chunk_size), int(col_chunk_size),
-        int(num_heads), int(head_dim)), M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
+        int(num_heads), int(head_dim)), chunks, False, M_m_0, M_v_0, M_k_0, M_eta_0, M_alpha_0, x, q_raw)
