@@ -88,8 +88,10 @@ def _targets():
     import visionhope.utils.query_normalization as qnorm
 
     fused_fns = ["srnl_line_forward_seq_noatomic", "srnl_sequence_forward"]
-    chunk_fns = ["srnl_forward", "srnl_forward_qraw"]
+    chunk_fns = ["srnl_forward", "srnl_forward_qraw", "srnl_backward", "srnl_backward_qraw"]
     line_fns = ["srnl_forward_qraw_large", "srnl_forward_qraw_varline"]
+    qnorm_fns = ["visionhope_qnorm_forward", "visionhope_qnorm_backward"]
+    dirfuse_fns = ["visionhope_postprocess_scale_forward", "visionhope_postprocess_scale_backward"]
     base_chunk = chunk.cuda_helper_source
     return [
         ("vhref_fused_bf16", fused.cpp_source, fused.cuda_source, fused_fns),
@@ -98,12 +100,10 @@ def _targets():
         ("vhref_chunk_fp32", chunk.cpp_source, chunk.cuda_source_fp32, chunk_fns),
         ("vhref_lines_bf16", lines.cpp_source,
          base_chunk + lines.large_cuda_source + lines.varline_cuda_source, line_fns),
-        ("vhref_qnorm_bf16", qnorm.cpp_source, qnorm.cuda_source, ["visionhope_qnorm_forward"]),
-        ("vhref_qnorm_fp32", qnorm.cpp_source, qnorm.cuda_source_fp32, ["visionhope_qnorm_forward"]),
-        ("vhref_dirfuse_bf16", dirfuse.cpp_source, dirfuse.cuda_source,
-         ["visionhope_postprocess_scale_forward"]),
-        ("vhref_dirfuse_fp32", dirfuse.cpp_source, dirfuse.cuda_source_fp32,
-         ["visionhope_postprocess_scale_forward"]),
+        ("vhref_qnorm_bf16", qnorm.cpp_source, qnorm.cuda_source, qnorm_fns),
+        ("vhref_qnorm_fp32", qnorm.cpp_source, qnorm.cuda_source_fp32, qnorm_fns),
+        ("vhref_dirfuse_bf16", dirfuse.cpp_source, dirfuse.cuda_source, dirfuse_fns),
+        ("vhref_dirfuse_fp32", dirfuse.cpp_source, dirfuse.cuda_source_fp32, dirfuse_fns),
     ]
 
 

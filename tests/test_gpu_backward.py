@@ -1,7 +1,9 @@
-"""Backward kernels (vh_qnorm_bwd, vh_dirfuse_bwd, vh_layernorm_bwd, vh_grn_bwd) through the
-autograd Functions of the drop-in modules, against fp64 CPU autograd of the gradient oracle
-(oracle/grad.py) on the same inputs.  Bar: normwise relative error 1e-5 for fp32 gradients,
-one 16-bit rounding (8e-3) where the gradient is returned in bf16/fp16 as the reference does."""
+"""Backward kernels (vh_qnorm_bwd, vh_dirfuse_bwd, vh_layernorm_bwd, vh_grn_bwd,
+vh_srnl_sequence_bwd) through the autograd Functions of the drop-in modules, against fp64 CPU
+autograd of the gradient oracle (oracle/grad.py) on the same inputs.  Bar: normwise relative
+error 1e-5 for fp32 gradients of the one-pass operators, 2e-4 through the SRNL recurrence (an fp32
+recurrence of up to 70 tokens against fp64), one 16-bit rounding (8e-3, 1e-2 through the
+recurrence) where the gradient is returned in bf16/fp16 as the reference does."""
 import pytest
 import torch
 
@@ -28,7 +30,8 @@ def test_qnorm_backward(dtype, heads, D, L):
 
     g = torch.Generator().manual_seed(heads * 100 + D + L)
     q = torch.randn(2, 4, L, heads * D, generator=g).to(dtype)
-    q[1, 2, 3, :D] = 0  # a zero vector: the clamped branch
+    if dtype != torch.float16:  # its gradient, g * 1e12, is beyond fp16's range
+        q[1, 2, 3, :D] = 0  # a zero vector: the clamped branch
     gout = torch.randn(2, 4, heads, L, D, generator=g)
     qd = q.to(DEV).requires_grad_(True)
     out = visionhope_qnorm(qd, heads, D)
@@ -171,7 +174,10 @@ def test_srnl_sequence_backward(q_normalized, per_chain, D, chunk, L, dtype, mem
     exp = og.grads(fn, [*mems, x.float(), q.float()], gy.to(dtype).float())
     names = ["M_m", "M_v", "M_k", "M_eta", "M_alpha", "x", "q"]
     for name, leaf, e in zip(names, leaves, exp):
-        assert leaf.grad is not None and leaf.grad.shape == e.shape, name
+        assert leaf.grad is not None and leaf.grad.shape == leaf.shape, name
+        if e is None:  # no path from this input to y (a one-chunk sequence never refreshes the state)
+            assert not leaf.grad.any(), name
+            continue
         tol = 2e-4 if leaf.grad.dtype == torch.float32 else 1e-2
         err = _rel(leaf.grad, e)
         assert err < tol, f"{name}: {err:.3e}"
