@@ -68,6 +68,9 @@ def parse():
                     help="time only the fused SRNL operator at the stage-1 shape (profiling aid)")
     ap.add_argument("--only-depthwise", action="store_true",
                     help="time the block's depthwise kernels and GRN apply at the model's shapes and exit")
+    ap.add_argument("--only-backward", action="store_true",
+                    help="time the backward (training) kernels at the operator and GRN/LN configurations' "
+                         "shapes, and the reference's own backward kernels beside them, and exit")
     ap.add_argument("--only-norms", action="store_true",
                     help="time only GRN and LayerNorm at the GRN/LN configuration's shapes")
     args = ap.parse_args()
@@ -605,6 +608,134 @@ def _time_calls(fn, iters, flush):
     return statistics.median(times), (_lib.launch_count - n0) // iters
 
 
+def roofline_backward(device, iters=5):
+    """The backward kernels at the configurations' shapes, each timed alone (L2 evicted before
+    every call, outside the events): query normalization and direction fusion at the operator
+    configuration (B = 64, 56 x 56, C = 96, bf16 activations as under autocast), LayerNorm and GRN
+    at the GRN/LN configuration's large shape (128 x 56 x 56 x 96, fp32), and the SRNL recurrence
+    backward at the operator configuration (1536 chains of 3136 tokens in chunks of 56, raw bf16
+    queries).  HBM-bound kernels report achieved GB/s of their algorithmic bytes (every input read
+    once, every output written once) against MEASURED_PEAKS.json; the recurrence reports
+    chain-tokens per second.  `reference` times the reference's own backward kernels (built from
+    its sources into oracle/_ref) on the same tensors where it has them."""
+    from visionhope_b200.srnl_core.chunk import recurrence_constants_tuple, sequence_backward
+    from visionhope_b200.utils.direction_fusion import postprocess_backward
+    from visionhope_b200.utils.grn_cuda import grn_backward, grn_forward
+    from visionhope_b200.utils.layer_norm_cuda import layernorm_rows, layernorm_rows_backward
+    from visionhope_b200.utils.query_normalization import _qnorm_forward, qnorm_backward
+
+    hbm = measured_peaks().get("hbm_gbs")
+    flush = l2_flush(device)
+    g = torch.Generator(device=device).manual_seed(9)
+    rows = []
+
+    def add(name, shape, fn, nbytes=None, units=None, unit_name=None, ref_fn=None):
+        ms, launches = _time_calls(fn, iters, flush)
+        row = {"kernel": name, "shape": shape, "ms": ms, "launches": launches}
+        if nbytes:
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            row.update(alg_bytes=nbytes, achieved_gbs=gbs, frac_of_measured_hbm=gbs / hbm if hbm else None)
+        if units:
+            row[unit_name] = units / (ms * 1e-3)
+        if ref_fn is not None:
+            try:
+                rms, _ = _time_calls(ref_fn, iters, flush)
+                row.update(reference_ms=rms, speedup_vs_reference=rms / ms)
+            except Exception as exc:  # the reference's kernels are optional here
+                row["reference"] = f"unavailable: {exc}"
+        rows.append(row)
+
+    def ref_mod(name):
+        try:
+            from oracle.build_ref import load_built
+            return load_built(name)
+        except Exception:
+            return None
+
+    # query normalization and direction fusion, operator configuration
+    B, H, W, heads, D = 64, 56, 56, 6, 16
+    L, C = H * W, heads * D
+    qr = torch.randn(B, 4, L, C, device=device, generator=g).to(torch.bfloat16)
+    qo, inv = _qnorm_forward(qr, heads, D, want_inv=True)
+    gq = torch.randn_like(qo)
+    rq = ref_mod("vhref_qnorm_bf16")
+    add("qnorm backward", [B, 4, L, C], lambda: qnorm_backward(gq, qo, inv, heads, D, torch.bfloat16),
+        nbytes=qo.numel() * (4 + 4 + 2) + inv.numel() * 4,
+        ref_fn=(lambda: rq.visionhope_qnorm_backward(gq, qo, inv, heads, D, True)) if rq else None)
+    del qo, gq
+    y = torch.randn(B, 4, heads, L, D, device=device, generator=g).to(torch.bfloat16)
+    xx = torch.randn(B, 4, heads, L, D, device=device, generator=g).to(torch.bfloat16)
+    skip = torch.randn(C, device=device, generator=g)
+    scale = torch.randn(4, C, device=device, generator=g)
+    gout = torch.randn(B, C, H, W, device=device, generator=g)
+    rd = ref_mod("vhref_dirfuse_bf16")
+    add("dirfuse backward (NCHW grad)", [B, 4, heads, L, D],
+        lambda: postprocess_backward(gout, y, xx, skip, scale, H, W),
+        nbytes=gout.numel() * 4 + y.numel() * 2 * 4,
+        ref_fn=(lambda: rd.visionhope_postprocess_scale_backward(gout, y, xx, skip, scale, H, W, False, False, 128))
+        if rd else None)
+    del y, xx, gout
+    # LayerNorm and GRN, GRN/LN configuration (large shape)
+    Bn, Hn, Wn, Cn = 128, 56, 56, 96
+    x = torch.randn(Bn, Cn, Hn, Wn, device=device, generator=g).contiguous(memory_format=torch.channels_last)
+    xr = x.permute(0, 2, 3, 1).reshape(-1, Cn)
+    w = torch.randn(Cn, device=device, generator=g)
+    bb = torch.randn(Cn, device=device, generator=g)
+    _, mean, rstd = layernorm_rows(xr, w, bb, 1e-6, want_stats=True)
+    gy = torch.randn_like(xr)
+    add("layernorm backward", [Bn, Hn, Wn, Cn], lambda: layernorm_rows_backward(gy, xr, w, mean, rstd),
+        nbytes=xr.numel() * 4 * 3)
+    gamma = torch.randn(Cn, device=device, generator=g) * 0.5
+    _, gx, invd = grn_forward(x, gamma, bb, 1e-6, want_stats=True)
+    gyn = torch.randn_like(x)
+    rg = ref_mod("vhref_grn")
+
+    def ref_grn():
+        s = torch.empty((Bn, Cn), device=device)
+        dg, db = torch.empty((Bn, Cn), device=device), torch.empty((Bn, Cn), device=device)
+        ssg = torch.empty((Bn,), device=device)
+        dx = torch.empty_like(x)
+        dgam, dbet = torch.empty(Cn, device=device), torch.empty(Cn, device=device)
+        rg.grn_backward_cuda(gyn, x, gamma, gx, invd, s, dg, db, ssg, dx, dgam, dbet)
+
+    add("grn backward", [Bn, Hn, Wn, Cn], lambda: grn_backward(gyn, x, gamma, gx, invd),
+        nbytes=x.numel() * 4 * 3, ref_fn=ref_grn if rg else None)
+    del x, xr, gy, gyn
+    # SRNL recurrence backward, operator configuration
+    mems = [torch.randn(4, heads, D, D, device=device, generator=g) * 0.3 for _ in range(3)]
+    mems += [torch.randn(4, heads, D, device=device, generator=g) * 0.6 for _ in range(2)]
+    xs = torch.randn(B, 4, heads, L, D, device=device, generator=g).to(torch.bfloat16)
+    qs = torch.randn(B, 4, L, C, device=device, generator=g).to(torch.bfloat16)
+    gys = torch.randn(B, 4, heads, L, D, device=device, generator=g)
+    chains = B * 4 * heads
+
+    def ref_train():
+        # The reference's own training step of the recurrence (chunk.py SRNLRawQueryFunction on its
+        # kernels: srnl_forward_qraw saving its buffers, then srnl_backward_qraw), against which
+        # ours is timed as forward + backward too.
+        leaves = [t.detach().requires_grad_(True) for t in (*mems, xs, qs)]
+        ref_chunk.srnl_raw_query(*leaves, W, heads, D).backward(gys.to(torch.bfloat16))
+
+    def ours_train():
+        from visionhope_b200.srnl_core.chunk import srnl_raw_query
+        leaves = [t.detach().requires_grad_(True) for t in (*mems, xs, qs)]
+        srnl_raw_query(*leaves, W, heads, D).backward(gys.to(torch.bfloat16))
+
+    try:
+        from oracle import refmodel
+        refmodel.load("native")
+        import visionhope.models.srnl_core.chunk as ref_chunk
+    except Exception:
+        ref_chunk = None
+    add("srnl recurrence backward (raw queries, chunk 56)", [B, 4, heads, L, D],
+        lambda: sequence_backward(mems, xs, qs, [W] * 4, gys, q_normalized=False),
+        units=chains * L, unit_name="chain_tokens_per_s")
+    add("srnl recurrence forward + backward (autograd, raw queries, chunk 56)", [B, 4, heads, L, D], ours_train,
+        units=chains * L, unit_name="chain_tokens_per_s", ref_fn=ref_train if ref_chunk is not None else None)
+    return {"backward": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+            "consts": list(recurrence_constants_tuple())}
+
+
 def roofline_depthwise(device, iters=10):
     """The block's depthwise kernels and the statistics-fed GRN at VisionHOPE-T's shapes, batch
     256 (the bench workload), each timed alone: achieved HBM GB/s of the algorithmic bytes
@@ -829,7 +960,7 @@ def main():
                     "e2e": {"value": ips, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
             return
-        if args.only_scan or args.only_norms or args.only_depthwise:
+        if args.only_scan or args.only_norms or args.only_depthwise or args.only_backward:
             if rank == 0:
                 torch.cuda.set_device(local)
                 dev = torch.device("cuda", local)
@@ -839,6 +970,8 @@ def main():
                            "ref_kernel": ref_kernel_compare(dev, args.batch)}
                 elif args.only_norms:
                     res = roofline_norms(dev, args.steps)
+                elif args.only_backward:
+                    res = roofline_backward(dev, max(args.steps, 3))
                 else:
                     res = roofline_depthwise(dev, args.steps)
                 print(json.dumps(res), flush=True)

@@ -76,135 +76,176 @@ int qnorm_bwd_dispatch(int D, const float* g, const float* q, const float* inv, 
 // l_d the position of pixel pix in scan d.  So for every (b, d, pixel, c):
 //   dy_d = scale[d, c] g,   dx_d = scale[d, c] skip_d[c] g,
 //   dscale[d, c] += g (y_d + skip_d[c] x_d),   dskip_d[c] += g scale[d, c] x_d.
-// CTA = (b, tile of kPix pixels, block of 32 channels); thread (channel lane, pixel lane).
-// Each CTA writes its per-channel partial sums; dirfuse_reduce_kernel adds the partials of
-// all CTAs in index order.
+// CTA = (b, head, tile of kPix row-major pixels), as the forward: the tile's gradient is staged
+// in shared memory first (read along whichever axis is contiguous), then each thread takes
+// (pixel, group of 4 channels) items, always of the same group, and keeps its partial sums in
+// registers; the CTA adds them over its threads in a fixed order and writes one partial row
+// per (image, tile).  reduce_parts_kernel adds the partial rows in order.
 constexpr int kPix = 64;
-constexpr int kPixLanes = kThreads / 32;
 
-__device__ __forceinline__ int64_t scan_pos(int d, int64_t pix, int H, int W) {
-    const int64_t L = (int64_t)H * W;
-    const int64_t i = pix / W, j = pix - i * W;
-    switch (d) {
-        case 0: return pix;
-        case 1: return L - 1 - pix;
-        case 2: return j * H + i;
-        default: return L - 1 - (j * H + i);
-    }
-}
-
-template <typename T>
+template <int D, typename T>
 __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
     const float* __restrict__ g, int64_t gsb, int64_t gsc, int64_t gsh, int64_t gsw, const T* __restrict__ y,
     const T* __restrict__ x, const float* __restrict__ skip, int skip_per_dir, const float* __restrict__ scale,
-    T* __restrict__ dy, T* __restrict__ dx, float* __restrict__ part, int heads, int H, int W, int D) {
-    const int C = heads * D;
+    T* __restrict__ dy, T* __restrict__ dx, float* __restrict__ part, int heads, int H, int W) {
+    constexpr int G4 = D / 4;
+    static_assert(kThreads % G4 == 0, "a thread keeps one channel group");
+    __shared__ float gt[D][kPix + 1];
+    __shared__ float red[kThreads / G4][8][4];
     const int64_t L = (int64_t)H * W;
+    const int C = heads * D;
     const int tiles = (int)((L + kPix - 1) / kPix);
-    const int b = blockIdx.z;
-    const int tile = blockIdx.x;
-    const int c = blockIdx.y * 32 + (threadIdx.x & 31);
-    const int pl = threadIdx.x >> 5;
-    float ps[4] = {0.f, 0.f, 0.f, 0.f}, pk[4] = {0.f, 0.f, 0.f, 0.f};
-    if (c < C) {
-        const int head = c / D, i = c - head * D;
-        float sc[4], sk[4];
-#pragma unroll
-        for (int d = 0; d < 4; ++d) {
-            sc[d] = scale[d * C + c];
-            sk[d] = skip[(skip_per_dir ? d * C : 0) + c];
-        }
-        for (int k = pl; k < kPix; k += kPixLanes) {
-            const int64_t pix = (int64_t)tile * kPix + k;
-            if (pix >= L) break;
+    const int tile = blockIdx.x % tiles;
+    const int head = (blockIdx.x / tiles) % heads;
+    const int b = blockIdx.x / (tiles * heads);
+    const int64_t pix0 = (int64_t)tile * kPix;
+    const bool pix_fast = gsc != 1;  // NCHW-like gradient: pixels contiguous per channel
+    for (int it = threadIdx.x; it < D * kPix; it += kThreads) {
+        const int k = pix_fast ? it % kPix : it / D, ch = pix_fast ? it / kPix : it % D;
+        const int64_t pix = pix0 + k;
+        float v = 0.f;
+        if (pix < L) {
             const int64_t pi = pix / W, pj = pix - pi * W;
-            const float gv = g[b * gsb + c * gsc + pi * gsh + pj * gsw];
-#pragma unroll
-            for (int d = 0; d < 4; ++d) {
-                const int64_t o = (((int64_t)b * 4 + d) * heads + head) * L * D + scan_pos(d, pix, H, W) * D + i;
-                const float yv = to_f(y[o]), xv = to_f(x[o]);
-                dy[o] = from_f<T>(sc[d] * gv);
-                dx[o] = from_f<T>(sc[d] * sk[d] * gv);
-                ps[d] = fmaf(gv, fmaf(sk[d], xv, yv), ps[d]);
-                pk[d] = fmaf(gv * sc[d], xv, pk[d]);
-            }
+            v = g[b * gsb + (int64_t)(head * D + ch) * gsc + pi * gsh + pj * gsw];
         }
-    }
-    // Reduce over the pixel lanes in lane order, then write this CTA's partials.
-    __shared__ float red[kPixLanes][8][32];
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-        red[pl][d][threadIdx.x & 31] = ps[d];
-        red[pl][4 + d][threadIdx.x & 31] = pk[d];
+        gt[ch][k] = v;
     }
     __syncthreads();
-    if (pl == 0 && c < C) {
-        float s[8];
+    const int grp = threadIdx.x % G4;
+    const int c0 = head * D + grp * 4;
+    float sc[4][4], sk[4][4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) s[q] = red[0][q][threadIdx.x];
-        for (int r = 1; r < kPixLanes; ++r)
+    for (int d = 0; d < 4; ++d)
 #pragma unroll
-            for (int q = 0; q < 8; ++q) s[q] += red[r][q][threadIdx.x];
-        const int64_t cta = (int64_t)b * tiles + tile;
-        float* dst = part + cta * 8 * C;
+        for (int e = 0; e < 4; ++e) {
+            sc[d][e] = scale[d * C + c0 + e];
+            sk[d][e] = skip[(skip_per_dir ? d * C : 0) + c0 + e];
+        }
+    float ps[4][4] = {}, pk[4][4] = {};
+    for (int it = threadIdx.x; it < kPix * G4; it += kThreads) {
+        const int k = it / G4;
+        const int64_t pix = pix0 + k;
+        if (pix >= L) break;
+        const int64_t pi = pix / W, pj = pix - pi * W;
+        const int64_t lhw = pix, lwh = pj * H + pi;
+        const int64_t ls[4] = {lhw, L - 1 - lhw, lwh, L - 1 - lwh};
+        const float gv[4] = {gt[grp * 4][k], gt[grp * 4 + 1][k], gt[grp * 4 + 2][k], gt[grp * 4 + 3][k]};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) dst[q * C + c] = s[q];
+        for (int d = 0; d < 4; ++d) {
+            const int64_t off = ((((int64_t)b * 4 + d) * heads + head) * L + ls[d]) * D + grp * 4;
+            const float4 yv = load4(y + off), xv = load4(x + off);
+            const float yy[4] = {yv.x, yv.y, yv.z, yv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w};
+            float o1[4], o2[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                o1[e] = sc[d][e] * gv[e];
+                o2[e] = sc[d][e] * sk[d][e] * gv[e];
+                ps[d][e] = fmaf(gv[e], fmaf(sk[d][e], xs[e], yy[e]), ps[d][e]);
+                pk[d][e] = fmaf(gv[e] * sc[d][e], xs[e], pk[d][e]);
+            }
+            store4(dy + off, make_float4(o1[0], o1[1], o1[2], o1[3]));
+            store4(dx + off, make_float4(o2[0], o2[1], o2[2], o2[3]));
+        }
+    }
+    // Threads of one channel group: tid = grp + G4 * slot.  Stage, then add the slots in order.
+    const int slot = threadIdx.x / G4;
+    constexpr int kSlots = kThreads / G4;
+    float* mine = &red[0][0][0];  // [slot][8][4] per group, in rounds of one group
+    for (int gg = 0; gg < G4; ++gg) {
+        if (grp == gg) {
+#pragma unroll
+            for (int d = 0; d < 4; ++d)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    mine[(slot * 8 + d) * 4 + e] = ps[d][e];
+                    mine[(slot * 8 + 4 + d) * 4 + e] = pk[d][e];
+                }
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {  // 8 quantities x 4 channels of group gg
+            const int q = threadIdx.x >> 2, e = threadIdx.x & 3;
+            float sum = 0.f;
+            for (int sl = 0; sl < kSlots; ++sl) sum += mine[(sl * 8 + q) * 4 + e];
+            part[((int64_t)(b * tiles + tile) * 8 + q) * C + head * D + gg * 4 + e] = sum;
+        }
+        __syncthreads();
     }
 }
 
-// dscale[d, c] and dskip (C or 4 C values) from the partials of `nparts` CTAs, in CTA order.
-__global__ void __launch_bounds__(kThreads) dirfuse_reduce_kernel(const float* __restrict__ part, int64_t nparts,
-                                                                  int C, int skip_per_dir, float* __restrict__ dscale,
-                                                                  float* __restrict__ dskip) {
+// out[q][c] = sum_p part[p][q][c] for q < nq, partial rows p in order; CTA = (32 columns, q),
+// threads (column, part lane), the part lanes added in lane order.
+__global__ void __launch_bounds__(kThreads) reduce_parts_kernel(const float* __restrict__ part, int64_t nparts,
+                                                                int nq, int C, float* __restrict__ out) {
+    const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+    const int q = blockIdx.y;
+    const int pl = threadIdx.x >> 5;
+    float sum = 0.f;
+    if (c < C)
+        for (int64_t p = pl; p < nparts; p += kThreads / 32) sum += part[(p * nq + q) * C + c];
+    __shared__ float red[kThreads / 32][32];
+    red[pl][threadIdx.x & 31] = sum;
+    __syncthreads();
+    if (pl == 0 && c < C) {
+        float t = red[0][threadIdx.x];
+        for (int k = 1; k < kThreads / 32; ++k) t += red[k][threadIdx.x];
+        out[(int64_t)q * C + c] = t;
+    }
+}
+
+// dscale and dskip from the 8 summed rows: rows 0-3 dscale[d], rows 4-7 dskip[d]
+// (added over d, in order, when the skip is shared).
+__global__ void dirfuse_finish_kernel(const float* __restrict__ sums, int C, int skip_per_dir,
+                                      float* __restrict__ dscale, float* __restrict__ dskip) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
-    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int64_t p = 0; p < nparts; ++p)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) s[q] += part[p * 8 * C + q * C + c];
-#pragma unroll
-    for (int d = 0; d < 4; ++d) dscale[d * C + c] = s[d];
+    for (int d = 0; d < 4; ++d) dscale[d * C + c] = sums[d * C + c];
     if (skip_per_dir) {
 #pragma unroll
-        for (int d = 0; d < 4; ++d) dskip[d * C + c] = s[4 + d];
+        for (int d = 0; d < 4; ++d) dskip[d * C + c] = sums[(4 + d) * C + c];
     } else {
-        dskip[c] = ((s[4] + s[5]) + s[6]) + s[7];
+        dskip[c] = ((sums[4 * C + c] + sums[5 * C + c]) + sums[6 * C + c]) + sums[7 * C + c];
     }
 }
-
 
 // ---- LayerNorm over channels (layer_norm_cuda.py:59-119) ----------------------------------
 // x_hat = (x - mean) rstd, y = w x_hat + b.  Per row r:
 //   dx = rstd (w dy - mean_c(w dy) - x_hat mean_c(w dy x_hat)),
 // and over rows: dw = sum_r dy x_hat, db = sum_r dy.
-// ln_dx_kernel: one warp per row, lanes over channels (two passes over the row: the sums, then
-// dx).  ln_param_kernel: CTA = (block of kLnRows rows, block of 32 channels), partial sums of
-// the block written per CTA; param_reduce_kernel adds them in row-block order.
-constexpr int kLnRows = 64;
+// ln_dx_kernel: eight lanes per row (two passes over the row: the sums, then dx).
+// ln_param_kernel: CTA = (block of kLnRows rows, block of 32 channels), partial sums of
+// the block written per CTA; reduce_parts_kernel adds them in row-block order.
+constexpr int kLnRows = 256;
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) ln_dx_kernel(const float* __restrict__ dy, const T* __restrict__ x,
                                                          const float* __restrict__ w, const float* __restrict__ mean,
                                                          const float* __restrict__ rstd, T* __restrict__ dx,
                                                          int64_t rows, int C) {
-    const int lane = threadIdx.x & 31;
-    const int64_t r = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
-    if (r >= rows) return;
-    const float* g = dy + r * C;
-    const T* xr = x + r * C;
-    const float mu = mean[r], rs = rstd[r];
+    // Eight lanes per row, four rows per warp: each load instruction covers four 32-byte runs.
+    const int lane = threadIdx.x & 31, sl = lane & 7;
+    const int64_t r = ((int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const bool live = r < rows;
+    const float* g = dy + (live ? r : 0) * C;
+    const T* xr = x + (live ? r : 0) * C;
+    const float mu = live ? mean[r] : 0.f, rs = live ? rstd[r] : 0.f;
     float s1 = 0.f, s2 = 0.f;
-    for (int c = lane; c < C; c += 32) {
-        const float wg = w[c] * g[c];
-        s1 += wg;
-        s2 = fmaf(wg, (to_f(xr[c]) - mu) * rs, s2);
+    if (live)
+        for (int c = sl; c < C; c += 8) {
+            const float wg = w[c] * g[c];
+            s1 += wg;
+            s2 = fmaf(wg, (to_f(xr[c]) - mu) * rs, s2);
+        }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
     }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
+    if (!live) return;
     const float invC = 1.f / (float)C;
     const float a = s1 * invC, bq = s2 * invC;
     T* dxr = dx + r * C;
-    for (int c = lane; c < C; c += 32) {
+    for (int c = sl; c < C; c += 8) {
         const float xh = (to_f(xr[c]) - mu) * rs;
         dxr[c] = from_f<T>((w[c] * g[c] - a - xh * bq) * rs);
     }
@@ -242,39 +283,29 @@ __global__ void __launch_bounds__(kThreads) ln_param_kernel(const float* __restr
     }
 }
 
-// out0[c] = sum_p part[p][0][c], out1[c] = sum_p part[p][1][c], p in order.
-__global__ void __launch_bounds__(kThreads) param_reduce_kernel(const float* __restrict__ part, int64_t nparts, int C,
-                                                                float* __restrict__ out0, float* __restrict__ out1) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
-    float a = 0.f, b = 0.f;
-    for (int64_t p = 0; p < nparts; ++p) {
-        a += part[(p * 2) * C + c];
-        b += part[(p * 2 + 1) * C + c];
-    }
-    out0[c] = a;
-    out1[c] = b;
-}
-
 // ---- GRN (grn_cuda.cu:126-265) ------------------------------------------------------------
 // y = x (1 + gamma Nx) + beta, Nx = Gx inv, Gx[b, c] = ||x[b, :, c]||, inv = 1 / (mean_c Gx + eps).
 // With t[b, c] = sum_s dy x and s = gamma t:
 //   dgamma = sum_b Nx t,  dbeta = sum_b sum_s dy,
 //   dGx = s inv - (sum_c s Gx) inv^2 / C,
 //   dx = dy (1 + gamma Nx) + dGx x / Gx   (0 where Gx = 0).
-// grn_stats_bwd_kernel: CTA = (b, block of 32 channels), pixel lanes reduced in lane order.
+// grn_stats_bwd_kernel: CTA = (b, block of 32 channels, slice of the pixels), pixel lanes
+// reduced in lane order; the slices' partial sums are added in slice order afterwards.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) grn_stats_bwd_kernel(const float* __restrict__ dy,
-                                                                 const T* __restrict__ x, int S, int C,
-                                                                 float* __restrict__ t_out,
-                                                                 float* __restrict__ dbeta_bc) {
+                                                                 const T* __restrict__ x, int S, int C, int nsl,
+                                                                 float* __restrict__ t_part,
+                                                                 float* __restrict__ db_part) {
     const int b = blockIdx.x;
     const int c = blockIdx.y * 32 + (threadIdx.x & 31);
+    const int sl = blockIdx.z;
     const int pl = threadIdx.x >> 5;
+    const int per = (S + nsl - 1) / nsl;
+    const int s0 = sl * per, s1 = min(S, s0 + per);
     float t = 0.f, sb = 0.f;
     if (c < C) {
         const int64_t base = (int64_t)b * S * C + c;
-        for (int s = pl; s < S; s += kThreads / 32) {
+        for (int s = s0 + pl; s < s1; s += kThreads / 32) {
             const float g = dy[base + (int64_t)s * C];
             t = fmaf(g, to_f(x[base + (int64_t)s * C]), t);
             sb += g;
@@ -290,17 +321,34 @@ __global__ void __launch_bounds__(kThreads) grn_stats_bwd_kernel(const float* __
             a += red[k][0][threadIdx.x];
             bsum += red[k][1][threadIdx.x];
         }
-        t_out[(int64_t)b * C + c] = a;
-        dbeta_bc[(int64_t)b * C + c] = bsum;
+        t_part[((int64_t)b * nsl + sl) * C + c] = a;
+        db_part[((int64_t)b * nsl + sl) * C + c] = bsum;
     }
 }
 
-// One CTA per image: dGx[b, :] from t, gamma, Gx and inv (the sum over channels in a fixed
-// tree order).
-__global__ void __launch_bounds__(kThreads) grn_dgx_kernel(const float* __restrict__ t, const float* __restrict__ gamma,
-                                                           const float* __restrict__ gx,
-                                                           const float* __restrict__ inv_den, int C,
-                                                           float* __restrict__ dgx) {
+// t[b, c] and dbeta_bc[b, c]: the slices added in order.
+__global__ void grn_slices_kernel(const float* __restrict__ t_part, const float* __restrict__ db_part, int B, int C,
+                                  int nsl, float* __restrict__ t, float* __restrict__ dbeta_bc) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)B * C) return;
+    const int64_t b = i / C, c = i % C;
+    float a = 0.f, bsum = 0.f;
+    for (int sl = 0; sl < nsl; ++sl) {
+        a += t_part[(b * nsl + sl) * C + c];
+        bsum += db_part[(b * nsl + sl) * C + c];
+    }
+    t[i] = a;
+    dbeta_bc[i] = bsum;
+}
+
+// One CTA per image: the factors of dx = dy f1 + x f2 for each channel, f1 = 1 + gamma Nx and
+// f2 = dGx / Gx (0 where Gx = 0), with dGx = gamma t inv - (sum_c gamma t Gx) inv^2 / C (the sum
+// over channels in a fixed tree order).
+__global__ void __launch_bounds__(kThreads) grn_factor_bwd_kernel(const float* __restrict__ t,
+                                                                  const float* __restrict__ gamma,
+                                                                  const float* __restrict__ gx,
+                                                                  const float* __restrict__ inv_den, int C,
+                                                                  float* __restrict__ f1, float* __restrict__ f2) {
     const int b = blockIdx.x;
     __shared__ float red[kThreads / 32];
     float sum = 0.f;
@@ -312,24 +360,37 @@ __global__ void __launch_bounds__(kThreads) grn_dgx_kernel(const float* __restri
 #pragma unroll
     for (int k = 0; k < kThreads / 32; ++k) tot += red[k];
     const float inv = inv_den[b];
-    for (int c = threadIdx.x; c < C; c += kThreads)
-        dgx[(int64_t)b * C + c] = gamma[c] * t[(int64_t)b * C + c] * inv - tot * inv * inv / (float)C;
+    for (int c = threadIdx.x; c < C; c += kThreads) {
+        const int64_t i = (int64_t)b * C + c;
+        const float g = gx[i];
+        const float dgx = gamma[c] * t[i] * inv - tot * inv * inv / (float)C;
+        f1[i] = fmaf(gamma[c], g * inv, 1.f);
+        f2[i] = g > 0.f ? dgx / g : 0.f;
+    }
 }
 
-template <typename T>
+// dx = dy f1[b, c] + x f2[b, c]; grid (vector blocks, image).  Vectors of 4 channels when C is a
+// multiple of 4 (VEC), single elements otherwise.
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreads) grn_dx_kernel(const float* __restrict__ dy, const T* __restrict__ x,
-                                                          const float* __restrict__ gamma, const float* __restrict__ gx,
-                                                          const float* __restrict__ inv_den,
-                                                          const float* __restrict__ dgx, T* __restrict__ dx, int S,
-                                                          int C, int64_t n) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C);
-        const int64_t b = i / ((int64_t)S * C);
-        const float g = gx[b * C + c];
-        const float nx = g * inv_den[b];
-        const float xv = to_f(x[i]);
-        const float igx = g > 0.f ? 1.f / g : 0.f;
-        dx[i] = from_f<T>(fmaf(dy[i], fmaf(gamma[c], nx, 1.f), dgx[b * C + c] * xv * igx));
+                                                          const float* __restrict__ f1, const float* __restrict__ f2,
+                                                          T* __restrict__ dx, int S, int C) {
+    const int b = blockIdx.y;
+    const int W = VEC ? 4 : 1;
+    const int64_t per = (int64_t)S * C / W;
+    const int64_t base = (int64_t)b * S * C;
+    const float* f1b = f1 + (int64_t)b * C;
+    const float* f2b = f2 + (int64_t)b * C;
+    for (int64_t v = (int64_t)blockIdx.x * kThreads + threadIdx.x; v < per; v += (int64_t)gridDim.x * kThreads) {
+        const int64_t i = base + v * W;
+        const int c = (int)((v * W) % C);
+        if constexpr (VEC) {
+            const float4 g = load4(dy + i), xv = load4(x + i), a = load4(f1b + c), bq = load4(f2b + c);
+            store4(dx + i, make_float4(fmaf(g.x, a.x, xv.x * bq.x), fmaf(g.y, a.y, xv.y * bq.y),
+                                       fmaf(g.z, a.z, xv.z * bq.z), fmaf(g.w, a.w, xv.w * bq.w)));
+        } else {
+            dx[i] = from_f<T>(fmaf(dy[i], f1b[c], to_f(x[i]) * f2b[c]));
+        }
     }
 }
 
@@ -395,7 +456,7 @@ extern "C" int vh_qnorm_bwd(const float* grad_out, const float* q_out, const flo
 extern "C" int64_t vh_dirfuse_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t height, int32_t width,
                                                   int32_t head_dim) {
     if (batch <= 0 || heads <= 0 || height <= 0 || width <= 0 || head_dim <= 0) return 0;
-    return dirfuse_parts(batch, height, width) * 8 * (int64_t)heads * head_dim * (int64_t)sizeof(float);
+    return (dirfuse_parts(batch, height, width) + 1) * 8 * (int64_t)heads * head_dim * (int64_t)sizeof(float);
 }
 
 extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c, int64_t gs_h, int64_t gs_w,
@@ -417,26 +478,43 @@ extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c,
         return fail(VH_E_RANGE, "vh_dirfuse_bwd: too many elements");
     const int C = heads * head_dim;
     const int tiles = (int)((L + kPix - 1) / kPix);
+    if (!head_dim_ok(head_dim)) return fail(VH_E_HEADDIM, "vh_dirfuse_bwd: unsupported head_dim %d", head_dim);
+    if (!aligned(y, io_dtype == VH_F32 ? 16 : 8) || !aligned(x, io_dtype == VH_F32 ? 16 : 8) ||
+        !aligned(grad_y, io_dtype == VH_F32 ? 16 : 8) || !aligned(grad_x, io_dtype == VH_F32 ? 16 : 8))
+        return fail(VH_E_ALIGN, "vh_dirfuse_bwd: misaligned pointers");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t nparts = dirfuse_parts(batch, height, width);
     float* part = static_cast<float*>(workspace);
+    float* sums = part + nparts * 8 * C;
+    const int64_t grid = (int64_t)batch * heads * tiles;
+    if (grid > INT32_MAX) return fail(VH_E_RANGE, "vh_dirfuse_bwd: too many tiles");
     int rc = by_dtype(io_dtype, [&](auto t) {
         using T = decltype(t);
-        const dim3 grid(tiles, (C + 31) / 32, batch);
-        dirfuse_bwd_kernel<T><<<grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, static_cast<const T*>(y),
-                                                         static_cast<const T*>(x), skip, skip_per_dir ? 1 : 0, scale,
-                                                         static_cast<T*>(grad_y), static_cast<T*>(grad_x), part,
-                                                         heads, height, width, head_dim);
+        const T* yp = static_cast<const T*>(y);
+        const T* xp = static_cast<const T*>(x);
+        T* dyp = static_cast<T*>(grad_y);
+        T* dxp = static_cast<T*>(grad_x);
+        const int spd = skip_per_dir ? 1 : 0;
+        switch (head_dim) {
+            case 4: dirfuse_bwd_kernel<4, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+            case 8: dirfuse_bwd_kernel<8, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+            case 16: dirfuse_bwd_kernel<16, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+            case 32: dirfuse_bwd_kernel<32, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+            default: dirfuse_bwd_kernel<64, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+        }
         return launch_status("vh_dirfuse_bwd");
     });
     if (rc) return rc;
-    dirfuse_reduce_kernel<<<(C + kThreads - 1) / kThreads, kThreads, 0, st>>>(
-        part, dirfuse_parts(batch, height, width), C, skip_per_dir ? 1 : 0, grad_scale, grad_skip);
-    return launch_status("vh_dirfuse_bwd (reduce)");
+    reduce_parts_kernel<<<dim3((C + 31) / 32, 8), kThreads, 0, st>>>(part, nparts, 8, C, sums);
+    if ((rc = launch_status("vh_dirfuse_bwd (reduce)"))) return rc;
+    dirfuse_finish_kernel<<<(C + kThreads - 1) / kThreads, kThreads, 0, st>>>(sums, C, skip_per_dir ? 1 : 0,
+                                                                              grad_scale, grad_skip);
+    return launch_status("vh_dirfuse_bwd (finish)");
 }
 
 extern "C" int64_t vh_layernorm_bwd_workspace_bytes(int64_t rows, int32_t channels) {
     if (rows <= 0 || channels <= 0) return 0;
-    return ((rows + kLnRows - 1) / kLnRows) * 2 * (int64_t)channels * (int64_t)sizeof(float);
+    return (((rows + kLnRows - 1) / kLnRows) + 1) * 2 * (int64_t)channels * (int64_t)sizeof(float);
 }
 
 extern "C" int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dtype, const float* weight,
@@ -457,7 +535,7 @@ extern "C" int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dt
     float* part = static_cast<float*>(workspace);
     int rc = by_dtype(x_dtype, [&](auto t) {
         using T = decltype(t);
-        const int64_t grid = (rows + kThreads / 32 - 1) / (kThreads / 32);
+        const int64_t grid = (rows + 4 * (kThreads / 32) - 1) / (4 * (kThreads / 32));
         if (grid > INT32_MAX) return fail(VH_E_RANGE, "vh_layernorm_bwd: too many rows");
         ln_dx_kernel<T><<<(unsigned)grid, kThreads, 0, st>>>(grad_y, static_cast<const T*>(x), weight, mean, rstd,
                                                               static_cast<T*>(grad_x), rows, channels);
@@ -468,14 +546,29 @@ extern "C" int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dt
         return launch_status("vh_layernorm_bwd (params)");
     });
     if (rc) return rc;
-    param_reduce_kernel<<<(channels + kThreads - 1) / kThreads, kThreads, 0, st>>>(part, rblocks, channels,
-                                                                                     grad_weight, grad_bias);
-    return launch_status("vh_layernorm_bwd (reduce)");
+    float* sums = part + rblocks * 2 * channels;
+    reduce_parts_kernel<<<dim3((channels + 31) / 32, 2), kThreads, 0, st>>>(part, rblocks, 2, channels, sums);
+    if ((rc = launch_status("vh_layernorm_bwd (reduce)"))) return rc;
+    if (cudaMemcpyAsync(grad_weight, sums, sizeof(float) * channels, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(grad_bias, sums + channels, sizeof(float) * channels, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return fail(VH_E_DEVICE, "vh_layernorm_bwd: copy of the parameter gradients failed");
+    return 0;
 }
+
+namespace {
+constexpr int kGrnMaxSlices = 16;
+// Pixel slices per image: enough CTAs for about four per SM.
+int grn_slices(int batch, int channels, int64_t S) {
+    const int64_t ctas = (int64_t)batch * ((channels + 31) / 32);
+    int64_t n = (4 * (int64_t)sm_count() + ctas - 1) / ctas;
+    n = std::min<int64_t>(n, std::max<int64_t>(1, S / 64));
+    return (int)std::max<int64_t>(1, std::min<int64_t>(n, kGrnMaxSlices));
+}
+}  // namespace
 
 extern "C" int64_t vh_grn_bwd_workspace_bytes(int32_t batch, int32_t channels) {
     if (batch <= 0 || channels <= 0) return 0;
-    return 3 * (int64_t)batch * channels * (int64_t)sizeof(float);
+    return (4 + 2 * kGrnMaxSlices) * (int64_t)batch * channels * (int64_t)sizeof(float);
 }
 
 extern "C" int vh_grn_bwd(const float* grad_y, const void* x, int32_t x_dtype, const float* gamma, const float* gx,
@@ -497,19 +590,36 @@ extern "C" int vh_grn_bwd(const float* grad_y, const void* x, int32_t x_dtype, c
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* t = static_cast<float*>(workspace);
     float* dbeta_bc = t + (int64_t)batch * channels;
-    float* dgx = dbeta_bc + (int64_t)batch * channels;
+    float* f1 = dbeta_bc + (int64_t)batch * channels;
+    float* f2 = f1 + (int64_t)batch * channels;
+    float* t_part = f2 + (int64_t)batch * channels;
+    const int nsl = grn_slices(batch, channels, S);
+    float* db_part = t_part + (int64_t)batch * nsl * channels;
+    if (batch > 65535) return fail(VH_E_RANGE, "vh_grn_bwd: batch above 65535");
     return by_dtype(x_dtype, [&](auto tag) {
         using T = decltype(tag);
         const T* xp = static_cast<const T*>(x);
-        grn_stats_bwd_kernel<T><<<dim3(batch, (channels + 31) / 32), kThreads, 0, st>>>(grad_y, xp, (int)S, channels,
-                                                                                      t, dbeta_bc);
+        grn_stats_bwd_kernel<T><<<dim3(batch, (channels + 31) / 32, nsl), kThreads, 0, st>>>(
+            grad_y, xp, (int)S, channels, nsl, t_part, db_part);
         int r = launch_status("vh_grn_bwd (stats)");
         if (r) return r;
-        grn_dgx_kernel<<<batch, kThreads, 0, st>>>(t, gamma, gx, inv_den, channels, dgx);
-        if ((r = launch_status("vh_grn_bwd (dGx)"))) return r;
-        const int grid = (int)std::min<int64_t>((n + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
-        grn_dx_kernel<T><<<grid, kThreads, 0, st>>>(grad_y, xp, gamma, gx, inv_den, dgx, static_cast<T*>(grad_x),
-                                                    (int)S, channels, n);
+        const int64_t bc = (int64_t)batch * channels;
+        grn_slices_kernel<<<(unsigned)((bc + kThreads - 1) / kThreads), kThreads, 0, st>>>(t_part, db_part, batch,
+                                                                                           channels, nsl, t, dbeta_bc);
+        if ((r = launch_status("vh_grn_bwd (slices)"))) return r;
+        grn_factor_bwd_kernel<<<batch, kThreads, 0, st>>>(t, gamma, gx, inv_den, channels, f1, f2);
+        if ((r = launch_status("vh_grn_bwd (factors)"))) return r;
+        const bool vec = channels % 4 == 0 && aligned(grad_y, 16) && aligned(x, 4 * dtype_size(x_dtype)) &&
+                         aligned(grad_x, 4 * dtype_size(x_dtype));
+        const int64_t per = S * channels / (vec ? 4 : 1);
+        const unsigned gx_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((per + kThreads - 1) / kThreads,
+                                                                                     (int64_t)sm_count() * 8 / batch + 1));
+        if (vec)
+            grn_dx_kernel<T, true><<<dim3(gx_blocks, batch), kThreads, 0, st>>>(grad_y, xp, f1, f2, static_cast<T*>(grad_x),
+                                                                               (int)S, channels);
+        else
+            grn_dx_kernel<T, false><<<dim3(gx_blocks, batch), kThreads, 0, st>>>(grad_y, xp, f1, f2, static_cast<T*>(grad_x),
+                                                                                (int)S, channels);
         if ((r = launch_status("vh_grn_bwd (dx)"))) return r;
         grn_param_kernel<<<(channels + kThreads - 1) / kThreads, kThreads, 0, st>>>(t, gx, inv_den, dbeta_bc, batch,
                                                                                    channels, grad_gamma, grad_beta);
