@@ -33,6 +33,7 @@ import subprocess
 import sys
 import tempfile
 import time
+import types
 from pathlib import Path
 
 import torch
@@ -612,7 +613,8 @@ def roofline_backward(device, iters=5):
     """The backward kernels at the configurations' shapes, each timed alone (L2 evicted before
     every call, outside the events): query normalization and direction fusion at the operator
     configuration (B = 64, 56 x 56, C = 96, bf16 activations as under autocast), LayerNorm and GRN
-    at the GRN/LN configuration's large shape (128 x 56 x 56 x 96, fp32), and the SRNL recurrence
+    at the GRN/LN configuration's large shape (128 x 56 x 56 x 96, fp32), the LayerScale residual
+    add (forward and backward; fp32 residual, bf16 branch) at that shape, and the SRNL recurrence
     backward at the operator configuration (1536 chains of 3136 tokens in chunks of 56, raw bf16
     queries).  HBM-bound kernels report achieved GB/s of their algorithmic bytes (every input read
     once, every output written once) against MEASURED_PEAKS.json; the recurrence reports
@@ -675,6 +677,14 @@ def roofline_backward(device, iters=5):
         ref_fn=(lambda: rd.visionhope_postprocess_scale_backward(gout, y, xx, skip, scale, H, W, False, False, 128))
         if rd else None)
     del y, xx, gout
+    try:
+        from oracle import refmodel
+        refmodel.load("native")
+        import visionhope.models.srnl_core.chunk as ref_chunk
+        import visionhope.utils.layer_norm_cuda as ref_ln
+        import visionhope.utils.residual as ref_res
+    except Exception:
+        ref_chunk = ref_ln = ref_res = None
     # LayerNorm and GRN, GRN/LN configuration (large shape)
     Bn, Hn, Wn, Cn = 128, 56, 56, 96
     x = torch.randn(Bn, Cn, Hn, Wn, device=device, generator=g).contiguous(memory_format=torch.channels_last)
@@ -683,8 +693,29 @@ def roofline_backward(device, iters=5):
     bb = torch.randn(Cn, device=device, generator=g)
     _, mean, rstd = layernorm_rows(xr, w, bb, 1e-6, want_stats=True)
     gy = torch.randn_like(xr)
+    # The reference's Triton backward (utils/layer_norm_cuda.py:150-185) called on the same
+    # saved tensors through its autograd Function's backward.
+    ln_ctx = types.SimpleNamespace(saved_tensors=(x, w, mean, rstd), shape=(Bn, Cn, Hn, Wn))
+    gy4 = gy.view(Bn, Hn, Wn, Cn).permute(0, 3, 1, 2)
     add("layernorm backward", [Bn, Hn, Wn, Cn], lambda: layernorm_rows_backward(gy, xr, w, mean, rstd),
-        nbytes=xr.numel() * 4 * 3)
+        nbytes=xr.numel() * 4 * 3,
+        ref_fn=(lambda: ref_ln._VisionHOPELayerNorm2dFunction.backward(ln_ctx, gy4)) if ref_ln else None)
+    # LayerScale residual add (fp32 residual, bf16 branch as under autocast) and its backward
+    from visionhope_b200.utils.residual import residual_add_backward, residual_add_forward
+    br = torch.randn(Bn, Cn, Hn, Wn, device=device, generator=g).to(torch.bfloat16).contiguous(
+        memory_format=torch.channels_last)
+    lsg = torch.randn(Cn, 1, 1, device=device, generator=g)
+    keep = torch.ones(Bn, device=device)
+    rs_ctx = types.SimpleNamespace(save_for_backward=lambda *t: None, saved_tensors=(br, lsg, keep),
+                                   shape=(Bn, Cn, Hn, Wn))
+    add("residual add forward", [Bn, Hn, Wn, Cn], lambda: residual_add_forward(x, br, lsg, keep),
+        nbytes=x.numel() * (4 + 2 + 4),
+        ref_fn=(lambda: ref_res._VisionHOPEResidualFunction.forward(rs_ctx, x, br, lsg, keep)) if ref_res else None)
+    gres = torch.randn_like(x)
+    add("residual add backward", [Bn, Hn, Wn, Cn], lambda: residual_add_backward(gres, br, lsg, keep),
+        nbytes=x.numel() * (4 + 2 + 2),
+        ref_fn=(lambda: ref_res._VisionHOPEResidualFunction.backward(rs_ctx, gres)) if ref_res else None)
+    del br, gres
     gamma = torch.randn(Cn, device=device, generator=g) * 0.5
     _, gx, invd = grn_forward(x, gamma, bb, 1e-6, want_stats=True)
     gyn = torch.randn_like(x)
@@ -721,12 +752,6 @@ def roofline_backward(device, iters=5):
         leaves = [t.detach().requires_grad_(True) for t in (*mems, xs, qs)]
         srnl_raw_query(*leaves, W, heads, D).backward(gys.to(torch.bfloat16))
 
-    try:
-        from oracle import refmodel
-        refmodel.load("native")
-        import visionhope.models.srnl_core.chunk as ref_chunk
-    except Exception:
-        ref_chunk = None
     add("srnl recurrence backward (raw queries, chunk 56)", [B, 4, heads, L, D],
         lambda: sequence_backward(mems, xs, qs, [W] * 4, gys, q_normalized=False),
         units=chains * L, unit_name="chain_tokens_per_s")

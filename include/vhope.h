@@ -443,6 +443,26 @@ int vh_grn_bwd(const float* grad_y, const void* x, int32_t x_dtype, const float*
                int64_t workspace_bytes, int32_t batch, int32_t height, int32_t width, int32_t channels,
                vh_stream_t stream);
 
+/* LayerScale residual add; replaces the Triton kernel utils/residual.py:30-52
+ * (`_residual_forward_kernel`, launched at residual.py:107-129):  residual (residual_dtype) and
+ * branch (branch_dtype) channels-last [B, S, C]; gamma fp32 [C]; drop_scale fp32 [B] (the
+ * drop-path keep mask, already divided by the keep probability).  Writes out fp32 [B, S, C] =
+ * residual + branch * gamma * drop_scale. */
+int vh_residual_add_fwd(const void* residual, int32_t residual_dtype, const void* branch, int32_t branch_dtype,
+                        const float* gamma, const float* drop_scale, float* out, int32_t batch, int64_t spatial,
+                        int32_t channels, vh_stream_t stream);
+
+/* LayerScale residual add, backward; replaces utils/residual.py:54-101, 131-169
+ * (`_residual_backward_kernel`, `_residual_reduce_kernel`):  grad_out fp32 [B, S, C]; branch
+ * (branch_dtype), gamma, drop_scale as in the forward.  Writes grad_branch (branch_dtype) =
+ * grad_out * gamma * drop_scale and grad_gamma fp32 [C]; the residual's gradient is grad_out
+ * itself.  workspace: vh_residual_add_bwd_workspace_bytes(B * S, C) bytes. */
+int64_t vh_residual_add_bwd_workspace_bytes(int64_t rows, int32_t channels);
+int vh_residual_add_bwd(const float* grad_out, const void* branch, int32_t branch_dtype, const float* gamma,
+                        const float* drop_scale, void* grad_branch, float* grad_gamma, void* workspace,
+                        int64_t workspace_bytes, int32_t batch, int64_t spatial, int32_t channels,
+                        vh_stream_t stream);
+
 /* Measurement helper (no reference counterpart): launches `blocks` x 256 threads, each
  * running 32 * iters dependent-free FMAs; out needs blocks * 256 floats.  bench.py times it
  * to measure the device's FP32 (non-tensor) FMA peak. */

@@ -60,6 +60,11 @@ def grn(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float):
     return x * (1 + gamma.reshape(1, -1, 1, 1) * nx) + beta.reshape(1, -1, 1, 1)
 
 
+def residual(res: torch.Tensor, branch: torch.Tensor, gamma: torch.Tensor, mask: torch.Tensor):
+    """res + branch * gamma[c] * mask[b] over [B, C, H, W] (utils/residual.py:30-52)."""
+    return res + branch * gamma.reshape(1, -1, 1, 1) * mask.reshape(-1, 1, 1, 1)
+
+
 def grads(fn, inputs, grad_out):
     """fp64 CPU gradients of fn(*inputs) against grad_out, for every floating input that is a
     tensor (None for the others)."""

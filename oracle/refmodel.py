@@ -12,7 +12,7 @@ reference kernels).  Nothing in the product imports this module.  Two modes:
              those builds instead of compiling at first use.
 ``"dropin"``  the reference's modules unchanged (``models/*.py``, ``inference/prepare.py``)
              with the modules this repository replaces -- ``models/srnl_core`` and
-             ``utils/{direction_fusion,grn,grn_cuda,layer_norm_cuda,query_normalization}`` --
+             ``utils/{direction_fusion,grn,grn_cuda,layer_norm_cuda,query_normalization,residual}`` --
              bound to ``visionhope_b200``'s, as a user integrating the drop-in would
              (option A).
 
@@ -41,6 +41,7 @@ DROPIN = {
     "visionhope.utils.grn_cuda": "visionhope_b200.utils.grn_cuda",
     "visionhope.utils.layer_norm_cuda": "visionhope_b200.utils.layer_norm_cuda",
     "visionhope.utils.query_normalization": "visionhope_b200.utils.query_normalization",
+    "visionhope.utils.residual": "visionhope_b200.utils.residual",
 }
 
 
@@ -94,6 +95,19 @@ def _patch_native():
             grn_mod.append(build_ref.load_built("vhref_grn"))
         return grn_mod[0]
     grn_cuda._load_cuda_extension = grn_loader
+
+    # The Triton LayerNorm and residual kernels size their rows from
+    # triton.runtime.driver.utils.get_device_properties()["max_shared_mem"]
+    # (utils/layer_norm_cuda.py:18-22, utils/residual.py:18-21), which the installed Triton no
+    # longer provides; the same number (the opt-in shared memory per block) comes from torch.
+    import visionhope.utils.layer_norm_cuda as ln_mod
+    import visionhope.utils.residual as res_mod
+
+    def row_capacity(device):
+        import torch
+        return torch.cuda.get_device_properties(device).shared_memory_per_block_optin // (8 * 4)
+    ln_mod._row_capacity = row_capacity
+    res_mod._row_capacity = row_capacity
 
 
 def load(mode: str) -> SimpleNamespace:

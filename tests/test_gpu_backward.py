@@ -193,3 +193,51 @@ def test_srnl_sequence_backward_is_deterministic():
     flat1 = [*r1[0], r1[1], r1[2]]
     flat2 = [*r2[0], r2[1], r2[2]]
     assert all(torch.equal(a, b) for a, b in zip(flat1, flat2))
+
+
+@pytest.mark.parametrize("rdtype,bdtype", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
+                                           (torch.bfloat16, torch.float16)])
+@pytest.mark.parametrize("B,C,H,W", [(2, 96, 14, 14), (3, 30, 5, 7), (4, 768, 7, 7), (1, 2, 3, 3)])
+def test_residual_add(rdtype, bdtype, B, C, H, W):
+    """LayerScale residual add with a drop-path mask (utils/residual.py): the forward and every
+    gradient against fp64 autograd; the mask's zero and 1/keep entries both occur."""
+    from visionhope_b200.utils.residual import _VisionHOPEResidualFunction
+
+    g = torch.Generator().manual_seed(B * 1000 + C + H)
+    res = torch.randn(B, C, H, W, generator=g).to(rdtype).contiguous(memory_format=torch.channels_last)
+    br = torch.randn(B, C, H, W, generator=g).to(bdtype).contiguous(memory_format=torch.channels_last)
+    gamma = torch.randn(C, 1, 1, generator=g) * 0.5
+    mask = torch.tensor([0.0, 1.25, 1.25, 0.0][:B] if B > 1 else [1.25])
+    gout = torch.randn(B, C, H, W, generator=g)
+    leaves = [t.to(DEV).requires_grad_(True) for t in (res, br, gamma)]
+    out = _VisionHOPEResidualFunction.apply(*leaves, mask.to(DEV))
+    assert out.dtype == torch.float32 and out.is_contiguous(memory_format=torch.channels_last)
+    out.backward(gout.to(DEV))
+    exp_out = og.residual(res.double(), br.double(), gamma.double(), mask.double())
+    assert _rel(out, exp_out) < 1e-6
+    exp = og.grads(og.residual, [res.float(), br.float(), gamma, mask], gout)
+    assert leaves[0].grad.dtype == rdtype and _rel(leaves[0].grad, exp[0]) < _tol(rdtype)
+    assert leaves[1].grad.dtype == bdtype and _rel(leaves[1].grad, exp[1]) < _tol(bdtype)
+    assert leaves[2].grad.shape == gamma.shape and _rel(leaves[2].grad, exp[2]) < 2e-5
+
+
+def test_residual_add_drop_path_and_determinism():
+    """Outside training the mask is ones (the add is exact); in training the keep mask is
+    drawn with bernoulli_ and divided by the keep probability; the backward repeats bit for bit."""
+    from visionhope_b200.utils.residual import residual_add_backward, visionhope_residual_add
+
+    g = torch.Generator().manual_seed(11)
+    res = torch.randn(8, 64, 9, 9, generator=g).to(DEV).contiguous(memory_format=torch.channels_last)
+    br = torch.randn(8, 64, 9, 9, generator=g).to(DEV).contiguous(memory_format=torch.channels_last)
+    gamma = torch.randn(64, 1, 1, generator=g).to(DEV)
+    out = visionhope_residual_add(res, br, gamma, 0.3, False)
+    assert torch.equal(out, res + br * gamma)
+    torch.manual_seed(5)
+    out = visionhope_residual_add(res, br, gamma, 0.5, True)
+    torch.manual_seed(5)
+    mask = torch.empty((8,), device=DEV).bernoulli_(0.5).div_(0.5)
+    assert torch.allclose(out, res + br * gamma * mask.view(-1, 1, 1, 1), rtol=1e-6, atol=1e-6)
+    gout = torch.randn(8, 64, 9, 9, generator=g).to(DEV).contiguous(memory_format=torch.channels_last)
+    r1 = residual_add_backward(gout, br, gamma, mask)
+    r2 = residual_add_backward(gout, br, gamma, mask)
+    assert all(torch.equal(a, b) for a, b in zip(r1, r2))

@@ -1,7 +1,7 @@
 """Training parity with the reference itself: the reference's own modules (models/srnl.py,
 models/operator.py, models/layers.py:LayerNorm2d, utils/grn.py:GlobalResponseNorm; unchanged, oracle/refmodel.py)
 run forward and backward twice on the same seeded parameters and inputs, once on the reference's
-own kernels ("native": its CUDA extensions built from its sources) and once
+own kernels ("native": its CUDA extensions built from its sources, its Triton kernels) and once
 over this repository's drop-in modules ("dropin"), and every gradient is compared.  Bar: 5e-4
 normwise through the SRNL recurrence (two fp32 implementations of a long recurrence), 1e-5 for the
 one-pass operators."""
@@ -96,8 +96,8 @@ def test_operator_training_matches_reference():
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_grn_and_layernorm_training_match_reference(dtype):
-    """The reference's GRN (utils/grn.py, its CUDA backward) and LayerNorm2d (models/layers.py,
-    F.layer_norm's backward) on channels-last input."""
+    """The reference's GRN (utils/grn.py, its CUDA backward) and LayerNorm2d (models/layers.py
+    over utils/layer_norm_cuda.py, its Triton backward) on channels-last input."""
     g = torch.Generator().manual_seed(4)
     x = torch.randn(3, 96, 14, 14, generator=g).to(dtype).contiguous(memory_format=torch.channels_last)
     gy = torch.randn(3, 96, 14, 14, generator=g)
@@ -111,10 +111,6 @@ def test_grn_and_layernorm_training_match_reference(dtype):
 
     def build_ln(ref):
         mod = importlib.import_module("visionhope.models.layers").LayerNorm2d(96)
-        # The reference's Triton LayerNorm sizes its blocks through triton.runtime.driver.utils
-        # (utils/layer_norm_cuda.py:19-22), which the installed Triton no longer has, so on its
-        # own kernels the module takes its F.layer_norm branch (models/layers.py:18-20).
-        mod.inference_layout = ref.mode == "native"
         with torch.no_grad():
             mod.weight.normal_(1, 0.2, generator=torch.Generator().manual_seed(7))
             mod.bias.normal_(0, 0.2, generator=torch.Generator().manual_seed(8))
@@ -122,5 +118,61 @@ def test_grn_and_layernorm_training_match_reference(dtype):
 
     tol = 1e-5 if dtype == torch.float32 else 8e-3
     _compare(_run_both(build_grn, [x], gy), tol)
-    if dtype == torch.float32:  # F.layer_norm takes no bf16 input with fp32 weights
-        _compare(_run_both(build_ln, [x], gy), tol)
+    _compare(_run_both(build_ln, [x], gy), tol)
+
+
+@pytest.mark.parametrize("bdtype", [torch.float32, torch.bfloat16])
+def test_residual_training_matches_reference(bdtype):
+    """The reference's LayerScale residual (utils/residual.py, its Triton forward, backward and
+    reduce kernels) against the drop-in, with a drop-path mask drawn from the same seed."""
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(4, 96, 14, 14, generator=g).contiguous(memory_format=torch.channels_last)
+    br = torch.randn(4, 96, 14, 14, generator=g).to(bdtype).contiguous(memory_format=torch.channels_last)
+    gy = torch.randn(4, 96, 14, 14, generator=g)
+    gamma0 = torch.randn(96, 1, 1, generator=g)
+    out = {}
+    for mode in ("native", "dropin"):
+        reference(mode)
+        mod = importlib.import_module("visionhope.utils.residual")
+        leaves = [x.cuda().requires_grad_(True), br.cuda().requires_grad_(True), gamma0.cuda().requires_grad_(True)]
+        assert mod.can_fuse_residual_add(*leaves)
+        torch.manual_seed(3)
+        y = mod.visionhope_residual_add(*leaves, 0.25, True)
+        y.backward(gy.cuda())
+        out[mode] = [y.detach()] + [t.grad.detach().clone() for t in leaves]
+    for a, b in zip(out["native"], out["dropin"]):
+        assert a.dtype == b.dtype and a.shape == b.shape
+        assert rel_err(b, a) < (1e-6 if a.dtype == torch.float32 else 8e-3)
+
+
+def test_block_training_matches_reference():
+    """A whole VisionHOPEBlock (models/block.py, unchanged) in training mode with drop path:
+    LayerNorm2d, the operator (W_q, four scans, fusion), the depthwise convolutions, the GRN
+    FFN and both LayerScale residual adds, forward and backward.  Every parameter's gradient
+    and the input's, native against drop-in."""
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(2, 64, 14, 14, generator=g).contiguous(memory_format=torch.channels_last)
+    gy = torch.randn(2, 64, 14, 14, generator=g)
+    out = {}
+    for mode in ("native", "dropin"):
+        ref = reference(mode)
+        blk_mod = importlib.import_module("visionhope.models.block")
+        torch.manual_seed(0)
+        blk = blk_mod.VisionHOPEBlock(64, 16, chunk_size=14, drop_path=0.2, norm_layer="layernorm2d")
+        _stress_(blk.operator.srnl, 4)
+        with torch.no_grad():
+            blk.gamma1.normal_(0, 0.5, generator=torch.Generator().manual_seed(13))
+            blk.gamma2.normal_(0, 0.5, generator=torch.Generator().manual_seed(14))
+        blk = blk.cuda().train().to(memory_format=torch.channels_last)
+        xd = x.cuda().requires_grad_(True)
+        torch.manual_seed(21)
+        y = blk(xd)
+        y.backward(gy.cuda().to(y.dtype))
+        out[mode] = {n: p.grad.detach().clone() for n, p in blk.named_parameters() if p.grad is not None}
+        out[mode]["input"] = xd.grad.detach().clone()
+        out[mode]["output"] = y.detach()
+        del ref
+    assert out["native"].keys() == out["dropin"].keys()
+    for name, a in out["native"].items():
+        err = rel_err(out["dropin"][name], a)
+        assert err < 5e-4, f"{name}: {err:.3e}"

@@ -166,6 +166,14 @@ def load() -> ctypes.CDLL:
             lib.vh_grn_bwd.restype = c_int32
             lib.vh_grn_bwd.argtypes = ([c_void_p, c_void_p, c_int32] + [c_void_p] * 7 + [c_int64] + [c_int32] * 4
                                        + [c_void_p])
+            lib.vh_residual_add_fwd.restype = c_int32
+            lib.vh_residual_add_fwd.argtypes = ([c_void_p, c_int32, c_void_p, c_int32] + [c_void_p] * 3
+                                                + [c_int32, c_int64, c_int32, c_void_p])
+            lib.vh_residual_add_bwd_workspace_bytes.restype = c_int64
+            lib.vh_residual_add_bwd_workspace_bytes.argtypes = [c_int64, c_int32]
+            lib.vh_residual_add_bwd.restype = c_int32
+            lib.vh_residual_add_bwd.argtypes = ([c_void_p, c_void_p, c_int32] + [c_void_p] * 5
+                                                + [c_int64, c_int32, c_int64, c_int32, c_void_p])
             _lib = lib
     return _lib
 

@@ -179,9 +179,20 @@ __global__ void __launch_bounds__(kThreads) reduce_parts_kernel(const float* __r
     const int c = blockIdx.x * 32 + (threadIdx.x & 31);
     const int q = blockIdx.y;
     const int pl = threadIdx.x >> 5;
+    constexpr int kL = kThreads / 32;  // part lanes
     float sum = 0.f;
-    if (c < C)
-        for (int64_t p = pl; p < nparts; p += kThreads / 32) sum += part[(p * nq + q) * C + c];
+    if (c < C) {
+        // Eight loads in flight per batch; the adds stay in p order.
+        int64_t p = pl;
+        for (; p + 7 * kL < nparts; p += 8 * kL) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = part[((p + u * kL) * nq + q) * C + c];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sum += v[u];
+        }
+        for (; p < nparts; p += kL) sum += part[(p * nq + q) * C + c];
+    }
     __shared__ float red[kThreads / 32][32];
     red[pl][threadIdx.x & 31] = sum;
     __syncthreads();
@@ -190,6 +201,11 @@ __global__ void __launch_bounds__(kThreads) reduce_parts_kernel(const float* __r
         for (int k = 1; k < kThreads / 32; ++k) t += red[k][threadIdx.x];
         out[(int64_t)q * C + c] = t;
     }
+}
+
+int reduce_parts(const float* part, int64_t nparts, int nq, int C, float* out, cudaStream_t st) {
+    reduce_parts_kernel<<<dim3((C + 31) / 32, nq), kThreads, 0, st>>>(part, nparts, nq, C, out);
+    return launch_status("reduce of partial sums");
 }
 
 // dscale and dskip from the 8 summed rows: rows 0-3 dscale[d], rows 4-7 dskip[d]
