@@ -89,7 +89,8 @@ def _targets():
 
     fused_fns = ["srnl_line_forward_seq_noatomic", "srnl_sequence_forward"]
     chunk_fns = ["srnl_forward", "srnl_forward_qraw", "srnl_backward", "srnl_backward_qraw"]
-    line_fns = ["srnl_forward_qraw_large", "srnl_forward_qraw_varline"]
+    line_fns = ["srnl_forward_qraw_large", "srnl_backward_qraw_large", "srnl_forward_qraw_varline",
+                "srnl_backward_qraw_varline"]
     qnorm_fns = ["visionhope_qnorm_forward", "visionhope_qnorm_backward"]
     dirfuse_fns = ["visionhope_postprocess_scale_forward", "visionhope_postprocess_scale_backward"]
     base_chunk = chunk.cuda_helper_source
@@ -100,6 +101,8 @@ def _targets():
         ("vhref_chunk_fp32", chunk.cpp_source, chunk.cuda_source_fp32, chunk_fns),
         ("vhref_lines_bf16", lines.cpp_source,
          base_chunk + lines.large_cuda_source + lines.varline_cuda_source, line_fns),
+        ("vhref_lines_fp32", lines.cpp_source,
+         base_chunk + lines.large_cuda_source_fp32 + lines.varline_cuda_source_fp32, line_fns),
         ("vhref_qnorm_bf16", qnorm.cpp_source, qnorm.cuda_source, qnorm_fns),
         ("vhref_qnorm_fp32", qnorm.cpp_source, qnorm.cuda_source_fp32, qnorm_fns),
         ("vhref_dirfuse_bf16", dirfuse.cpp_source, dirfuse.cuda_source, dirfuse_fns),

@@ -151,18 +151,29 @@ def _srnl_case(seed, B, R, H, L, D, per_chain, q_normalized, dtype, mem_scale=0.
 @pytest.mark.parametrize("D,chunk,L,dtype,mem_scale", [
     (16, 14, 30, torch.float32, 0.35), (8, 7, 20, torch.float32, 0.35), (16, 64, 70, torch.float32, 0.35),
     (32, 5, 12, torch.float32, 0.35), (4, 9, 9, torch.float32, 0.35), (16, 12, 26, torch.float32, 1.0),
-    (16, 14, 28, torch.bfloat16, 0.35)])
+    (16, 14, 28, torch.bfloat16, 0.35), (16, 100, 230, torch.float32, 0.35), (16, 45, 100, torch.bfloat16, 1.0),
+    (16, 33, 33, torch.float32, 0.35)])
 def test_srnl_sequence_backward(q_normalized, per_chain, D, chunk, L, dtype, mem_scale):
     """The reference's training path (chunk.py SRNLNormalizedQueryFunction / SRNLRawQueryFunction)
     through the drop-in functions: every input's gradient against fp64 autograd of the oracle
-    recurrence.  mem_scale 1.0 makes the spectral clamp bind on part of the tokens."""
+    recurrence.  mem_scale 1.0 makes the spectral clamp bind on part of the tokens.  Chunks of
+    100 and 45 tokens (head_dim 16) span several 32-token tiles of the warp backward; 33 leaves
+    one token in the second tile."""
     from visionhope_b200.srnl_core.chunk import (recurrence_constants_tuple, srnl_normalized_query,
                                                   srnl_raw_query)
 
     B, R, H = 2, 4, 2
     mems, x, q, gy = _srnl_case(D * 100 + chunk + L, B, R, H, L, D, per_chain, q_normalized, dtype, mem_scale)
     leaves = [t.to(DEV).requires_grad_(True) for t in (*mems, x, q)]
-    if q_normalized:
+    if chunk > 64:  # past MAX_CHUNK: srnl_long_chunk (lines.py), or the packed function itself
+        from visionhope_b200.srnl_core import chunk as core
+        from visionhope_b200.srnl_core.lines import srnl_long_chunk
+        if q_normalized:
+            y = core._apply(lambda: core.run_sequence(leaves[:5], leaves[5], leaves[6], [chunk] * R,
+                                                      q_normalized=True), [chunk] * R, True, *leaves)
+        else:
+            y = srnl_long_chunk(*leaves, chunk, H, D)
+    elif q_normalized:
         y = srnl_normalized_query(*leaves, chunk)
     else:
         y = srnl_raw_query(*leaves, chunk, H, D)

@@ -76,9 +76,12 @@ def test_srnl_four_directions_training_matches_reference():
     _compare(res, 5e-4)
 
 
-def test_operator_training_matches_reference():
-    """VisionHOPEOperator(96) on [2, 96, 14, 14] fp32 in training mode: W_q, the four scans
-    (srnl_raw_query) and the direction fusion, backward through all of them."""
+@pytest.mark.parametrize("B,H,W", [(2, 14, 14), (2, 6, 70), (1, 72, 72)])
+def test_operator_training_matches_reference(B, H, W):
+    """VisionHOPEOperator(96) on [B, 96, H, W] fp32 in training mode: W_q, the four scans and the
+    direction fusion, backward through all of them.  14 x 14 runs srnl_raw_query (chunks of 14);
+    6 x 70 srnl_variable_lines (row chunk 70, lines.py:402-671); 72 x 72 srnl_long_chunk (chunk
+    72, lines.py:183-399): the reference's lines kernels against chunks longer than one tile."""
     def build(ref):
         op = ref.VisionHOPEOperator(96, 16)
         _stress_(op.srnl, 3)
@@ -89,8 +92,8 @@ def test_operator_training_matches_reference():
         return op
 
     g = torch.Generator().manual_seed(2)
-    x = torch.randn(2, 96, 14, 14, generator=g)
-    res = _run_both(build, [x], torch.randn(2, 96, 14, 14, generator=g))
+    x = torch.randn(B, 96, H, W, generator=g)
+    res = _run_both(build, [x], torch.randn(B, 96, H, W, generator=g))
     _compare(res, 5e-4)
 
 

@@ -46,7 +46,8 @@ struct Params {
     float* dq;        // q's layout
     float* dS;        // [chains][(3D+2) D]: gradient of the chain's initial state
     float* states;    // [chains][nchunks_max][(3D+2) D]
-    float* gseq;      // [chains][kMaxT][D D]
+    float* gseq;      // [chains][gseq_stride]: G_{t-1} of each token of the chunk being reversed
+    int64_t gseq_stride;
     int B, R, heads, L, nchunks_max;
     int chunk[4];
     SrnlConsts k;
@@ -220,7 +221,7 @@ __global__ void __launch_bounds__(kT) srnl_bwd_kernel(const Params p) {
     const int Lc = p.chunk[r];
     const int nch = (p.L + Lc - 1) / Lc;
     float* states = p.states + chain * (int64_t)p.nchunks_max * SR * D;
-    float* gseq = p.gseq + chain * (int64_t)kMaxT * D * D;
+    float* gseq = p.gseq + chain * p.gseq_stride;
     Tok<D>& tk = s.tok;
 
     // ---- A: forward sweep, chunk-start states --------------------------------------------
@@ -484,6 +485,8 @@ __global__ void __launch_bounds__(kT) srnl_bwd_mem_kernel(const float* __restric
     }
 }
 
+#include "srnl_bwd_warp.cuh"
+
 }  // namespace sbwd
 }  // namespace vh
 
@@ -492,6 +495,18 @@ using namespace vh::sbwd;
 
 namespace {
 
+// Floats of G_{t-1} history per chain: the longest chunk (head_dim 16, the warp kernel, takes
+// any chunk length) or kMaxT tokens.
+template <int D>
+int64_t gseq_floats(const vh_srnl_sequence_bwd_args* a) {
+    int64_t t = kMaxT;
+    if (D == 16) {
+        t = 1;
+        for (int r = 0; r < a->dirs; ++r) t = std::max<int64_t>(t, std::min(a->chunk[r], a->length));
+    }
+    return t * D * D;
+}
+
 template <int D>
 int64_t bwd_workspace(const vh_srnl_sequence_bwd_args* a, int* nmax) {
     int n = 1;
@@ -499,7 +514,16 @@ int64_t bwd_workspace(const vh_srnl_sequence_bwd_args* a, int* nmax) {
     if (nmax) *nmax = n;
     const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
     const int64_t SR = 3 * D + 2;
-    return chains * ((int64_t)n * SR * D + (int64_t)kMaxT * D * D + SR * D) * (int64_t)sizeof(float);
+    return chains * ((int64_t)n * SR * D + gseq_floats<D>(a) + SR * D) * (int64_t)sizeof(float);
+}
+
+int64_t gseq_floats_d(const vh_srnl_sequence_bwd_args* a) {
+    switch (a->head_dim) {
+        case 4: return gseq_floats<4>(a);
+        case 8: return gseq_floats<8>(a);
+        case 16: return gseq_floats<16>(a);
+        default: return gseq_floats<32>(a);
+    }
 }
 
 int64_t bwd_workspace_d(const vh_srnl_sequence_bwd_args* a, int* nmax) {
@@ -514,10 +538,19 @@ int64_t bwd_workspace_d(const vh_srnl_sequence_bwd_args* a, int* nmax) {
 template <int D, typename XT, typename QT>
 int launch_bwd(const vh_srnl_sequence_bwd_args* a, Params p, cudaStream_t st) {
     const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
-    const size_t smem = sizeof(Smem<D>);
-    const void* fn = reinterpret_cast<const void*>(&srnl_bwd_kernel<D, XT, QT>);
-    if (!ensure_smem_attr(fn, smem)) return fail(VH_E_DEVICE, "vh_srnl_sequence_bwd: cannot reserve %zu bytes of shared memory", smem);
-    srnl_bwd_kernel<D, XT, QT><<<(unsigned)chains, kT, smem, st>>>(p);
+    if constexpr (D == 16) {
+        const size_t smem = sizeof(wb::WSmem);
+        const void* fn = reinterpret_cast<const void*>(&wb::srnl_bwd_warp_kernel<XT, QT>);
+        if (!ensure_smem_attr(fn, smem))
+            return fail(VH_E_DEVICE, "vh_srnl_sequence_bwd: cannot reserve %zu bytes of shared memory", smem);
+        wb::srnl_bwd_warp_kernel<XT, QT><<<(unsigned)chains, 32, smem, st>>>(p);
+    } else {
+        const size_t smem = sizeof(Smem<D>);
+        const void* fn = reinterpret_cast<const void*>(&srnl_bwd_kernel<D, XT, QT>);
+        if (!ensure_smem_attr(fn, smem))
+            return fail(VH_E_DEVICE, "vh_srnl_sequence_bwd: cannot reserve %zu bytes of shared memory", smem);
+        srnl_bwd_kernel<D, XT, QT><<<(unsigned)chains, kT, smem, st>>>(p);
+    }
     int rc = launch_status("vh_srnl_sequence_bwd");
     if (rc) return rc;
     const int64_t slots = a->mem.per_chain ? chains : (int64_t)a->dirs * a->heads;
@@ -572,8 +605,9 @@ extern "C" int vh_srnl_sequence_bwd(const vh_srnl_sequence_bwd_args* a, void* wo
         return fail(VH_E_SHAPE, "SRNL requires nonempty batches and sequences");
     for (int r = 0; r < a->dirs; ++r) {
         if (a->chunk[r] <= 0) return fail(VH_E_SHAPE, "SRNL chunk length must be positive");
-        if (a->chunk[r] > kMaxT)
-            return fail(VH_E_RANGE, "chunk_size=%d exceeds MAX_CHUNK=%d in the SRNL backward", a->chunk[r], kMaxT);
+        if (a->chunk[r] > kMaxT && a->head_dim != 16)
+            return fail(VH_E_RANGE, "chunk_size=%d exceeds MAX_CHUNK=%d in the SRNL backward for head_dim %d",
+                        a->chunk[r], kMaxT, a->head_dim);
     }
     const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
     if (chains > INT32_MAX || (int64_t)a->length > ((int64_t)1 << 30))
@@ -592,7 +626,8 @@ extern "C" int vh_srnl_sequence_bwd(const vh_srnl_sequence_bwd_args* a, void* wo
     float* ws = static_cast<float*>(workspace);
     p.states = ws;
     p.gseq = p.states + chains * (int64_t)nmax * SR * D;
-    p.dS = p.gseq + chains * (int64_t)kMaxT * D * D;
+    p.gseq_stride = gseq_floats_d(a);
+    p.dS = p.gseq + chains * p.gseq_stride;
     p.B = a->batch; p.R = a->dirs; p.heads = a->heads; p.L = a->length; p.nchunks_max = nmax;
     for (int r = 0; r < 4; ++r) p.chunk[r] = r < a->dirs ? a->chunk[r] : 1;
     const vh_srnl_consts& c = a->consts;

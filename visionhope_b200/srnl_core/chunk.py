@@ -97,8 +97,8 @@ def run_sequence(states, x, q, chunk_sizes, *, q_normalized):
 def sequence_backward(states, x, q, chunk_sizes, grad_y, *, q_normalized):
     """Gradients of :func:`run_sequence` (``vh_srnl_sequence_bwd``, replaces
     models/srnl_core/csrc/chunk.cu:511-1057): returns (dM_m, dM_v, dM_k, dM_eta, dM_alpha) in the
-    memories' shapes, dx in x's shape and dq in q's shape, all fp32.  Chunks of up to 64 tokens,
-    head_dim up to 32."""
+    memories' shapes, dx in x's shape and dq in q's shape, all fp32.  head_dim 4, 8, 16 or 32;
+    any chunk length for head_dim 16, up to 64 tokens for the others."""
     _lib.ensure_device(x)
     B, R, heads, L, D = x.shape
     mems, per_chain = _memories_f32(states, x)

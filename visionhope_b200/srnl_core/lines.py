@@ -4,8 +4,9 @@ Mirror of models/srnl_core/lines.py (srnl_long_chunk, srnl_variable_lines): same
 arguments and errors.  One kernel serves every chunk length -- chunks longer than a
 shared-memory tile are processed tile by tile with the gain carried in registers -- so
 there is no separate "large"/"varline" kernel family.  The autograd path uses the sequence
-backward (``vh_srnl_sequence_bwd``), which takes chunks of up to 64 tokens; a backward through
-longer chunks raises.
+backward (``vh_srnl_sequence_bwd``, replacing lines.py:183-399 and 402-643): any chunk length
+for head_dim 16, chunks of up to 64 tokens for the other head dims (a backward through longer
+ones raises).
 """
 from __future__ import annotations
 
