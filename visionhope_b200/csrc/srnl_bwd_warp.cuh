@@ -9,7 +9,11 @@
 //     quantities that need dG_t itself (dG k, <dG, G_{t-1}>, -eff dG^T r + G_{t-1}^T dr and
 //     d eff) with warp shuffles, and leaves the rest of the gate adjoint to the token-parallel
 //     phase.  G_{t-1} of every token is written to the workspace by the forward pass of the chunk
-//     and read back, four tokens ahead, by the reverse pass.
+//     and read back, one token ahead, by the reverse pass.
+// The token-parallel phases that run once per tile (dx, the parameter adjoint) are kept as
+// loops rather than unrolled: with eleven warps per SM in different phases, instruction fetch
+// is the largest stall, and the smaller code measured faster (as did a prefetch distance of one
+// token over two to eight).
 // Tokens past the sequence end in the last chunk are skipped: the last chunk's gain is never
 // applied, so its dG is zero throughout and those tokens contribute nothing.
 #pragma once
@@ -20,7 +24,6 @@ constexpr int D = 16;
 constexpr int SR = 3 * D + 2;  // rows of the state [M_m; M_v; M_k; e; a]
 constexpr int kTile = 32;      // tokens per record tile (one per lane)
 constexpr int kRS = kTile + 1; // record row stride: lane t and row i at i * kRS + t
-constexpr int kPf = 4;         // G_{t-1} prefetch distance of the reverse pass
 constexpr unsigned kFull = 0xffffffffu;
 
 // Record rows (one column per token of the tile).  In the reverse pass R_K is overwritten
@@ -327,11 +330,12 @@ __device__ __forceinline__ void gate_adjoint(WSmem& s, const SrnlConsts& K, int 
     const float sg = rec[R_SIG][tt];
     const float d_ap = ap_in * d_alpha * (1.f - K.min_retention) * sg * (1.f - sg);
     const float d_ep = ep_in * d_eta * K.step_scale * sp;
+    const float ddn = d_dn / dn;  // d(dn) / dn, applied to each d_j
     float dk[D], kv[D], kdk = 0.f;
 #pragma unroll
     for (int j = 0; j < D; ++j) {
         const float dr = -eff * rec[R_DGK + j][tt];
-        const float dd = dr + d_dn * rec[R_D + j][tt] / dn;
+        const float dd = fmaf(ddn, rec[R_D + j][tt], dr);
         kv[j] = rec[R_K + j][tt];
         dk[j] = rec[R_WG + j][tt] + dd + 2.f * d_ke * kv[j];
         rec[R_D + j][tt] = -dd;
@@ -456,25 +460,21 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
             tile_tokens<XT, QT, true>(p, s, chain, b, r, head, tok0 + t0, nt, lane);
             __syncwarp();
             if (!last) {
-                float ring[kPf][8];
+                float gc[8], gn[8];
+                load_ring(gseq, t0 + nt - 1, lane, gc);
+#pragma unroll 1
+                for (int tt = nt - 1; tt >= 0; --tt) {
+                    if (tt > 0) load_ring(gseq, t0 + tt - 1, lane, gn);
+                    reverse_step(s, tt, gc, dG, lane);
 #pragma unroll
-                for (int u = 0; u < kPf; ++u)
-                    if (nt - 1 - u >= 0) load_ring(gseq, t0 + nt - 1 - u, lane, ring[u]);
-                for (int base = nt - 1; base >= 0; base -= kPf) {
-#pragma unroll
-                    for (int u = 0; u < kPf; ++u) {
-                        const int tt = base - u;
-                        if (tt >= 0) {
-                            reverse_step(s, tt, ring[u], dG, lane);
-                            if (tt - kPf >= 0) load_ring(gseq, t0 + tt - kPf, lane, ring[u]);
-                        }
-                    }
+                    for (int jj = 0; jj < 8; ++jj) gc[jj] = gn[jj];
                 }
             }
             __syncwarp();
             if (lane < nt) gate_adjoint(s, K, lane, last);
             __syncwarp();
             // Parameter adjoint: dS += sum_t [dy q^T; dv x^T; dk~ x^T; d(x.e) x; d(x.a) x]
+#pragma unroll 1
             for (int tt = 0; tt < nt; ++tt) {
                 const float xj = s.rec[R_X + col][tt], qj = s.rec[R_QH + col][tt];
 #pragma unroll
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
                     dy[q] = s.rec[R_DY + q][lane];
                 }
                 float* dxp = p.dx + (chain * p.L + tok) * D;
-#pragma unroll
+#pragma unroll 1
                 for (int j4 = 0; j4 < D / 4; ++j4) {
                     float o[4];
 #pragma unroll
