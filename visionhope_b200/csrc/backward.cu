@@ -76,18 +76,20 @@ int qnorm_bwd_dispatch(int D, const float* g, const float* q, const float* inv, 
 // l_d the position of pixel pix in scan d.  So for every (b, d, pixel, c):
 //   dy_d = scale[d, c] g,   dx_d = scale[d, c] skip_d[c] g,
 //   dscale[d, c] += g (y_d + skip_d[c] x_d),   dskip_d[c] += g scale[d, c] x_d.
-// CTA = (b, head, tile of kPix row-major pixels), as the forward: the tile's gradient is staged
-// in shared memory first (read along whichever axis is contiguous), then each thread takes
-// (pixel, group of 4 channels) items, always of the same group, and keeps its partial sums in
-// registers; the CTA adds them over its threads in a fixed order and writes one partial row
-// per (image, tile).  reduce_parts_kernel adds the partial rows in order.
+// CTA = (b, head, group of `tpc` tiles of kPix row-major pixels): each tile's gradient is
+// staged in shared memory first (read along whichever axis is contiguous), then each thread
+// takes (pixel, group of 4 channels) items, always of the same channel group, and keeps its
+// partial sums in registers across the CTA's tiles; the CTA adds them over its threads in a
+// fixed order and writes one partial row per (image, tile group).  reduce_parts_kernel adds the
+// partial rows in order.  The tile group depends on the sizes only, so the summation order is
+// the same on every GPU.
 constexpr int kPix = 64;
 
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
     const float* __restrict__ g, int64_t gsb, int64_t gsc, int64_t gsh, int64_t gsw, const T* __restrict__ y,
     const T* __restrict__ x, const float* __restrict__ skip, int skip_per_dir, const float* __restrict__ scale,
-    T* __restrict__ dy, T* __restrict__ dx, float* __restrict__ part, int heads, int H, int W) {
+    T* __restrict__ dy, T* __restrict__ dx, float* __restrict__ part, int heads, int H, int W, int tpc) {
     constexpr int G4 = D / 4;
     static_assert(kThreads % G4 == 0, "a thread keeps one channel group");
     __shared__ float gt[D][kPix + 1];
@@ -95,22 +97,11 @@ __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
     const int64_t L = (int64_t)H * W;
     const int C = heads * D;
     const int tiles = (int)((L + kPix - 1) / kPix);
-    const int tile = blockIdx.x % tiles;
-    const int head = (blockIdx.x / tiles) % heads;
-    const int b = blockIdx.x / (tiles * heads);
-    const int64_t pix0 = (int64_t)tile * kPix;
+    const int ngroups = (tiles + tpc - 1) / tpc;
+    const int group = blockIdx.x % ngroups;
+    const int head = (blockIdx.x / ngroups) % heads;
+    const int b = blockIdx.x / (ngroups * heads);
     const bool pix_fast = gsc != 1;  // NCHW-like gradient: pixels contiguous per channel
-    for (int it = threadIdx.x; it < D * kPix; it += kThreads) {
-        const int k = pix_fast ? it % kPix : it / D, ch = pix_fast ? it / kPix : it % D;
-        const int64_t pix = pix0 + k;
-        float v = 0.f;
-        if (pix < L) {
-            const int64_t pi = pix / W, pj = pix - pi * W;
-            v = g[b * gsb + (int64_t)(head * D + ch) * gsc + pi * gsh + pj * gsw];
-        }
-        gt[ch][k] = v;
-    }
-    __syncthreads();
     const int grp = threadIdx.x % G4;
     const int c0 = head * D + grp * 4;
     float sc[4][4], sk[4][4];
@@ -122,29 +113,45 @@ __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
             sk[d][e] = skip[(skip_per_dir ? d * C : 0) + c0 + e];
         }
     float ps[4][4] = {}, pk[4][4] = {};
-    for (int it = threadIdx.x; it < kPix * G4; it += kThreads) {
-        const int k = it / G4;
-        const int64_t pix = pix0 + k;
-        if (pix >= L) break;
-        const int64_t pi = pix / W, pj = pix - pi * W;
-        const int64_t lhw = pix, lwh = pj * H + pi;
-        const int64_t ls[4] = {lhw, L - 1 - lhw, lwh, L - 1 - lwh};
-        const float gv[4] = {gt[grp * 4][k], gt[grp * 4 + 1][k], gt[grp * 4 + 2][k], gt[grp * 4 + 3][k]};
-#pragma unroll
-        for (int d = 0; d < 4; ++d) {
-            const int64_t off = ((((int64_t)b * 4 + d) * heads + head) * L + ls[d]) * D + grp * 4;
-            const float4 yv = load4(y + off), xv = load4(x + off);
-            const float yy[4] = {yv.x, yv.y, yv.z, yv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w};
-            float o1[4], o2[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                o1[e] = sc[d][e] * gv[e];
-                o2[e] = sc[d][e] * sk[d][e] * gv[e];
-                ps[d][e] = fmaf(gv[e], fmaf(sk[d][e], xs[e], yy[e]), ps[d][e]);
-                pk[d][e] = fmaf(gv[e] * sc[d][e], xs[e], pk[d][e]);
+    const int tile_end = min(tiles, (group + 1) * tpc);
+    for (int tile = group * tpc; tile < tile_end; ++tile) {
+        const int64_t pix0 = (int64_t)tile * kPix;
+        __syncthreads();  // the previous tile's gradient has been read
+        for (int it = threadIdx.x; it < D * kPix; it += kThreads) {
+            const int k = pix_fast ? it % kPix : it / D, ch = pix_fast ? it / kPix : it % D;
+            const int64_t pix = pix0 + k;
+            float v = 0.f;
+            if (pix < L) {
+                const int64_t pi = pix / W, pj = pix - pi * W;
+                v = g[b * gsb + (int64_t)(head * D + ch) * gsc + pi * gsh + pj * gsw];
             }
-            store4(dy + off, make_float4(o1[0], o1[1], o1[2], o1[3]));
-            store4(dx + off, make_float4(o2[0], o2[1], o2[2], o2[3]));
+            gt[ch][k] = v;
+        }
+        __syncthreads();
+        for (int it = threadIdx.x; it < kPix * G4; it += kThreads) {
+            const int k = it / G4;
+            const int64_t pix = pix0 + k;
+            if (pix >= L) break;
+            const int64_t pi = pix / W, pj = pix - pi * W;
+            const int64_t lhw = pix, lwh = pj * H + pi;
+            const int64_t ls[4] = {lhw, L - 1 - lhw, lwh, L - 1 - lwh};
+            const float gv[4] = {gt[grp * 4][k], gt[grp * 4 + 1][k], gt[grp * 4 + 2][k], gt[grp * 4 + 3][k]};
+#pragma unroll
+            for (int d = 0; d < 4; ++d) {
+                const int64_t off = ((((int64_t)b * 4 + d) * heads + head) * L + ls[d]) * D + grp * 4;
+                const float4 yv = load4(y + off), xv = load4(x + off);
+                const float yy[4] = {yv.x, yv.y, yv.z, yv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w};
+                float o1[4], o2[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    o1[e] = sc[d][e] * gv[e];
+                    o2[e] = sc[d][e] * sk[d][e] * gv[e];
+                    ps[d][e] = fmaf(gv[e], fmaf(sk[d][e], xs[e], yy[e]), ps[d][e]);
+                    pk[d][e] = fmaf(gv[e] * sc[d][e], xs[e], pk[d][e]);
+                }
+                store4(dy + off, make_float4(o1[0], o1[1], o1[2], o1[3]));
+                store4(dx + off, make_float4(o2[0], o2[1], o2[2], o2[3]));
+            }
         }
     }
     // Threads of one channel group: tid = grp + G4 * slot.  Stage, then add the slots in order.
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
             const int q = threadIdx.x >> 2, e = threadIdx.x & 3;
             float sum = 0.f;
             for (int sl = 0; sl < kSlots; ++sl) sum += mine[(sl * 8 + q) * 4 + e];
-            part[((int64_t)(b * tiles + tile) * 8 + q) * C + head * D + gg * 4 + e] = sum;
+            part[((int64_t)(b * ngroups + group) * 8 + q) * C + head * D + gg * 4 + e] = sum;
         }
         __syncthreads();
     }
@@ -443,8 +450,18 @@ int by_dtype(int dt, F&& f) {
     }
 }
 
-int64_t dirfuse_parts(int batch, int height, int width) {
-    return (int64_t)batch * (((int64_t)height * width + kPix - 1) / kPix);
+// Tiles per CTA of the direction-fusion backward: about 2368 CTAs (two waves of eight per SM
+// on 148 SMs), at most 16 tiles; from the sizes alone.
+int dirfuse_tpc(int batch, int heads, int height, int width) {
+    const int64_t tiles = ((int64_t)height * width + kPix - 1) / kPix;
+    const int64_t want = ((int64_t)batch * heads * tiles + 2367) / 2368;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(16, want));
+}
+
+int64_t dirfuse_parts(int batch, int heads, int height, int width) {
+    const int64_t tiles = ((int64_t)height * width + kPix - 1) / kPix;
+    const int tpc = dirfuse_tpc(batch, heads, height, width);
+    return (int64_t)batch * ((tiles + tpc - 1) / tpc);
 }
 
 }  // namespace
@@ -472,7 +489,7 @@ extern "C" int vh_qnorm_bwd(const float* grad_out, const float* q_out, const flo
 extern "C" int64_t vh_dirfuse_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t height, int32_t width,
                                                   int32_t head_dim) {
     if (batch <= 0 || heads <= 0 || height <= 0 || width <= 0 || head_dim <= 0) return 0;
-    return (dirfuse_parts(batch, height, width) + 1) * 8 * (int64_t)heads * head_dim * (int64_t)sizeof(float);
+    return (dirfuse_parts(batch, heads, height, width) + 1) * 8 * (int64_t)heads * head_dim * (int64_t)sizeof(float);
 }
 
 extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c, int64_t gs_h, int64_t gs_w,
@@ -499,10 +516,11 @@ extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c,
         !aligned(grad_y, io_dtype == VH_F32 ? 16 : 8) || !aligned(grad_x, io_dtype == VH_F32 ? 16 : 8))
         return fail(VH_E_ALIGN, "vh_dirfuse_bwd: misaligned pointers");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int64_t nparts = dirfuse_parts(batch, height, width);
+    const int tpc = dirfuse_tpc(batch, heads, height, width);
+    const int64_t nparts = dirfuse_parts(batch, heads, height, width);
     float* part = static_cast<float*>(workspace);
     float* sums = part + nparts * 8 * C;
-    const int64_t grid = (int64_t)batch * heads * tiles;
+    const int64_t grid = (int64_t)batch * heads * ((tiles + tpc - 1) / tpc);
     if (grid > INT32_MAX) return fail(VH_E_RANGE, "vh_dirfuse_bwd: too many tiles");
     int rc = by_dtype(io_dtype, [&](auto t) {
         using T = decltype(t);
@@ -512,11 +530,11 @@ extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c,
         T* dxp = static_cast<T*>(grad_x);
         const int spd = skip_per_dir ? 1 : 0;
         switch (head_dim) {
-            case 4: dirfuse_bwd_kernel<4, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
-            case 8: dirfuse_bwd_kernel<8, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
-            case 16: dirfuse_bwd_kernel<16, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
-            case 32: dirfuse_bwd_kernel<32, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
-            default: dirfuse_bwd_kernel<64, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width); break;
+            case 4: dirfuse_bwd_kernel<4, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width, tpc); break;
+            case 8: dirfuse_bwd_kernel<8, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width, tpc); break;
+            case 16: dirfuse_bwd_kernel<16, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width, tpc); break;
+            case 32: dirfuse_bwd_kernel<32, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width, tpc); break;
+            default: dirfuse_bwd_kernel<64, T><<<(unsigned)grid, kThreads, 0, st>>>(grad_out, gs_b, gs_c, gs_h, gs_w, yp, xp, skip, spd, scale, dyp, dxp, part, heads, height, width, tpc); break;
         }
         return launch_status("vh_dirfuse_bwd");
     });
