@@ -306,6 +306,91 @@ __global__ void __launch_bounds__(kThreads) ln_param_kernel(const float* __restr
     }
 }
 
+// ln_fused_kernel (C <= kLnFusedMaxC): dx as ln_dx_kernel, with the parameter sums taken in
+// the same pass.  Lane sl of a row owns channels sl + 8 m and keeps its dw, db sums over the
+// CTA's rows in registers; the four row groups of a warp are added by shuffles, then the warps
+// in order through shared memory, into one partial row per CTA of kLnRows rows.  dy and x are
+// read from DRAM once (ln_param_kernel reads them a second time).
+constexpr int kLnFusedMaxC = 128;
+
+template <typename T, int NM>
+__global__ void __launch_bounds__(kThreads) ln_fused_kernel(const float* __restrict__ dy, const T* __restrict__ x,
+                                                            const float* __restrict__ w,
+                                                            const float* __restrict__ mean,
+                                                            const float* __restrict__ rstd, T* __restrict__ dx,
+                                                            float* __restrict__ part, int64_t rows, int C) {
+    const int lane = threadIdx.x & 31, sl = lane & 7, warp = threadIdx.x >> 5;
+    float wv[NM], aw[NM], ab[NM];
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+        const int c = sl + 8 * m;
+        wv[m] = c < C ? w[c] : 0.f;
+        aw[m] = 0.f;
+        ab[m] = 0.f;
+    }
+    const float invC = 1.f / (float)C;
+    const int64_t r0 = (int64_t)blockIdx.x * kLnRows;
+    for (int it = 0; it < kLnRows / 32; ++it) {  // the same trip count for every lane
+        const int64_t r = r0 + it * 32 + warp * 4 + (lane >> 3);
+        const bool live = r < rows;
+        const float* gr = dy + (live ? r : 0) * C;
+        const T* xr = x + (live ? r : 0) * C;
+        const float mu = live ? mean[r] : 0.f, rs = live ? rstd[r] : 0.f;
+        float gv[NM], xh[NM], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+            const int c = sl + 8 * m;
+            const bool ok = live && c < C;
+            gv[m] = ok ? gr[c] : 0.f;
+            xh[m] = ok ? (to_f(xr[c]) - mu) * rs : 0.f;
+            const float wg = wv[m] * gv[m];
+            s1 += wg;
+            s2 = fmaf(wg, xh[m], s2);
+            aw[m] = fmaf(gv[m], xh[m], aw[m]);
+            ab[m] += gv[m];
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (live) {
+            const float a = s1 * invC, bq = s2 * invC;
+            T* dxr = dx + r * C;
+#pragma unroll
+            for (int m = 0; m < NM; ++m) {
+                const int c = sl + 8 * m;
+                if (c < C) dxr[c] = from_f<T>((wv[m] * gv[m] - a - xh[m] * bq) * rs);
+            }
+        }
+    }
+    __shared__ float red[kThreads / 32][2][kLnFusedMaxC];
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+        aw[m] += __shfl_xor_sync(0xffffffffu, aw[m], 8);
+        ab[m] += __shfl_xor_sync(0xffffffffu, ab[m], 8);
+        aw[m] += __shfl_xor_sync(0xffffffffu, aw[m], 16);
+        ab[m] += __shfl_xor_sync(0xffffffffu, ab[m], 16);
+    }
+    if (lane < 8) {
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+            const int c = sl + 8 * m;
+            if (c < C) {
+                red[warp][0][c] = aw[m];
+                red[warp][1][c] = ab[m];
+            }
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 2 * C; e += kThreads) {
+        const int q = e / C, c = e - q * C;
+        float t = red[0][q][c];
+        for (int k = 1; k < kThreads / 32; ++k) t += red[k][q][c];
+        part[((int64_t)blockIdx.x * 2 + q) * C + c] = t;
+    }
+}
+
 // ---- GRN (grn_cuda.cu:126-265) ------------------------------------------------------------
 // y = x (1 + gamma Nx) + beta, Nx = Gx inv, Gx[b, c] = ||x[b, :, c]||, inv = 1 / (mean_c Gx + eps).
 // With t[b, c] = sum_s dy x and s = gamma t:
@@ -569,6 +654,15 @@ extern "C" int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dt
     float* part = static_cast<float*>(workspace);
     int rc = by_dtype(x_dtype, [&](auto t) {
         using T = decltype(t);
+        if (channels <= kLnFusedMaxC) {
+            if (channels <= 64)
+                ln_fused_kernel<T, 8><<<(unsigned)rblocks, kThreads, 0, st>>>(
+                    grad_y, static_cast<const T*>(x), weight, mean, rstd, static_cast<T*>(grad_x), part, rows, channels);
+            else
+                ln_fused_kernel<T, 16><<<(unsigned)rblocks, kThreads, 0, st>>>(
+                    grad_y, static_cast<const T*>(x), weight, mean, rstd, static_cast<T*>(grad_x), part, rows, channels);
+            return launch_status("vh_layernorm_bwd (fused)");
+        }
         const int64_t grid = (rows + 4 * (kThreads / 32) - 1) / (4 * (kThreads / 32));
         if (grid > INT32_MAX) return fail(VH_E_RANGE, "vh_layernorm_bwd: too many rows");
         ln_dx_kernel<T><<<(unsigned)grid, kThreads, 0, st>>>(grad_y, static_cast<const T*>(x), weight, mean, rstd,
