@@ -757,8 +757,47 @@ def roofline_backward(device, iters=5):
         units=chains * L, unit_name="chain_tokens_per_s")
     add("srnl recurrence forward + backward (autograd, raw queries, chunk 56)", [B, 4, heads, L, D], ours_train,
         units=chains * L, unit_name="chain_tokens_per_s", ref_fn=ref_train if ref_chunk is not None else None)
-    return {"backward": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
-            "consts": list(recurrence_constants_tuple())}
+    del xs, qs, gys
+    out = {"backward": rows, "peak_hbm_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+           "consts": list(recurrence_constants_tuple())}
+    try:
+        out["training_step"] = training_step_compare(device, iters)
+    except Exception as exc:  # the reference's modules are optional here
+        out["training_step"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    return out
+
+
+def training_step_compare(device, iters, batch=64):
+    """One training step (forward and backward, no optimizer) of the reference's own
+    VisionHOPE-T (models/factory.py, unchanged) at 224 x 224 under bf16 autocast, channels-last,
+    in training mode: once on the reference's kernels ("native") and once with its kernel-owning
+    modules bound to this package ("dropin").  The same seeded weights and input; the loss is
+    the sum of the logits.  Every operator takes the ordinary path (training mode), so the step
+    runs query normalization, the SRNL recurrence, direction fusion, LayerNorm, GRN and the
+    residual adds forward and backward on the library under test."""
+    from oracle import refmodel
+
+    res = {"model": "visionhope_tiny", "batch": batch, "image": [224, 224],
+           "precision": "bf16 autocast, fp32 params", "mode": "train (drop path on), forward + backward"}
+    for mode in ("native", "dropin"):
+        ref = refmodel.load(mode)
+        torch.manual_seed(0)
+        model = ref.create_model("visionhope_tiny").to(device).train().to(memory_format=torch.channels_last)
+        x = torch.randn(batch, 3, 224, 224, device=device).contiguous(memory_format=torch.channels_last)
+
+        def step():
+            model.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                logits = model(x)
+            logits.float().sum().backward()
+
+        ms, _ = _time_calls(step, iters, lambda: None)
+        res[f"{mode}_ms"] = ms
+        res[f"{mode}_images_per_s"] = batch / (ms * 1e-3)
+        del model, x
+        torch.cuda.empty_cache()
+    res["speedup_vs_reference"] = res["native_ms"] / res["dropin_ms"]
+    return res
 
 
 def roofline_depthwise(device, iters=10):
