@@ -172,7 +172,8 @@ def build(only=None):
 
 
 PYREF_DIR = OUT_DIR / "pyref"
-_STAGED = ("__init__.py", "models", "utils", "inference/__init__.py", "inference/prepare.py")
+_STAGED = ("__init__.py", "models", "utils", "inference/__init__.py", "inference/prepare.py",
+           "tasks/__init__.py", "tasks/backbone.py", "tools/__init__.py", "tools/checkpoint.py")
 
 
 def stage_python():

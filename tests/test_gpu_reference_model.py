@@ -14,6 +14,9 @@ drop-in mode (the reference's modules resolve their kernel modules at call time)
 * Config 2 at its own shape: VisionHOPEOperator(96) at B=64, 56 x 56, fp32 x under bf16
   autocast (the ordinary path: qnorm, chunk forward, direction fusion) -- native, drop-in and
   the CPU oracle on the exact inputs, all within 1e-4.
+* The dense-prediction adapter (tasks/backbone.py ``VisionHOPEBackbone``, with its per-stage
+  output norms) against ``visionhope_b200.backbone.DenseBackbone`` on one state_dict, measured
+  against the reference's own fp32 run.
 * VisionHOPE-B's stage-1 operator at the dense configuration's shape (config 5): B=2,
   C=48, 128 x 512 tokens (row chunks of 512, column chunks of 128), bf16, on the fast spatial
   path (1e-4 against native and oracle) and on the ordinary path (``srnl_variable_lines``,
@@ -232,3 +235,58 @@ def test_config5_stage1_operator_128x512(fast, oracle, cuda):
           f"reference {e_ref:.2e}; ours vs reference {e_pair:.2e}; operator call: reference {t_ref:.2f} ms, "
           f"ours {t_ours:.2f} ms")
     assert e_ours < tol and e_ref < tol and e_pair < tol
+
+
+def test_dense_backbone_matches_reference(cuda):
+    """tasks/backbone.py's VisionHOPEBackbone (the reference's adapter for Mask R-CNN and
+    UPerNet, unchanged, on its own kernels) against DenseBackbone with its state_dict:
+    VisionHOPE-T, 2 x 3 x 256 x 384 (stage 1: 64 x 96 tokens), prepared, output norms with
+    non-trivial weights, LayerScale 0.1 and stressed SRNL memories (every block matters).
+
+    The normalized stage features of a bf16-autocast run drift from an fp32 run by about 2e-2
+    after a few such blocks, whichever kernels run, so the bar is relative to the reference's own
+    drift: against the reference's fp32 run, ours (bf16) must be within 1.5x of the reference's
+    bf16 run (floor 1e-2), and within 4e-2 of the reference's bf16 run itself."""
+    import importlib
+
+    from visionhope_b200.backbone import DenseBackbone, prepare_for_inference
+
+    native = reference("native")
+    tb = importlib.import_module("visionhope.tasks.backbone")
+    torch.manual_seed(4)
+    ref_bb = tb.VisionHOPEBackbone("tiny", layer_scale_init_value=0.1)
+    _stress_memories(ref_bb, np.random.default_rng(5))
+    with torch.no_grad():
+        for n in ref_bb.out_norms:
+            n.weight.normal_(1, 0.2)
+            n.bias.normal_(0, 0.2)
+    sd = {k: v.detach().clone() for k, v in ref_bb.state_dict().items()}
+    ref_bb = ref_bb.cuda().to(memory_format=torch.channels_last)
+    native.prepare_for_inference(ref_bb)
+    x = torch.randn(2, 3, 256, 384, generator=torch.Generator().manual_seed(6)).to(cuda)
+    with torch.inference_mode():
+        ref32 = [o.float() for o in ref_bb(x)]
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            ref16 = [o.float() for o in ref_bb(x)]
+            ref_ms = _time_ms(lambda: ref_bb(x))
+    del ref_bb
+
+    ours = DenseBackbone("tiny", layer_scale_init_value=0.1)
+    ours.load_state_dict(sd, strict=True)
+    ours = ours.cuda().to(memory_format=torch.channels_last)
+    prepare_for_inference(ours)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        our16 = [o.float() for o in ours(x)]
+        our_ms = _time_ms(lambda: ours(x))
+    assert len(our16) == len(ref16) == len(ref32) == 4
+    e_ref = [rel_err(a, t) for a, t in zip(ref16, ref32)]
+    e_our = [rel_err(b, t) for b, t in zip(our16, ref32)]
+    e_pair = [rel_err(b, a) for a, b in zip(ref16, our16)]
+    fmt = lambda v: " ".join(f"{e:.2e}" for e in v)
+    print(f"\n[dense backbone] vs fp32 reference: reference bf16 {fmt(e_ref)}; ours bf16 {fmt(e_our)}; "
+          f"ours vs reference bf16 {fmt(e_pair)}; eager bf16 forward reference {ref_ms:.2f} ms, ours {our_ms:.2f} ms")
+    for a, b, t in zip(ref16, our16, ref32):
+        assert a.shape == b.shape == t.shape and torch.isfinite(b).all()
+    for er, eo, ep in zip(e_ref, e_our, e_pair):
+        assert eo < max(1e-2, 1.5 * er), (e_ref, e_our)
+        assert ep < 4e-2, e_pair

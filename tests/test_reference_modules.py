@@ -64,3 +64,26 @@ def test_harness_loads_reference_state_dict(name):
     assert not missing and not unexpected
     theirs = {k: tuple(v.shape) for k, v in sd.items()}
     assert {k: tuple(v.shape) for k, v in ours.state_dict().items()} == theirs
+
+
+@pytest.mark.parametrize("arch,out_norm", [("tiny", True), ("base", False)])
+def test_dense_backbone_loads_reference_adapter_state_dict(arch, out_norm):
+    """DenseBackbone keeps the parameter names of tasks/backbone.py's VisionHOPEBackbone
+    (downsample_layers, stages, out_norms) and its argument checks."""
+    import importlib
+
+    from visionhope_b200.backbone import DenseBackbone
+
+    reference("native")
+    tb = importlib.import_module("visionhope.tasks.backbone")
+    torch.manual_seed(3)
+    sd = tb.VisionHOPEBackbone(arch, out_norm=out_norm).state_dict()
+    ours = DenseBackbone(arch, out_norm=out_norm)
+    missing, unexpected = ours.load_state_dict(sd, strict=True)
+    assert not missing and not unexpected
+    for bad in ({"arch": "huge"}, {"out_indices": (1, 0)}, {"out_indices": (0, 4)}, {"out_indices": ()}):
+        args = {"arch": "tiny", **bad}
+        with pytest.raises(ValueError):
+            DenseBackbone(**args)
+        with pytest.raises(ValueError):
+            tb.VisionHOPEBackbone(**args)

@@ -506,6 +506,61 @@ class HierarchicalVisionHOPE(nn.Module):
         return self.head(self.forward_features(x))
 
 
+class DenseBackbone(nn.Module):
+    """Stage features for detection and segmentation necks (tasks/backbone.py:19-125): the
+    hierarchical backbone's downsample layers and stages, then one LayerNorm2d per stage
+    (``out_norms``) on the features of ``out_indices``.  Parameter names match the reference's
+    ``VisionHOPEBackbone``, so its state_dict loads with strict=True.  Each returned stage's last
+    residual add runs fused with its output norm (``LayerNorm2d.forward_add``: one pass gives
+    the stage output, which the next downsample reads, and its normalized copy).  Loading
+    ImageNet weights, frozen stages and activation checkpointing stay with the caller (training
+    options of the reference's adapter)."""
+
+    def __init__(self, arch="tiny", in_chans=3, out_indices=(0, 1, 2, 3), out_norm=True, channels_last=True,
+                 **kwargs):
+        super().__init__()
+        if arch not in {"tiny", "small", "base"}:
+            raise ValueError("arch must be 'tiny', 'small', or 'base'")
+        indices = tuple(int(i) for i in out_indices)
+        if not indices or len(set(indices)) != len(indices) or any(i not in range(4) for i in indices):
+            raise ValueError("out_indices must contain unique stage indices in [0, 3]")
+        if indices != tuple(sorted(indices)):
+            raise ValueError("out_indices must be in increasing stage order")
+        model = create_model(f"visionhope_{arch}", in_chans=in_chans, num_classes=1000, **kwargs)
+        self.arch = arch
+        self.embed_dims = list(model.embed_dims)
+        self.downsample_layers = model.downsample_layers
+        self.stages = model.stages
+        self.out_norms = nn.ModuleList(LayerNorm2d(d) if out_norm else nn.Identity() for d in self.embed_dims)
+        self.out_indices = indices
+        self.num_features = [self.embed_dims[i] for i in indices]
+        self.channels_last = bool(channels_last)
+
+    def forward(self, x):
+        if self.channels_last:
+            x = x.contiguous(memory_format=torch.channels_last)
+        outs = []
+        pending = None
+        for i, (down, stage) in enumerate(zip(self.downsample_layers, self.stages)):
+            if pending is not None and isinstance(down, Downsample):
+                x = down(x, pending)  # the previous stage's last add fused with this input's cast
+            else:
+                x = down(x if pending is None else x + pending)
+            x, pending = HierarchicalVisionHOPE._run_stage(stage, x)
+            if i in self.out_indices:
+                norm = self.out_norms[i]
+                if pending is not None and isinstance(norm, LayerNorm2d):
+                    x, y = norm.forward_add(x, pending)
+                else:
+                    x = x if pending is None else x + pending
+                    y = norm(x)
+                pending = None
+                outs.append(y)
+            if i == max(self.out_indices):
+                break
+        return tuple(outs)
+
+
 def create_model(name, **kwargs):
     if name not in MODEL_CONFIGS:
         raise ValueError(f"Unknown model {name!r}; choose from {tuple(MODEL_CONFIGS)}")
