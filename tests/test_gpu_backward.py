@@ -252,3 +252,18 @@ def test_residual_add_drop_path_and_determinism():
     r1 = residual_add_backward(gout, br, gamma, mask)
     r2 = residual_add_backward(gout, br, gamma, mask)
     assert all(torch.equal(a, b) for a, b in zip(r1, r2))
+
+
+def test_srnl_backward_recompute_path_matches_full_history(monkeypatch):
+    """head_dim 16 keeps the whole G history when it fits (the default here); with the history
+    budget at 0 the backward recomputes each chunk's history instead.  Both give the same
+    gradients (the same arithmetic in the same order)."""
+    from visionhope_b200.srnl_core.chunk import sequence_backward
+
+    mems, x, q, gy = _srnl_case(11, 2, 4, 2, 90, 16, False, False, torch.float32)
+    args = ([m.to(DEV) for m in mems], x.to(DEV), q.to(DEV), [20] * 4, gy.to(DEV))
+    full = sequence_backward(*args, q_normalized=False)
+    monkeypatch.setenv("VHOPE_SRNL_BWD_HISTORY_BYTES", "0")
+    rec = sequence_backward(*args, q_normalized=False)
+    flat = lambda r: [*r[0], r[1], r[2]]
+    assert all(torch.equal(a, b) for a, b in zip(flat(full), flat(rec)))

@@ -19,6 +19,7 @@
 // bit-reproducible.  Shared (per direction and head) memories get their gradient as the sum
 // over the batch of the per-chain ones, added in batch order by a second kernel.
 #include <algorithm>
+#include <cstdlib>
 #include <climits>
 
 #include "abi_util.h"
@@ -46,8 +47,10 @@ struct Params {
     float* dq;        // q's layout
     float* dS;        // [chains][(3D+2) D]: gradient of the chain's initial state
     float* states;    // [chains][nchunks_max][(3D+2) D]
-    float* gseq;      // [chains][gseq_stride]: G_{t-1} of each token of the chunk being reversed
+    float* gseq;      // [chains][gseq_stride]: G_{t-1} of each token (one chunk, or all: full_history)
     int64_t gseq_stride;
+    int full_history;  // head_dim 16: sweep A keeps every token's G_{t-1} and each chunk's G_T
+    float* gend;       // [chains][nchunks_max][D D]: G_T of each chunk (full_history)
     int B, R, heads, L, nchunks_max;
     int chunk[4];
     SrnlConsts k;
@@ -462,27 +465,38 @@ __global__ void __launch_bounds__(kT) srnl_bwd_kernel(const Params p) {
 
 // Gradients of shared memories: the per-chain ones summed over the batch, in batch order, and
 // split into the five parameter tensors ([R, heads, D, D] x 3, [R, heads, D] x 2).
+// Grid (slot, block of 64 state entries); each thread sums one entry over the batch with
+// eight loads in flight.
+constexpr int kMemThreads = 64;
+
 template <int D>
-__global__ void __launch_bounds__(kT) srnl_bwd_mem_kernel(const float* __restrict__ dS, int B, int R, int heads,
-                                                          int per_chain, float* __restrict__ dMm,
-                                                          float* __restrict__ dMv, float* __restrict__ dMk,
-                                                          float* __restrict__ dMe, float* __restrict__ dMa) {
+__global__ void __launch_bounds__(kMemThreads) srnl_bwd_mem_kernel(const float* __restrict__ dS, int B, int R,
+                                                                   int heads, int per_chain, float* __restrict__ dMm,
+                                                                   float* __restrict__ dMv, float* __restrict__ dMk,
+                                                                   float* __restrict__ dMe, float* __restrict__ dMa) {
     constexpr int SR = 3 * D + 2;
     const int64_t slot = blockIdx.x;  // per_chain: chain; else r * heads + head
+    const int e = blockIdx.y * kMemThreads + threadIdx.x;
+    if (e >= SR * D) return;
     const int nb = per_chain ? 1 : B;
-    for (int e = threadIdx.x; e < SR * D; e += kT) {
-        float a = 0.f;
-        for (int bb = 0; bb < nb; ++bb) {
-            const int64_t chain = per_chain ? slot : (int64_t)bb * R * heads + slot;
-            a += dS[chain * SR * D + e];
-        }
-        const int row = e / D, col = e % D;
-        if (row < D) dMm[(slot * D + row) * D + col] = a;
-        else if (row < 2 * D) dMv[(slot * D + row - D) * D + col] = a;
-        else if (row < 3 * D) dMk[(slot * D + row - 2 * D) * D + col] = a;
-        else if (row == 3 * D) dMe[slot * D + col] = a;
-        else dMa[slot * D + col] = a;
+    const int64_t stride = (int64_t)R * heads * SR * D;  // from one image's chain to the next
+    const float* src = dS + slot * SR * D + e;
+    float a = 0.f;
+    int bb = 0;
+    for (; bb + 8 <= nb; bb += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = src[(int64_t)(bb + u) * stride];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a += v[u];
     }
+    for (; bb < nb; ++bb) a += src[(int64_t)bb * stride];
+    const int row = e / D, col = e % D;
+    if (row < D) dMm[(slot * D + row) * D + col] = a;
+    else if (row < 2 * D) dMv[(slot * D + row - D) * D + col] = a;
+    else if (row < 3 * D) dMk[(slot * D + row - 2 * D) * D + col] = a;
+    else if (row == 3 * D) dMe[slot * D + col] = a;
+    else dMa[slot * D + col] = a;
 }
 
 #include "srnl_bwd_warp.cuh"
@@ -495,26 +509,50 @@ using namespace vh::sbwd;
 
 namespace {
 
-// Floats of G_{t-1} history per chain: the longest chunk (head_dim 16, the warp kernel, takes
-// any chunk length) or kMaxT tokens.
+// The whole G_{t-1} history is kept (head_dim 16) while it stays within this many bytes: 6 GiB,
+// or VHOPE_SRNL_BWD_HISTORY_BYTES (0: always recompute each chunk's history, the smaller
+// workspace).  Read at each call, so the workspace query and the call agree while it is unchanged.
+int64_t history_cap() {
+    const char* e = std::getenv("VHOPE_SRNL_BWD_HISTORY_BYTES");
+    return e && *e ? std::atoll(e) : ((int64_t)6 << 30);
+}
+
+int max_chunks(const vh_srnl_sequence_bwd_args* a) {
+    int n = 1;
+    for (int r = 0; r < a->dirs; ++r) n = std::max(n, (a->length + a->chunk[r] - 1) / a->chunk[r]);
+    return n;
+}
+
+int64_t max_chunk_len(const vh_srnl_sequence_bwd_args* a) {
+    int64_t t = 1;
+    for (int r = 0; r < a->dirs; ++r) t = std::max<int64_t>(t, std::min(a->chunk[r], a->length));
+    return t;
+}
+
+template <int D>
+bool full_history(const vh_srnl_sequence_bwd_args* a) {
+    if (D != 16) return false;
+    const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
+    return chains * max_chunks(a) * max_chunk_len(a) * D * D * (int64_t)sizeof(float) <= history_cap();
+}
+
+// Floats of G_{t-1} history per chain: every token (full history), the longest chunk (head_dim
+// 16, the warp kernel, takes any chunk length) or kMaxT tokens.
 template <int D>
 int64_t gseq_floats(const vh_srnl_sequence_bwd_args* a) {
-    int64_t t = kMaxT;
-    if (D == 16) {
-        t = 1;
-        for (int r = 0; r < a->dirs; ++r) t = std::max<int64_t>(t, std::min(a->chunk[r], a->length));
-    }
-    return t * D * D;
+    if (D != 16) return (int64_t)kMaxT * D * D;
+    const int64_t t = max_chunk_len(a);
+    return (full_history<D>(a) ? max_chunks(a) * t : t) * D * D;
 }
 
 template <int D>
 int64_t bwd_workspace(const vh_srnl_sequence_bwd_args* a, int* nmax) {
-    int n = 1;
-    for (int r = 0; r < a->dirs; ++r) n = std::max(n, (a->length + a->chunk[r] - 1) / a->chunk[r]);
+    const int n = max_chunks(a);
     if (nmax) *nmax = n;
     const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
     const int64_t SR = 3 * D + 2;
-    return chains * ((int64_t)n * SR * D + gseq_floats<D>(a) + SR * D) * (int64_t)sizeof(float);
+    const int64_t gend = full_history<D>(a) ? (int64_t)n * D * D : 0;
+    return chains * ((int64_t)n * SR * D + gseq_floats<D>(a) + SR * D + gend) * (int64_t)sizeof(float);
 }
 
 int64_t gseq_floats_d(const vh_srnl_sequence_bwd_args* a) {
@@ -554,8 +592,10 @@ int launch_bwd(const vh_srnl_sequence_bwd_args* a, Params p, cudaStream_t st) {
     int rc = launch_status("vh_srnl_sequence_bwd");
     if (rc) return rc;
     const int64_t slots = a->mem.per_chain ? chains : (int64_t)a->dirs * a->heads;
-    srnl_bwd_mem_kernel<D><<<(unsigned)slots, kT, 0, st>>>(p.dS, a->batch, a->dirs, a->heads, a->mem.per_chain ? 1 : 0,
-                                                           a->grad_m, a->grad_v, a->grad_k, a->grad_eta, a->grad_alpha);
+    constexpr int SRD = (3 * D + 2) * D;
+    srnl_bwd_mem_kernel<D><<<dim3((unsigned)slots, (SRD + kMemThreads - 1) / kMemThreads), kMemThreads, 0, st>>>(
+        p.dS, a->batch, a->dirs, a->heads, a->mem.per_chain ? 1 : 0, a->grad_m, a->grad_v, a->grad_k, a->grad_eta,
+        a->grad_alpha);
     return launch_status("vh_srnl_sequence_bwd (memories)");
 }
 
@@ -628,6 +668,8 @@ extern "C" int vh_srnl_sequence_bwd(const vh_srnl_sequence_bwd_args* a, void* wo
     p.gseq = p.states + chains * (int64_t)nmax * SR * D;
     p.gseq_stride = gseq_floats_d(a);
     p.dS = p.gseq + chains * p.gseq_stride;
+    p.full_history = a->head_dim == 16 && full_history<16>(a) ? 1 : 0;
+    p.gend = p.dS + chains * SR * D;  // used (and sized) only with full_history
     p.B = a->batch; p.R = a->dirs; p.heads = a->heads; p.L = a->length; p.nchunks_max = nmax;
     for (int r = 0; r < 4; ++r) p.chunk[r] = r < a->dirs ? a->chunk[r] : 1;
     const vh_srnl_consts& c = a->consts;

@@ -8,8 +8,11 @@
 //     lane (lane = 2 i + h: row i, columns 8h..8h+7).  The reverse step also forms the
 //     quantities that need dG_t itself (dG k, <dG, G_{t-1}>, -eff dG^T r + G_{t-1}^T dr and
 //     d eff) with warp shuffles, and leaves the rest of the gate adjoint to the token-parallel
-//     phase.  G_{t-1} of every token is written to the workspace by the forward pass of the chunk
-//     and read back, one token ahead, by the reverse pass.
+//     phase.  G_{t-1} of every token is written to the workspace by the gain recurrence and read
+//     back, one token ahead, by the reverse pass.  When the whole history fits the workspace
+//     budget (`full_history`), sweep A writes it for every chunk, with each chunk's final gain,
+//     and sweep B does not run the gain recurrence again; otherwise sweep B recomputes each
+//     chunk's history just before reversing it.
 // The token-parallel phases that run once per tile (dx, the parameter adjoint) are kept as
 // loops rather than unrolled: with eleven warps per SM in different phases, instruction fetch
 // is the largest stall, and the smaller code measured faster (as did a prefetch distance of one
@@ -348,7 +351,7 @@ __device__ __forceinline__ void gate_adjoint(WSmem& s, const SrnlConsts& K, int 
     rec[R_DAP][tt] = d_ap;
 }
 
-__device__ __forceinline__ void load_ring(const float* gseq, int t, int lane, float (&g)[8]) {
+__device__ __forceinline__ void load_ring(const float* gseq, int64_t t, int lane, float (&g)[8]) {
     const float* gp = gseq + (int64_t)t * (D * D) + lane * 8;
     const float4 a = ldcg4(gp), c = ldcg4(gp + 4);
     g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
@@ -368,6 +371,10 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
     const int nch = (p.L + Lc - 1) / Lc;
     float* states = p.states + chain * (int64_t)p.nchunks_max * SR * D;
     float* gseq = p.gseq + chain * p.gseq_stride;
+    // full: sweep A keeps G_{t-1} of every token of the sequence and each chunk's final gain,
+    // and sweep B reads them instead of running the gain recurrence a second time.
+    const bool full = p.full_history != 0;
+    float* gend = p.gend + chain * (int64_t)p.nchunks_max * (D * D);
     const int i = lane >> 1, h = lane & 1;
     const int rb = lane >> 4, col = lane & 15;  // element layout of dS: rows rb + 2k, column col
 
@@ -390,7 +397,13 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
         for (int e = lane; e < SR * D; e += 32) states[(int64_t)c * SR * D + e] = s.S[e / D][e % D];
         if (c + 1 == nch) break;
         float G[8];
-        chunk_gain_warp<XT, QT>(p, s, chain, b, r, head, (int64_t)c * Lc, Lc, nullptr, G, lane);
+        chunk_gain_warp<XT, QT>(p, s, chain, b, r, head, (int64_t)c * Lc, Lc,
+                                full ? gseq + (int64_t)c * Lc * (D * D) : nullptr, G, lane);
+        if (full) {
+            float* ge = gend + (int64_t)c * (D * D) + lane * 8;
+            stcg4(ge, make_float4(G[0], G[1], G[2], G[3]));
+            stcg4(ge + 4, make_float4(G[4], G[5], G[6], G[7]));
+        }
         // S <- S G
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) s.m.GT[i][8 * h + jj] = G[jj];
@@ -428,9 +441,14 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
         float dG[8];
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) dG[jj] = 0.f;
+        const float* gseq_c = full ? gseq + (int64_t)c * Lc * (D * D) : gseq;
         if (!last) {
             float G[8];
-            chunk_gain_warp<XT, QT>(p, s, chain, b, r, head, tok0, n, gseq, G, lane);
+            if (full) {
+                load_ring(gend + (int64_t)c * (D * D), 0, lane, G);  // G_T kept by sweep A
+            } else {
+                chunk_gain_warp<XT, QT>(p, s, chain, b, r, head, tok0, n, gseq, G, lane);
+            }
             // dG_T = S_c^T dS_{c+1};  dS_c starts as dS_{c+1} G_T^T
 #pragma unroll
             for (int k = 0; k < SR * D / 32; ++k) s.m.dS[rb + 2 * k][col] = dS[k];
@@ -461,10 +479,10 @@ __global__ void __launch_bounds__(32, 11) srnl_bwd_warp_kernel(const Params p) {
             __syncwarp();
             if (!last) {
                 float gc[8], gn[8];
-                load_ring(gseq, t0 + nt - 1, lane, gc);
+                load_ring(gseq_c, t0 + nt - 1, lane, gc);
 #pragma unroll 1
                 for (int tt = nt - 1; tt >= 0; --tt) {
-                    if (tt > 0) load_ring(gseq, t0 + tt - 1, lane, gn);
+                    if (tt > 0) load_ring(gseq_c, t0 + tt - 1, lane, gn);
                     reverse_step(s, tt, gc, dG, lane);
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj) gc[jj] = gn[jj];
