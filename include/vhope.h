@@ -366,12 +366,17 @@ int vh_add_layernorm_fwd(const void* x, int32_t x_dtype, const void* r, int32_t 
  * of the size their *_workspace_bytes function gives.
  * =====================================================================================*/
 
-/* SRNL recurrence backward for packed sequences (chunks of up to 64 tokens, head_dim 4, 8, 16
- * or 32); replaces models/srnl_core/csrc/chunk.cu:511-1057, 1133-1206 `srnl_backward` /
- * `srnl_backward_qraw` (chunk.py:286-359 SRNLNormalizedQueryFunction.backward, 507-588
- * SRNLRawQueryFunction.backward).  The inputs are the forward's (mem, x, q, q_mode, sizes,
- * chunks, consts: see vh_srnl_sequence_args); nothing from the forward is saved besides them:
- * the chunk states and the gain sequence are recomputed.  grad_y fp32 [B, R, heads, L, D].
+/* SRNL recurrence backward for packed sequences (head_dim 16: any chunk length; head_dim 4, 8
+ * or 32: chunks of up to 64 tokens); replaces models/srnl_core/csrc/chunk.cu:511-1057,
+ * 1133-1206 `srnl_backward` / `srnl_backward_qraw` (chunk.py:286-359
+ * SRNLNormalizedQueryFunction.backward, 507-588 SRNLRawQueryFunction.backward) and
+ * models/srnl_core/csrc/lines.cu:252-669 (lines.py: srnl_long_chunk, srnl_variable_lines).  The
+ * inputs are the forward's (mem, x, q, q_mode, sizes, chunks, consts: see
+ * vh_srnl_sequence_args); nothing from the forward is saved besides them: the chunk states and
+ * the gain sequence are recomputed.  For head_dim 16 the workspace holds the whole gain history
+ * when that fits 6 GiB (environment variable VHOPE_SRNL_BWD_HISTORY_BYTES sets the budget; 0
+ * keeps one chunk's history and recomputes it per chunk); the workspace size and the call must
+ * see the same setting.  grad_y fp32 [B, R, heads, L, D].
  * Writes grad_x (fp32, x's shape), grad_q (fp32, q's shape: [B, R, L, C] for raw queries,
  * through their normalization; [B, R, heads, L, D] for normalized ones) and grad_m, grad_v,
  * grad_k, grad_eta, grad_alpha (fp32, the memories' shapes; shared memories get the sum over the
