@@ -489,9 +489,16 @@ __global__ void __launch_bounds__(kThreads) grn_dx_kernel(const float* __restric
     const int64_t base = (int64_t)b * S * C;
     const float* f1b = f1 + (int64_t)b * C;
     const float* f2b = f2 + (int64_t)b * C;
-    for (int64_t v = (int64_t)blockIdx.x * kThreads + threadIdx.x; v < per; v += (int64_t)gridDim.x * kThreads) {
+    // The channel of vector v, v mod (C / W), kept up to date by adding the stride's remainder
+    // (no 64-bit division per vector).
+    const int CV = C / W;
+    const int64_t stride = (int64_t)gridDim.x * kThreads;
+    const int smod = (int)(stride % CV);
+    int64_t v = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    int cv = (int)(v % CV);
+    for (; v < per; v += stride, cv = cv + smod >= CV ? cv + smod - CV : cv + smod) {
         const int64_t i = base + v * W;
-        const int c = (int)((v * W) % C);
+        const int c = cv * W;
         if constexpr (VEC) {
             const float4 g = load4(dy + i), xv = load4(x + i), a = load4(f1b + c), bq = load4(f2b + c);
             store4(dx + i, make_float4(fmaf(g.x, a.x, xv.x * bq.x), fmaf(g.y, a.y, xv.y * bq.y),
@@ -510,7 +517,25 @@ __global__ void __launch_bounds__(kThreads) grn_param_kernel(const float* __rest
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
     float a = 0.f, bsum = 0.f;
-    for (int b = 0; b < B; ++b) {
+    int b = 0;
+    // Eight images' loads in flight per batch; the sums stay in image order.
+    for (; b + 8 <= B; b += 8) {
+        float g[8], iv[8], tv[8], db[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int64_t i = (int64_t)(b + u) * C + c;
+            g[u] = gx[i];
+            iv[u] = inv_den[b + u];
+            tv[u] = t[i];
+            db[u] = dbeta_bc[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            a = fmaf(g[u] * iv[u], tv[u], a);
+            bsum += db[u];
+        }
+    }
+    for (; b < B; ++b) {
         a = fmaf(gx[(int64_t)b * C + c] * inv_den[b], t[(int64_t)b * C + c], a);
         bsum += dbeta_bc[(int64_t)b * C + c];
     }
@@ -749,8 +774,8 @@ extern "C" int vh_grn_bwd(const float* grad_y, const void* x, int32_t x_dtype, c
             grn_dx_kernel<T, false><<<dim3(gx_blocks, batch), kThreads, 0, st>>>(grad_y, xp, f1, f2, static_cast<T*>(grad_x),
                                                                                 (int)S, channels);
         if ((r = launch_status("vh_grn_bwd (dx)"))) return r;
-        grn_param_kernel<<<(channels + kThreads - 1) / kThreads, kThreads, 0, st>>>(t, gx, inv_den, dbeta_bc, batch,
-                                                                                   channels, grad_gamma, grad_beta);
+        grn_param_kernel<<<(channels + 63) / 64, 64, 0, st>>>(t, gx, inv_den, dbeta_bc, batch, channels, grad_gamma,
+                                                             grad_beta);
         return launch_status("vh_grn_bwd (params)");
     });
 }

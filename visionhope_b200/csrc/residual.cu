@@ -88,8 +88,14 @@ __global__ void __launch_bounds__(kThreads) residual_bwd_kernel(const float* __r
 #pragma unroll
         for (int v = 0; v < V; ++v) g[v] = gamma[c + v];
         const int64_t r1 = std::min<int64_t>(rows, (int64_t)(blockIdx.x + 1) * rpp);
-        for (int64_t r = (int64_t)blockIdx.x * rpp + rl; r < r1; r += lanes) {
-            const float m = drop[r / spatial];
+        int64_t r = (int64_t)blockIdx.x * rpp + rl;
+        int64_t bi = r / spatial, bend = (bi + 1) * spatial;  // image of row r, and its end
+        for (; r < r1; r += lanes) {
+            while (r >= bend) {
+                ++bi;
+                bend += spatial;
+            }
+            const float m = drop[bi];
             const int64_t off = r * C + c;
             if constexpr (V == 4) {
                 const float4 d = *reinterpret_cast<const float4*>(dout + off);
