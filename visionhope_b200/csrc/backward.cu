@@ -76,14 +76,17 @@ int qnorm_bwd_dispatch(int D, const float* g, const float* q, const float* inv, 
 // l_d the position of pixel pix in scan d.  So for every (b, d, pixel, c):
 //   dy_d = scale[d, c] g,   dx_d = scale[d, c] skip_d[c] g,
 //   dscale[d, c] += g (y_d + skip_d[c] x_d),   dskip_d[c] += g scale[d, c] x_d.
-// CTA = (b, head, group of `tpc` tiles of kPix row-major pixels): each tile's gradient is
+// CTA = (b, head, group of `tpc` tiles of 8 x 8 pixels): each tile's gradient is
 // staged in shared memory first (read along whichever axis is contiguous), then each thread
 // takes (pixel, group of 4 channels) items, always of the same channel group, and keeps its
 // partial sums in registers across the CTA's tiles; the CTA adds them over its threads in a
 // fixed order and writes one partial row per (image, tile group).  reduce_parts_kernel adds the
 // partial rows in order.  The tile group depends on the sizes only, so the summation order is
 // the same on every GPU.
-constexpr int kPix = 64;
+constexpr int kPix = 64;  // an 8 x 8 pixel tile: rows of 8 pixels for the row scans and columns
+                          // of 8 for the column scans, so every scan reads runs of 8 positions
+
+__host__ __device__ inline int dirfuse_tiles(int H, int W) { return ((H + 7) / 8) * ((W + 7) / 8); }
 
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
@@ -96,7 +99,8 @@ __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
     __shared__ float red[kThreads / G4][8][4];
     const int64_t L = (int64_t)H * W;
     const int C = heads * D;
-    const int tiles = (int)((L + kPix - 1) / kPix);
+    const int tiles = dirfuse_tiles(H, W);
+    const int tcols = (W + 7) / 8;
     const int ngroups = (tiles + tpc - 1) / tpc;
     const int group = blockIdx.x % ngroups;
     const int head = (blockIdx.x / ngroups) % heads;
@@ -115,25 +119,21 @@ __global__ void __launch_bounds__(kThreads) dirfuse_bwd_kernel(
     float ps[4][4] = {}, pk[4][4] = {};
     const int tile_end = min(tiles, (group + 1) * tpc);
     for (int tile = group * tpc; tile < tile_end; ++tile) {
-        const int64_t pix0 = (int64_t)tile * kPix;
+        const int ti0 = (tile / tcols) * 8, tj0 = (tile % tcols) * 8;
         __syncthreads();  // the previous tile's gradient has been read
         for (int it = threadIdx.x; it < D * kPix; it += kThreads) {
             const int k = pix_fast ? it % kPix : it / D, ch = pix_fast ? it / kPix : it % D;
-            const int64_t pix = pix0 + k;
+            const int pi = ti0 + (k >> 3), pj = tj0 + (k & 7);
             float v = 0.f;
-            if (pix < L) {
-                const int64_t pi = pix / W, pj = pix - pi * W;
-                v = g[b * gsb + (int64_t)(head * D + ch) * gsc + pi * gsh + pj * gsw];
-            }
+            if (pi < H && pj < W) v = g[b * gsb + (int64_t)(head * D + ch) * gsc + (int64_t)pi * gsh + (int64_t)pj * gsw];
             gt[ch][k] = v;
         }
         __syncthreads();
         for (int it = threadIdx.x; it < kPix * G4; it += kThreads) {
             const int k = it / G4;
-            const int64_t pix = pix0 + k;
-            if (pix >= L) break;
-            const int64_t pi = pix / W, pj = pix - pi * W;
-            const int64_t lhw = pix, lwh = pj * H + pi;
+            const int pi = ti0 + (k >> 3), pj = tj0 + (k & 7);
+            if (pi >= H || pj >= W) continue;
+            const int64_t lhw = (int64_t)pi * W + pj, lwh = (int64_t)pj * H + pi;
             const int64_t ls[4] = {lhw, L - 1 - lhw, lwh, L - 1 - lwh};
             const float gv[4] = {gt[grp * 4][k], gt[grp * 4 + 1][k], gt[grp * 4 + 2][k], gt[grp * 4 + 3][k]};
 #pragma unroll
@@ -563,13 +563,13 @@ int by_dtype(int dt, F&& f) {
 // Tiles per CTA of the direction-fusion backward: about 2368 CTAs (two waves of eight per SM
 // on 148 SMs), at most 16 tiles; from the sizes alone.
 int dirfuse_tpc(int batch, int heads, int height, int width) {
-    const int64_t tiles = ((int64_t)height * width + kPix - 1) / kPix;
+    const int64_t tiles = dirfuse_tiles(height, width);
     const int64_t want = ((int64_t)batch * heads * tiles + 2367) / 2368;
     return (int)std::max<int64_t>(1, std::min<int64_t>(16, want));
 }
 
 int64_t dirfuse_parts(int batch, int heads, int height, int width) {
-    const int64_t tiles = ((int64_t)height * width + kPix - 1) / kPix;
+    const int64_t tiles = dirfuse_tiles(height, width);
     const int tpc = dirfuse_tpc(batch, heads, height, width);
     return (int64_t)batch * ((tiles + tpc - 1) / tpc);
 }
@@ -620,7 +620,7 @@ extern "C" int vh_dirfuse_bwd(const float* grad_out, int64_t gs_b, int64_t gs_c,
     if ((int64_t)batch * 4 * L * heads * head_dim > ((int64_t)1 << 40) || batch > 65535)
         return fail(VH_E_RANGE, "vh_dirfuse_bwd: too many elements");
     const int C = heads * head_dim;
-    const int tiles = (int)((L + kPix - 1) / kPix);
+    const int tiles = dirfuse_tiles(height, width);
     if (!head_dim_ok(head_dim)) return fail(VH_E_HEADDIM, "vh_dirfuse_bwd: unsupported head_dim %d", head_dim);
     if (!aligned(y, io_dtype == VH_F32 ? 16 : 8) || !aligned(x, io_dtype == VH_F32 ? 16 : 8) ||
         !aligned(grad_y, io_dtype == VH_F32 ? 16 : 8) || !aligned(grad_x, io_dtype == VH_F32 ? 16 : 8))
