@@ -229,3 +229,53 @@ def test_dwconv_tile_count_query():
     assert lib.vh_dwconv_tiles(7, 7) == 1      # whole images, four per CTA
     assert lib.vh_dwconv_tiles(32, 32) == 4    # 16 x 16 tiles
     assert lib.vh_dwconv_tiles(0, 5) == 0
+
+
+def _bwd_args(lib_mod, p, **kw):
+    base = dict(x_dtype=0, q_dtype=0, q_mode=0, batch=2, dirs=4, heads=2, length=100, head_dim=16,
+                chunk=(100, 100, 100, 100))
+    base.update(kw)
+    k = lib_mod.consts(0.025, 0, 2.2, 0.999, 0.999999)
+    return lib_mod.VhSequenceBwdArgs(lib_mod.VhMemories(p, p, p, p, p, 0), p, p, base["x_dtype"], base["q_dtype"],
+                                     base["q_mode"], p, p, p, p, p, p, p, p, base["batch"], base["dirs"],
+                                     base["heads"], base["length"], base["head_dim"],
+                                     (lib_mod.c_int32 * 4)(*base["chunk"]), k)
+
+
+def test_sequence_backward_validation_and_workspace(monkeypatch):
+    """vh_srnl_sequence_bwd's host checks (no GPU): chunks past 64 tokens are taken for head_dim
+    16 only; the workspace query grows with the kept gain history, which
+    VHOPE_SRNL_BWD_HISTORY_BYTES=0 turns off; a short workspace is refused before any launch."""
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    a8 = _bwd_args(_lib, p, head_dim=8)
+    assert lib.vh_srnl_sequence_bwd(ctypes.byref(a8), p, 1 << 40, None) == -6
+    assert "MAX_CHUNK" in _err(lib)
+    a16 = _bwd_args(_lib, p)
+    full = lib.vh_srnl_sequence_bwd_workspace_bytes(ctypes.byref(a16))
+    chains, n, Lc = 2 * 4 * 2, 1, 100
+    # states + full history + dS + chunk-end gains (floats)
+    assert full == 4 * chains * (n * 800 + n * Lc * 256 + 800 + n * 256)
+    monkeypatch.setenv("VHOPE_SRNL_BWD_HISTORY_BYTES", "0")
+    small = lib.vh_srnl_sequence_bwd_workspace_bytes(ctypes.byref(a16))
+    assert small == 4 * chains * (n * 800 + Lc * 256 + 800)
+    assert lib.vh_srnl_sequence_bwd(ctypes.byref(a16), p, small - 4, None) == -1
+    assert "workspace too small" in _err(lib)
+
+
+def test_residual_and_norm_backward_validation():
+    from visionhope_b200 import _lib
+
+    lib = _lib.load()
+    p, keep = _fake()
+    assert lib.vh_residual_add_fwd(p, 0, p, 9, p, p, p, 2, 4, 8, None) == -3
+    assert lib.vh_residual_add_fwd(p, 0, p, 0, p, p, p, 0, 4, 8, None) == -2
+    assert lib.vh_residual_add_fwd(None, 0, p, 0, p, p, p, 2, 4, 8, None) == -1
+    need = lib.vh_residual_add_bwd_workspace_bytes(2 * 4, 8)
+    assert need == 4 * 8  # one partial row for 8 rows
+    assert lib.vh_residual_add_bwd(p, p, 0, p, p, p, p, p, need - 4, 2, 4, 8, None) == -1
+    assert "workspace too small" in _err(lib)
+    assert lib.vh_layernorm_bwd_workspace_bytes(1000, 96) == 4 * 2 * 96 * (4 + 1)
+    assert lib.vh_layernorm_bwd(p, p, 0, p, p, p, p, p, p, p, 16, 1000, 96, None) == -1
