@@ -82,8 +82,11 @@ def test_dirfuse_backward_is_deterministic():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("B,C,H,W", [(2, 96, 14, 14), (3, 40, 5, 7), (1, 768, 7, 7), (2, 1000, 3, 3)])
+@pytest.mark.parametrize("B,C,H,W", [(2, 96, 14, 14), (3, 40, 5, 7), (2, 256, 9, 9), (1, 500, 7, 7),
+                                     (1, 768, 7, 7), (2, 1000, 3, 3)])
 def test_layernorm_backward(dtype, B, C, H, W):
+    """One-pass kernels for C <= 128 (eight lanes per row) and C <= 512 (a warp per row), the
+    two-kernel path above; 500 leaves lanes without a channel."""
     from visionhope_b200.utils.layer_norm_cuda import visionhope_layernorm2d
 
     g = torch.Generator().manual_seed(B + C + H)

@@ -391,6 +391,77 @@ __global__ void __launch_bounds__(kThreads) ln_fused_kernel(const float* __restr
     }
 }
 
+// ln_fused_wide_kernel (kLnFusedMaxC < C <= kLnWideMaxC): the one-pass backward with a warp
+// per row, lane l owning channels l + 32 m; the same block of kLnRows rows per CTA (32 rows per
+// warp), the warps' dw, db sums added in order through shared memory.
+constexpr int kLnWideMaxC = 512;
+
+template <typename T, int NM>
+__global__ void __launch_bounds__(kThreads) ln_fused_wide_kernel(const float* __restrict__ dy,
+                                                                 const T* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 const float* __restrict__ mean,
+                                                                 const float* __restrict__ rstd,
+                                                                 T* __restrict__ dx, float* __restrict__ part,
+                                                                 int64_t rows, int C) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float wv[NM], aw[NM], ab[NM];
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+        const int c = lane + 32 * m;
+        wv[m] = c < C ? w[c] : 0.f;
+        aw[m] = 0.f;
+        ab[m] = 0.f;
+    }
+    const float invC = 1.f / (float)C;
+    const int64_t r0 = (int64_t)blockIdx.x * kLnRows;
+    for (int it = 0; it < kLnRows / (kThreads / 32); ++it) {
+        const int64_t r = r0 + it * (kThreads / 32) + warp;
+        if (r >= rows) break;  // uniform across the warp
+        const float* gr = dy + r * C;
+        const T* xr = x + r * C;
+        const float mu = mean[r], rs = rstd[r];
+        float gv[NM], xh[NM], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+            const int c = lane + 32 * m;
+            const bool ok = c < C;
+            gv[m] = ok ? gr[c] : 0.f;
+            xh[m] = ok ? (to_f(xr[c]) - mu) * rs : 0.f;
+            const float wg = wv[m] * gv[m];
+            s1 += wg;
+            s2 = fmaf(wg, xh[m], s2);
+            aw[m] = fmaf(gv[m], xh[m], aw[m]);
+            ab[m] += gv[m];
+        }
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        const float a = s1 * invC, bq = s2 * invC;
+        T* dxr = dx + r * C;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+            const int c = lane + 32 * m;
+            if (c < C) dxr[c] = from_f<T>((wv[m] * gv[m] - a - xh[m] * bq) * rs);
+        }
+    }
+    __shared__ float red[kThreads / 32][2][kLnWideMaxC];
+#pragma unroll
+    for (int m = 0; m < NM; ++m) {
+        const int c = lane + 32 * m;
+        if (c < C) {
+            red[warp][0][c] = aw[m];
+            red[warp][1][c] = ab[m];
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 2 * C; e += kThreads) {
+        const int q = e / C, c = e - q * C;
+        float t = red[0][q][c];
+        for (int k = 1; k < kThreads / 32; ++k) t += red[k][q][c];
+        part[((int64_t)blockIdx.x * 2 + q) * C + c] = t;
+    }
+}
+
 // ---- GRN (grn_cuda.cu:126-265) ------------------------------------------------------------
 // y = x (1 + gamma Nx) + beta, Nx = Gx inv, Gx[b, c] = ||x[b, :, c]||, inv = 1 / (mean_c Gx + eps).
 // With t[b, c] = sum_s dy x and s = gamma t:
@@ -687,6 +758,15 @@ extern "C" int vh_layernorm_bwd(const float* grad_y, const void* x, int32_t x_dt
                 ln_fused_kernel<T, 16><<<(unsigned)rblocks, kThreads, 0, st>>>(
                     grad_y, static_cast<const T*>(x), weight, mean, rstd, static_cast<T*>(grad_x), part, rows, channels);
             return launch_status("vh_layernorm_bwd (fused)");
+        }
+        if (channels <= kLnWideMaxC) {
+            if (channels <= 256)
+                ln_fused_wide_kernel<T, 8><<<(unsigned)rblocks, kThreads, 0, st>>>(
+                    grad_y, static_cast<const T*>(x), weight, mean, rstd, static_cast<T*>(grad_x), part, rows, channels);
+            else
+                ln_fused_wide_kernel<T, 16><<<(unsigned)rblocks, kThreads, 0, st>>>(
+                    grad_y, static_cast<const T*>(x), weight, mean, rstd, static_cast<T*>(grad_x), part, rows, channels);
+            return launch_status("vh_layernorm_bwd (fused, wide rows)");
         }
         const int64_t grid = (rows + 4 * (kThreads / 32) - 1) / (4 * (kThreads / 32));
         if (grid > INT32_MAX) return fail(VH_E_RANGE, "vh_layernorm_bwd: too many rows");
