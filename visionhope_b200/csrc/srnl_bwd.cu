@@ -533,7 +533,9 @@ template <int D>
 bool full_history(const vh_srnl_sequence_bwd_args* a) {
     if (D != 16) return false;
     const int64_t chains = (int64_t)a->batch * a->dirs * a->heads;
-    return chains * max_chunks(a) * max_chunk_len(a) * D * D * (int64_t)sizeof(float) <= history_cap();
+    const int64_t per_chain = (int64_t)max_chunks(a) * max_chunk_len(a) * D * D * (int64_t)sizeof(float);
+    const int64_t cap = history_cap();
+    return cap > 0 && chains <= cap / per_chain;  // no overflow of chains x per_chain
 }
 
 // Floats of G_{t-1} history per chain: every token (full history), the longest chunk (head_dim

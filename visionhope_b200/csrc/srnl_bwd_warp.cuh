@@ -15,8 +15,8 @@
 //     chunk's history just before reversing it.
 // The token-parallel phases that run once per tile (dx, the parameter adjoint) are kept as
 // loops rather than unrolled: with eleven warps per SM in different phases, instruction fetch
-// is the largest stall, and the smaller code measured faster (as did a prefetch distance of one
-// token over two to eight).
+// had been the largest stall, and the smaller code measured faster (as did a prefetch distance
+// of one token over two to eight).
 // Tokens past the sequence end in the last chunk are skipped: the last chunk's gain is never
 // applied, so its dG is zero throughout and those tokens contribute nothing.
 #pragma once
