@@ -179,3 +179,47 @@ def test_block_training_matches_reference():
     for name, a in out["native"].items():
         err = rel_err(out["dropin"][name], a)
         assert err < 5e-4, f"{name}: {err:.3e}"
+
+
+def test_visionhope_tiny_training_matches_reference():
+    """The reference's whole VisionHOPE-T (models/factory.py, unchanged) trained for one step in
+    fp32 at 2 x 3 x 64 x 64 with drop path on and LayerScale 0.1 (every block matters), native
+    against drop-in, the same seeds: the input's and every parameter's gradient.  Bar: 3e-3
+    normwise over all gradients together and 2e-2 per tensor (29 SRNL recurrences and their
+    backward in a different summation order, through the whole network; measured on a B200:
+    1.5e-3 together, 6.1e-3 for the worst tensor, the first stage's alpha memory).  The BatchNorm
+    layers run with frozen statistics (eval mode, as the reference's dense adapter's norm_eval
+    does): in training mode a BatchNorm's input gradient sums to zero over the batch, so the
+    biases feeding it linearly (the final norm's, the head projection's) have an exact gradient
+    of zero and a relative error of rounding noise on both sides."""
+    from tests.conftest import reference as ref_mode
+
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(2, 3, 64, 64, generator=g).contiguous(memory_format=torch.channels_last)
+    out = {}
+    for mode in ("native", "dropin"):
+        ref = ref_mode(mode)
+        torch.manual_seed(0)
+        model = ref.create_model("visionhope_tiny", layer_scale_init_value=0.1)
+        for blk in [m for m in model.modules() if type(m).__name__ == "VisionHOPEBlock"]:
+            _stress_(blk.operator.srnl, 6)
+        model = model.cuda().train().to(memory_format=torch.channels_last)
+        for m in model.modules():
+            if isinstance(m, torch.nn.BatchNorm2d):
+                m.eval()
+        xd = x.cuda().requires_grad_(True)
+        torch.manual_seed(5)
+        logits = model(xd)
+        logits.square().mean().backward()
+        out[mode] = {n: p.grad.detach().double().cpu() for n, p in model.named_parameters() if p.grad is not None}
+        out[mode]["input"] = xd.grad.detach().double().cpu()
+        del model
+    nat, ours = out["native"], out["dropin"]
+    assert nat.keys() == ours.keys() and len(nat) > 100
+    worst = max(((rel_err(ours[k], nat[k]), k) for k in nat if nat[k].abs().max() > 0))
+    flat_n = torch.cat([nat[k].flatten() for k in nat])
+    flat_o = torch.cat([ours[k].flatten() for k in nat])
+    total = float((flat_o - flat_n).norm() / flat_n.norm())
+    print(f"\n[visionhope_tiny training] all gradients {total:.2e} normwise; worst tensor {worst[1]} {worst[0]:.2e}")
+    assert total < 3e-3
+    assert worst[0] < 2e-2, worst
