@@ -623,6 +623,7 @@ const char* check_bwd(const vh_srnl_sequence_bwd_args* a) {
 
 extern "C" int64_t vh_srnl_sequence_bwd_workspace_bytes(const vh_srnl_sequence_bwd_args* a) {
     if (!a || a->batch <= 0 || a->dirs <= 0 || a->dirs > 4 || a->heads <= 0 || a->length <= 0) return 0;
+    if (a->length > (1 << 30)) return 0;  // beyond the supported range (the call refuses it too)
     if (a->head_dim != 4 && a->head_dim != 8 && a->head_dim != 16 && a->head_dim != 32) return 0;
     for (int r = 0; r < a->dirs; ++r)
         if (a->chunk[r] <= 0) return 0;
