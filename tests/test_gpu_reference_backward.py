@@ -1,10 +1,11 @@
 """Training parity with the reference itself: the reference's own modules (models/srnl.py,
-models/operator.py, models/layers.py:LayerNorm2d, utils/grn.py:GlobalResponseNorm; unchanged, oracle/refmodel.py)
-run forward and backward twice on the same seeded parameters and inputs, once on the reference's
-own kernels ("native": its CUDA extensions built from its sources, its Triton kernels) and once
-over this repository's drop-in modules ("dropin"), and every gradient is compared.  Bar: 5e-4
-normwise through the SRNL recurrence (two fp32 implementations of a long recurrence), 1e-5 for the
-one-pass operators."""
+models/operator.py, models/block.py, models/layers.py:LayerNorm2d, utils/grn.py:GlobalResponseNorm,
+utils/residual.py, models/factory.py; unchanged, oracle/refmodel.py) run forward and backward
+twice on the same seeded parameters and inputs, once on the reference's own kernels ("native": its
+CUDA extensions built from its sources, its Triton kernels) and once over this repository's
+drop-in modules ("dropin"), and every gradient is compared.  Bar: 5e-4 normwise through the SRNL
+recurrence (two fp32 implementations of a long recurrence), 1e-5 for the one-pass operators; the
+whole-model step has its own bar (its docstring)."""
 import importlib
 
 import numpy as np
