@@ -111,3 +111,26 @@ def test_srnl_sequence_matches_c_oracle(q_normalized, per_chain):
     got = og.srnl_sequence([torch.from_numpy(m).double() for m in mems], torch.from_numpy(x).double(),
                            torch.from_numpy(q).double(), chunks, recurrence_constants_tuple(), q_normalized)
     assert _rel(got.numpy(), exp) < 1e-12
+
+
+def test_residual_matches_reference_block_fallback():
+    """The residual oracle (res + branch gamma mask) against the reference's own CPU code path
+    for the same add: VisionHOPEBlock._residual_add (models/block.py:90-97), which on CPU tensors
+    takes `x + drop_path(gamma * branch)`.  timm is not installed, so the reference's DropPath is
+    the parity harness's stand-in, the identity: the mask is all ones here (the drop-path mask
+    itself is compared on the GPU, where the reference takes its fused path)."""
+    import importlib
+
+    from tests.conftest import reference
+
+    reference("dropin")
+    blk_mod = importlib.import_module("visionhope.models.block")
+    torch.manual_seed(0)
+    blk = blk_mod.VisionHOPEBlock(32, 16, drop_path=0.4, norm_layer="layernorm2d").train()
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(6, 32, 5, 7, generator=g).double()
+    br = torch.randn(6, 32, 5, 7, generator=g).double()
+    gamma = torch.randn(32, 1, 1, generator=g).double()
+    ref = blk._residual_add(x, br, gamma)
+    exp = og.residual(x, br, gamma, torch.ones(6, dtype=torch.float64))
+    assert torch.allclose(ref, exp, rtol=1e-15, atol=1e-15)
