@@ -16,6 +16,10 @@ from .. import _lib
 def residual_add_forward(residual, branch, gamma, mask):
     """fp32 channels-last residual + branch * gamma[c] * mask[b] (``vh_residual_add_fwd``)."""
     _lib.ensure_device(branch)
+    if residual.shape != branch.shape or branch.dim() != 4:
+        raise RuntimeError("visionhope_residual_add expects residual and branch of one [B, C, H, W] shape")
+    residual = residual.contiguous(memory_format=torch.channels_last)  # no copy when already so
+    branch = branch.contiguous(memory_format=torch.channels_last)
     batch, channels, height, width = branch.shape
     out = torch.empty_like(branch, dtype=torch.float32, memory_format=torch.channels_last)
     g = gamma.detach().reshape(-1).contiguous().float()
@@ -32,6 +36,7 @@ def residual_add_backward(dout, branch, gamma, mask):
     """(d branch in branch's dtype, channels-last; d gamma fp32 [C]) (``vh_residual_add_bwd``);
     d residual is dout itself."""
     batch, channels, height, width = branch.shape
+    branch = branch.contiguous(memory_format=torch.channels_last)
     d = dout.contiguous(memory_format=torch.channels_last).float()
     g = gamma.detach().reshape(-1).contiguous().float()
     m = mask.detach().reshape(-1).contiguous().float()
